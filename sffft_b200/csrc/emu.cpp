@@ -1,0 +1,164 @@
+// Host emulator of the fused kernel: runs the same stage templates (stages.h) with a CPU backend.
+//
+// tcgen05.mma is emulated from the raw descriptors: the smem matrix descriptor is decoded (start,
+// LBO, SBO, layout type) and operands are read through the canonical UMMA layouts as CUTLASS
+// documents them (cute/atom/mma_traits_sm100.hpp, make_umma_desc):
+//   K-major, swizzle W (32/64/128 B):  row i -> (i%8)*W + (i/8)*SBO, k -> (k/8)*16 + (k%8)*2
+//   MN-major, 128-B swizzle:           m -> (m%64)*2 + (m/64)*LBO,   k -> (k%8)*128 + (k/8)*SBO
+// with the swizzle applied to the absolute byte address.  This is deliberately a separate
+// transcription from the writers in plan.h, so a mismatch between what an epilogue writes and what a
+// descriptor makes the tensor core read shows up here without a GPU.
+//
+// Exposed through a C entry point for the CPU test-suite; not part of the product path.
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "catalog.h"
+#include "hostmath.h"
+#include "stages.h"
+
+namespace sffft {
+namespace emu {
+
+using hostmath::h2f;
+using hostmath::f2h;
+
+static inline uint32_t bf16_from_float(float f) {
+  uint32_t x; std::memcpy(&x, &f, 4);
+  if ((x & 0x7FFFFFFFu) > 0x7F800000u) return 0x7FC0u;
+  x += 0x7FFFu + ((x >> 16) & 1u);
+  return x >> 16;
+}
+
+struct HostOps {
+  std::vector<uint8_t>* smem;
+  std::vector<uint32_t>* tmem;   // 128 lanes x 512 columns
+  int cur_lane;                  // TMEM lane of the emulated thread
+  bool acc16;
+
+  static uint32_t swz(uint32_t addr, int lt) {
+    if (lt == LT_SW128) return addr ^ (((addr >> 7) & 7u) << 4);
+    if (lt == LT_SW64) return addr ^ (((addr >> 7) & 3u) << 4);
+    if (lt == LT_SW32) return addr ^ (((addr >> 7) & 1u) << 4);
+    return addr;
+  }
+  float rd(uint64_t desc, bool mn, int i, int k) const {
+    const uint32_t start = (uint32_t)(desc & 0x3FFFu) << 4, lbo = (uint32_t)((desc >> 16) & 0x3FFFu) << 4,
+                   sbo = (uint32_t)((desc >> 32) & 0x3FFFu) << 4;
+    const int lt = (int)(desc >> 61);
+    uint32_t a;
+    if (mn) {
+      a = start + (uint32_t)((i % 64) * 2) + (uint32_t)(i / 64) * lbo + (uint32_t)((k % 8) * 128) + (uint32_t)(k / 8) * sbo;
+    } else {
+      const uint32_t W = lt == LT_SW128 ? 128 : lt == LT_SW64 ? 64 : 32;
+      a = start + (uint32_t)(i % 8) * W + (uint32_t)(i / 8) * sbo + (uint32_t)((k / 8) * 16 + (k % 8) * 2);
+    }
+    a = swz(a, lt);
+    uint16_t h; std::memcpy(&h, smem->data() + a, 2);
+    return h2f(h);
+  }
+  void mma(uint32_t d, uint64_t ad, uint64_t bd, uint32_t idesc, uint32_t acc) {
+    const int N = (int)((idesc >> 17) & 63) * 8, M = (int)((idesc >> 24) & 31) * 16;
+    const bool amn = (idesc >> 15) & 1, bmn = (idesc >> 16) & 1, f32 = (idesc >> 4) & 1;
+    const int col = (int)(d & 0xFFFF);
+    for (int i = 0; i < M; i++)
+      for (int n = 0; n < N; n++) {
+        double s = 0;
+        for (int k = 0; k < 16; k++) s += (double)rd(ad, amn, i, k) * (double)rd(bd, bmn, n, k);
+        uint32_t& cell = (*tmem)[(size_t)i * 512 + col + n];
+        if (f32) {
+          float prev; std::memcpy(&prev, &cell, 4);
+          const float v = (float)(s + (acc ? (double)prev : 0.0));
+          std::memcpy(&cell, &v, 4);
+        } else {
+          const float prev = h2f((uint16_t)(cell & 0xFFFF));
+          cell = f2h((float)(s + (acc ? (double)prev : 0.0)));
+        }
+      }
+  }
+  void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+    const int lane = (int)(taddr >> 16) + cur_lane % 32, col = (int)(taddr & 0xFFFF);
+    for (int j = 0; j < 16; j++) r[j] = (*tmem)[(size_t)lane * 512 + col + j];
+  }
+  void tmem_wait() {}
+  void st16(uint32_t off, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    const uint32_t w[4] = {a, b, c, d};
+    std::memcpy(smem->data() + off, w, 16);
+  }
+  void sincospi(float x, float* s, float* c) {
+    *s = (float)std::sin(M_PI * (double)x);
+    *c = (float)std::cos(M_PI * (double)x);
+  }
+  uint32_t pack2(float lo, float hi) { return (uint32_t)f2h(lo) | ((uint32_t)f2h(hi) << 16); }
+  float lo16f(uint32_t w) { return h2f((uint16_t)(w & 0xFFFF)); }
+  float hi16f(uint32_t w) { return h2f((uint16_t)(w >> 16)); }
+  float acc_val(uint32_t w) {
+    if (acc16) return h2f((uint16_t)(w & 0xFFFF));
+    float f; std::memcpy(&f, &w, 4); return f;
+  }
+  void ldK(const float* p, float (&k)[4]) { for (int e = 0; e < 4; e++) k[e] = p[e]; }
+  void load8(const float* p, float* v) { for (int e = 0; e < 8; e++) v[e] = p[e]; }
+  void load8(const uint16_t* p, float* v) {
+    for (int e = 0; e < 8; e++) { uint32_t b = (uint32_t)p[e] << 16; std::memcpy(&v[e], &b, 4); }
+  }
+  void store1(float* p, float v) { *p = v; }
+  void store1(uint16_t* p, float v) { *p = (uint16_t)bf16_from_float(v); }
+};
+
+template <int SID, class P, class TIO, bool ACC16>
+void run_stage_emu(HostOps& ops, const EpiArgs& ea0) {
+  issue_stage<P, ACC16, SID>(ops, 0u, 0u, (uint32_t)P::DATA_BYTES);
+  EpiArgs ea = ea0;
+  ea.tmem = 0;
+  for (int t = 0; t < P::tiles(SID); t++)
+    for (int q = 0; q < 4; q++)
+      for (int lane = 0; lane < 32; lane++) {
+        ops.cur_lane = lane;
+        epilogue_row<P, TIO, ACC16, SID>(ops, ea, t, q, lane);
+      }
+  if constexpr (SID + 1 < 2 * P::S) run_stage_emu<SID + 1, P, TIO, ACC16>(ops, ea0);
+}
+
+template <class P, class TIO, bool ACC16>
+int run_plan(const void* u, const float* Kf, void* y, int B, int H) {
+  const int PB = (B + 1) / 2;
+  const long long pairs = (long long)PB * H;
+  const int grid = (int)((pairs + P::G - 1) / P::G);
+  std::vector<uint8_t> smem(P::DATA_BYTES + P::BMAT_BYTES, 0);
+  std::vector<uint32_t> tmem(128 * 512, 0);
+  hostmath::build_bmat_image<P>(smem.data() + P::DATA_BYTES);
+  HostOps ops{&smem, &tmem, 0, ACC16};
+  for (int cta = 0; cta < grid; cta++) {
+    std::memset(smem.data(), 0xFF, P::DATA_BYTES);   // poison: stale data must never be read
+    for (int tid = 0; tid < P::NT; tid++) load_input<P, TIO>(ops, (const TIO*)u, cta, B, H, tid);
+    EpiArgs ea{0u, Kf, y, B, H, cta};
+    run_stage_emu<0, P, TIO, ACC16>(ops, ea);
+  }
+  return 0;
+}
+
+}  // namespace emu
+}  // namespace sffft
+
+extern "C" {
+// Runs the emulated fused kernel for catalog entry `config` ("64x32/w4" ...).  io: 0 fp32, 1 bf16 (u,y as
+// uint16 bf16 bits).  acc: 0 fp32, 1 fp16.  Returns 0 on success, nonzero for an unknown config.
+int sffft_emu_conv(const char* config, int io, int acc, const void* u, const float* Kf, void* y, int B, int H) {
+  using namespace sffft;
+  int rc = 2;
+#define SF_EMU_CASE(R0, R1, R2, G, W, NAME)                                                           \
+  if (std::string(config) == NAME) {                                                                  \
+    using Pl = Plan<R0, R1, R2, G, W>;                                                                \
+    if (io == 0 && acc == 0) rc = emu::run_plan<Pl, float, false>(u, Kf, y, B, H);                    \
+    else if (io == 0 && acc == 1) rc = emu::run_plan<Pl, float, true>(u, Kf, y, B, H);                \
+    else if (io == 1 && acc == 0) rc = emu::run_plan<Pl, uint16_t, false>(u, Kf, y, B, H);            \
+    else rc = emu::run_plan<Pl, uint16_t, true>(u, Kf, y, B, H);                                      \
+  }
+  SFFFT_CATALOG(SF_EMU_CASE)
+#undef SF_EMU_CASE
+  return rc;
+}
+}

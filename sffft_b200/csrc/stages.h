@@ -1,0 +1,258 @@
+// Stage logic of the fused convolution, written once for the device (tcgen05 PTX, fused_conv.cuh)
+// and for the host emulator (emu.cpp) through an `Ops` backend:
+//   ops.mma(d_tmem, a_desc, b_desc, idesc, accumulate)      tcgen05.mma.cta_group::1.kind::f16
+//   ops.tmem_ld16(taddr, r[16]) / ops.tmem_wait()            tcgen05.ld.32x32b.x16 of this lane
+//   ops.st16(byte_off, w0..w3)                               16-byte shared-memory store
+//   ops.sincospi(x, &s, &c)                                  sin/cos of pi*x
+//   ops.pack2(lo, hi)                                        two floats -> f16x2 (round to nearest)
+//   ops.acc_val(raw)                                         TMEM word -> float (fp32 or fp16 accumulator)
+//   ops.ldK(p)                                               four floats (two complex) of the spectrum
+//
+// Algorithm per pair (reference: sfFFT src/sffft.cu:137-280, restated for tcgen05 and pairing):
+//   forward digits 0..S-1, each: DFT_R along the digit, x 1/sqrt(R), then the four-step twiddle
+//   (src/sffft.cu:106-113) or, after the last digit, the filter spectrum Kf (src/sffft.cu:229-236);
+//   inverse digits S-1..0 with conjugate DFTs and conjugate twiddles; the last inverse digit keeps
+//   only time rows n0 < R0/2, i.e. outputs n < L (src/sffft.cu:180-181).
+#pragma once
+#include "plan.h"
+
+namespace sffft {
+
+// Pair bookkeeping for one CTA: pair gp = cta*G + g covers batch elements 2j, 2j+1 of channel h.
+struct PairInfo {
+  long long off0, off1;   // element offsets of the two sequences in u / y, or -1 when absent
+  int h;                  // channel (spectrum row), -1 when the pair slot is empty
+};
+
+SF_HD PairInfo pair_info(int cta, int g, int G, int B, int H, int L) {
+  const int PB = (B + 1) / 2;
+  const long long gp = (long long)cta * G + g;
+  PairInfo pi;
+  if (gp >= (long long)PB * H) { pi.off0 = pi.off1 = -1; pi.h = -1; return pi; }
+  const int h = (int)(gp / PB), j = (int)(gp % PB);
+  pi.h = h;
+  pi.off0 = ((long long)(2 * j) * H + h) * L;
+  pi.off1 = (2 * j + 1 < B) ? ((long long)(2 * j + 1) * H + h) * L : -1;
+  return pi;
+}
+
+// ---------------------------------------------------------------------------------------------
+// Input: u (two real sequences per pair) -> first-stage A operand, fp16 hi + lo split.
+//   element (row m = g*V0 + v, K-row plane*R0 + n0 [hi] / plane*R0 + R0/2 + n0 [lo]), n = n0*V0 + v.
+// ---------------------------------------------------------------------------------------------
+template <class P, class TIO, class Ops>
+SF_HD void load_input(Ops& ops, const TIO* u, int cta, int B, int H, int tid) {
+  constexpr int V0 = P::N / P::R0, CH = P::L / 8, MB0 = P::MB(0);
+  for (int idx = tid; idx < P::G * 2 * CH; idx += P::NT) {
+    const int g = idx / (2 * CH), rem = idx - g * 2 * CH, plane = rem / CH, c = rem - plane * CH;
+    const PairInfo pi = pair_info(cta, g, P::G, B, H, P::L);
+    const long long off = plane == 0 ? pi.off0 : pi.off1;
+    float v[8];
+    if (off >= 0) ops.load8(u + off + c * 8, v);
+    else {
+      for (int e = 0; e < 8; e++) v[e] = 0.f;
+    }
+    uint32_t hi[4], lo[4];
+    for (int e = 0; e < 4; e++) {
+      hi[e] = ops.pack2(v[2 * e], v[2 * e + 1]);
+      lo[e] = ops.pack2(v[2 * e] - ops.lo16f(hi[e]), v[2 * e + 1] - ops.hi16f(hi[e]));
+    }
+    const int n = c * 8, n0 = n / V0, vv = n - n0 * V0, m = g * V0 + vv;
+    const int k = plane * P::R0 + n0;
+    ops.st16(mn_off(m, k, MB0), hi[0], hi[1], hi[2], hi[3]);
+    ops.st16(mn_off(m, k + P::R0 / 2, MB0), lo[0], lo[1], lo[2], lo[3]);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// MMA issue for stage SID (one thread)
+// ---------------------------------------------------------------------------------------------
+template <class P, bool ACC16, int SID, class Ops>
+SF_HD void issue_stage(Ops& ops, uint32_t tmem, uint32_t data_s, uint32_t bmat_s) {
+  constexpr int R = P::rad(SID), T = P::tiles(SID), NSL = R / 16;
+  constexpr bool KM = P::kmajor(SID), INV = P::inv(SID);
+  constexpr bool B0 = (SID == 0 && P::R0 == 16);
+  constexpr int HS = P::R0 >= 32 ? P::R0 / 32 : 1;           // B K-slices per first-stage half
+  constexpr uint32_t idesc = make_idesc(128, 2 * R, !ACC16, !KM, false);
+  for (int t = 0; t < T; t++) {
+    for (int p = 0; p < 2; p++) {
+      for (int j = 0; j < NSL; j++) {
+        const int ks = p * NSL + j;
+        uint64_t ad;
+        if constexpr (KM) {
+          constexpr int RB = kmaj_data_pitch(R);
+          const uint32_t colblk = R == 64 ? (uint32_t)((ks >> 2) * P::rows(SID) * 128) : 0u;
+          const uint32_t start = data_s + colblk + (uint32_t)(t * 128 * RB) + (uint32_t)(32 * (R == 64 ? (ks & 3) : ks));
+          ad = make_sdesc(start, 16, 8 * RB, lt_for_pitch(RB));
+        } else {
+          constexpr int MB = P::MB(SID);
+          ad = make_sdesc(data_s + (uint32_t)((2 * ks * MB + 2 * t) << 10), 1024, MB * 1024, LT_SW128);
+        }
+        for (int sp = 0; sp < P::NSET; sp++) {
+          uint64_t bd;
+          if constexpr (B0) {
+            // duplicated-K blocks [-Fi', Fr', Fi']: forward real plane -> window 1, imag plane -> window 0
+            bd = make_sdesc(bmat_s + (uint32_t)(P::b0_off(sp) + (p == 0 ? 1 : 0) * 16 * 32), 16, 8 * 32, LT_SW32);
+          } else {
+            const int w = INV ? (p == 0 ? 1 : 0) : (p == 0 ? 3 : 2);
+            const int bj = SID == 0 ? (j % HS) : j;
+            bd = make_sdesc(bmat_s + (uint32_t)(P::slot_off(R, sp) + w * R * 2 * R + 32 * bj), 16, 16 * R,
+                            lt_for_pitch(2 * R));
+          }
+          ops.mma(tmem + (uint32_t)(t * 2 * R), ad, bd, idesc, (uint32_t)((p | j | sp) != 0));
+        }
+      }
+    }
+  }
+}
+
+// Twiddle exponent reduced to (-N/2, N/2] and turned into the argument of sincospi: angle = -2*pi*e/N.
+template <int N>
+SF_HD float tw_arg(int e) {
+  e &= (N - 1);
+  if (e > N / 2) e -= N;
+  return -2.0f * (float)e / (float)N;
+}
+
+// ---------------------------------------------------------------------------------------------
+// Epilogue for stage SID: one thread per TMEM lane (row r = t*128 + q*32 + lane of tile t).
+// ---------------------------------------------------------------------------------------------
+struct EpiArgs {
+  uint32_t tmem;
+  const float* Kf;      // [H][N] complex fp32, digit order
+  void* y;              // output base (TIO*)
+  int B, H, cta;
+};
+
+template <class P, class TIO, bool ACC16, int SID, class Ops>
+SF_HD void epilogue_row(Ops& ops, const EpiArgs& ea, int t, int q, int lane) {
+  constexpr int S = P::S, R = P::rad(SID), N = P::N, RPP = N / R;   // rows per pair
+  constexpr bool OUT = (SID == 2 * S - 1), SPEC = (SID == S - 1);
+  constexpr int NOUT = OUT ? (P::R0 / 2 < 16 ? 16 : P::R0 / 2) : R;  // columns to read
+  constexpr float SC = (R == 16) ? 0.25f : (R == 64 ? 0.125f : 0.17677669529663687f);
+  const int r = t * 128 + q * 32 + lane, g = r / RPP, rr = r - g * RPP;
+  const uint32_t taddr = ea.tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(t * 2 * R);
+
+  // thread-specific twiddle exponent e(c) = ta*c + tb, next-stage write target (m0, kre)
+  int ta = 0, tb = 0, m0 = 0, kre = 0;
+  long long yo0 = -1, yo1 = -1; int vv = 0;
+  const float* Kp = nullptr;
+  if constexpr (SID == 0) {
+    if constexpr (S == 2) { ta = rr; m0 = g * P::R0; kre = rr; }
+    else { const int n1 = rr / P::R2, n2 = rr - n1 * P::R2; ta = rr; m0 = g * P::R0 * P::R2 + n2 * P::R0; kre = n1; }
+  } else if constexpr (S == 3 && SID == 1) {
+    const int n2 = rr / P::R0, k0 = rr - n2 * P::R0;
+    ta = P::R0 * n2; m0 = g * P::R0 * P::R1 + k0 * P::R1; kre = n2;
+  } else if constexpr (SPEC) {
+    const PairInfo pi = pair_info(ea.cta, g, P::G, ea.B, ea.H, P::L);
+    Kp = ea.Kf + 2 * ((long long)(pi.h < 0 ? 0 : pi.h) * N + (long long)rr * R);
+  } else if constexpr (SID == S) {
+    if constexpr (S == 2) { ta = -rr; m0 = g * P::R1; kre = rr; }
+    else { const int k0 = rr / P::R1, k1 = rr - k0 * P::R1; ta = -P::R0 * k1; m0 = g * P::R0 * P::R2 + k0 * P::R2; kre = k1; }
+  } else if constexpr (S == 3 && SID == S + 1) {
+    const int k0 = rr / P::R2, n2 = rr - k0 * P::R2;
+    ta = -k0 * P::R2; tb = -k0 * n2; m0 = g * P::R1 * P::R2 + n2 * P::R1; kre = k0;
+  } else {  // OUT
+    if constexpr (S == 2) vv = rr;
+    else { const int n2 = rr / P::R1, n1 = rr - n2 * P::R1; vv = n1 * P::R2 + n2; }
+    const PairInfo pi = pair_info(ea.cta, g, P::G, ea.B, ea.H, P::L);
+    yo0 = pi.off0; yo1 = pi.off1;
+  }
+
+  float t_re = SC, t_im = 0.f, w_re = 1.f, w_im = 0.f;
+  constexpr bool TW = !SPEC && !OUT;
+  if constexpr (TW) {
+    float s, c;
+    ops.sincospi(tw_arg<N>(ta), &s, &c); w_re = c; w_im = s;
+    if (tb != 0) { ops.sincospi(tw_arg<N>(tb), &s, &c); t_re = SC * c; t_im = SC * s; }
+  }
+
+  for (int c0 = 0; c0 < NOUT; c0 += 16) {
+    uint32_t raw_re[16], raw_im[16];
+    ops.tmem_ld16(taddr + (uint32_t)c0, raw_re);
+    ops.tmem_ld16(taddr + (uint32_t)(R + c0), raw_im);
+    ops.tmem_wait();
+    float o_re[16], o_im[16];
+    if constexpr (TW) {
+      for (int j = 0; j < 16; j++) {
+        const float a = ops.acc_val(raw_re[j]), b = ops.acc_val(raw_im[j]);
+        o_re[j] = a * t_re - b * t_im;
+        o_im[j] = a * t_im + b * t_re;
+        const float nr = t_re * w_re - t_im * w_im;
+        t_im = t_re * w_im + t_im * w_re; t_re = nr;
+      }
+    } else if constexpr (SPEC) {
+      for (int j = 0; j < 16; j += 2) {
+        float kk[4];
+        ops.ldK(Kp + 2 * (c0 + j), kk);
+        for (int e = 0; e < 2; e++) {
+          const float a = ops.acc_val(raw_re[j + e]) * SC, b = ops.acc_val(raw_im[j + e]) * SC;
+          o_re[j + e] = a * kk[2 * e] - b * kk[2 * e + 1];
+          o_im[j + e] = a * kk[2 * e + 1] + b * kk[2 * e];
+        }
+      }
+    } else {
+      for (int j = 0; j < 16; j++) { o_re[j] = ops.acc_val(raw_re[j]) * SC; o_im[j] = ops.acc_val(raw_im[j]) * SC; }
+    }
+
+    if constexpr (OUT) {
+      TIO* y = (TIO*)ea.y;
+      constexpr int V0 = N / P::R0;
+      for (int j = 0; j < 16; j++) {
+        const int n0 = c0 + j;
+        if (n0 < P::R0 / 2) {
+          if (yo0 >= 0) ops.store1(y + yo0 + (long long)n0 * V0 + vv, o_re[j]);
+          if (yo1 >= 0) ops.store1(y + yo1 + (long long)n0 * V0 + vv, o_im[j]);
+        }
+      }
+    } else {
+      uint32_t pr[8], pim[8];
+      for (int e = 0; e < 8; e++) { pr[e] = ops.pack2(o_re[2 * e], o_re[2 * e + 1]); pim[e] = ops.pack2(o_im[2 * e], o_im[2 * e + 1]); }
+      if constexpr (SPEC) {
+        constexpr int RWS = P::rows(SID + 1);
+        ops.st16(kmaj_data_off(r, c0, R, RWS), pr[0], pr[1], pr[2], pr[3]);
+        ops.st16(kmaj_data_off(r, c0 + 8, R, RWS), pr[4], pr[5], pr[6], pr[7]);
+        ops.st16(kmaj_data_off(r, R + c0, R, RWS), pim[0], pim[1], pim[2], pim[3]);
+        ops.st16(kmaj_data_off(r, R + c0 + 8, R, RWS), pim[4], pim[5], pim[6], pim[7]);
+      } else {
+        constexpr int MBn = P::MB(SID + 1), Rn = P::rad(SID + 1);
+        ops.st16(mn_off(m0 + c0, kre, MBn), pr[0], pr[1], pr[2], pr[3]);
+        ops.st16(mn_off(m0 + c0 + 8, kre, MBn), pr[4], pr[5], pr[6], pr[7]);
+        ops.st16(mn_off(m0 + c0, Rn + kre, MBn), pim[0], pim[1], pim[2], pim[3]);
+        ops.st16(mn_off(m0 + c0 + 8, Rn + kre, MBn), pim[4], pim[5], pim[6], pim[7]);
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// DFT-matrix region image (identical for the cached table and the in-kernel "legacy" build)
+// ---------------------------------------------------------------------------------------------
+// Calls emit(byte_off, radix, phase_index q, which, set) for every fp16 entry of the region;
+// `which`: 0 -> cos(2*pi*q/R), 1 -> -sin(2*pi*q/R), 2 -> +sin(2*pi*q/R); `set` 0 = hi, 1 = lo.
+template <class P, class Emit>
+SF_HD void for_each_bmat_entry(Emit& emit, int tid, int nthreads) {
+  for (int set = 0; set < P::NSET; set++) {
+    for (int rq = 16; rq <= 64; rq <<= 1) {
+      if (!P::uses(rq)) continue;
+      const int base = P::slot_off(rq, set), total = 5 * rq * rq;
+      for (int i = tid; i < total; i += nthreads) {
+        const int row = i / rq, k = i - row * rq, b = row / rq, n = row - b * rq;
+        int q, which;
+        block_entry(b, n, k, rq, &q, &which);
+        emit(base + (int)km_off(row, k, 2 * rq), rq, q, which, set);
+      }
+    }
+    if (P::R0 == 16) {
+      // first-stage blocks [-Fi', Fr', Fi'] with K duplicated: column k uses input index k % 8
+      const int base = P::b0_off(set);
+      for (int i = tid; i < 3 * 16 * 16; i += nthreads) {
+        const int row = i / 16, k = i - row * 16, b = row / 16, n = row - b * 16;
+        const int q = (n * (k & 7)) % 16, which = b == 1 ? 0 : (b == 0 ? 2 : 1);
+        emit(base + (int)km_off(row, k, 32), 16, q, which, set);
+      }
+    }
+  }
+}
+
+}  // namespace sffft
