@@ -1,0 +1,120 @@
+/* sffft — B200 (sm_100a) fused causal long convolution, C ABI.
+ *
+ *   y[b,h,n] = sum_{m<=n} u[b,h,m] * k[h,n-m],   0 <= n < L
+ *
+ * Drop-in for the operator surface of sfFFT (github.com/solidsf-inc/sfFFT, src/sffft.cu and
+ * src/selection.h).  All device buffers are caller-owned; calls are asynchronous on the given CUDA
+ * stream (cudaStream_t passed as void*, NULL = default stream); every call returns an int status
+ * (SFFFT_OK = 0) and never exits the process.  Plans are immutable after creation and may be shared
+ * by host threads.  There is no CPU fallback: without a B200-class device, plan creation fails.
+ *
+ * Layouts (identical to the reference):
+ *   u, y : [B][H][L] contiguous, fp32 or bf16 (plan io), 16-byte aligned
+ *   k    : [H][L] contiguous real filter, fp32 or bf16 (k_dtype)
+ *   Kf   : [H][N] complex fp32 (float pairs), N = 2L, unnormalised DFT of the zero-padded filter in the
+ *          plan's digit order: position p = k0*R1*R2 + k1*R2 + k2 holds frequency k0 + R0*k1 + R0*R1*k2
+ *          (the layout permuteK writes, src/sffft.cu:283-288)
+ */
+#ifndef SFFFT_H_
+#define SFFFT_H_
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SFFFT_OK 0
+#define SFFFT_ERR_INVALID_ARGUMENT 1
+#define SFFFT_ERR_UNSUPPORTED 2
+#define SFFFT_ERR_CUDA 3
+#define SFFFT_ERR_DEVICE 4
+#define SFFFT_ERR_TIMEOUT 5
+#define SFFFT_ERR_NO_MATCH 6
+#define SFFFT_ERR_ALLOC 7
+
+#define SFFFT_IO_FP32 0
+#define SFFFT_IO_BF16 1
+#define SFFFT_ACC_FP32 0
+#define SFFFT_ACC_FP16 1
+#define SFFFT_KERNEL_LEGACY 0 /* DFT matrices computed inside every CTA (reference --kernel legacy) */
+#define SFFFT_KERNEL_CACHED 1 /* DFT matrices copied from a precomputed table (reference --kernel cached) */
+
+typedef struct sffft_plan* sffft_plan_t;
+
+typedef struct {
+  int L, N, stages, R0, R1, R2;
+  int pairs_per_cta;   /* G: pairs of batch elements (same channel) per CTA */
+  int warps, threads, smem_bytes, tmem_cols, occupancy;
+  int io, acc, kernel_mode, device;
+  char config[96];     /* catalog name, e.g. "64x32/w4" */
+} sffft_plan_info_t;
+
+/* Creates a plan for length L (128..16384, power of two).  config: catalog name ("64x32/w4"), or NULL /
+ * "" for the built-in B200 default for L.  Replaces the compile-time choice of fftconv<Plan<R0,R1,R2>,W,
+ * TIO,TAcc,CACHED> plus its cudaFuncSetAttribute / occupancy setup (src/sffft.cu:243-245, 385-388). */
+int sffft_plan_create(sffft_plan_t* plan, int L, int io, int acc, const char* config, int kernel_mode, int device);
+int sffft_plan_destroy(sffft_plan_t plan);
+int sffft_plan_info(sffft_plan_t plan, sffft_plan_info_t* info);
+
+/* Filter spectrum in the plan's digit order, once per channel (untimed prep).  k_dtype: SFFFT_IO_FP32 or
+ * SFFFT_IO_BF16.  Replaces host zero-padding + cufftExecC2C + permuteK (src/sffft.cu:342-344, 365,
+ * 283-288, 384). */
+int sffft_filter_spectrum(sffft_plan_t plan, const void* k, int k_dtype, int H, void* Kf, void* stream);
+
+/* The fused convolution: one kernel launch per call.  Replaces the launch
+ * fftconv<P,W,TIO,TAcc,CACHED><<<B*H, 32*W, smem>>>(u, Kf, tw, dft, y, B, H) (src/sffft.cu:243-280,
+ * 389-390); the unused twiddle table and the DFT table are owned by the plan. */
+int sffft_conv(sffft_plan_t plan, const void* u, const void* Kf, void* y, int B, int H, void* stream);
+
+/* Waits for the plan's device and returns (and clears) the device-side status word: SFFFT_OK, or
+ * SFFFT_ERR_TIMEOUT when a kernel barrier wait gave up.  No reference counterpart (the reference has no
+ * device-side error reporting; its CUDA errors surface through cudaGetLastError, src/sffft.cu:324). */
+int sffft_plan_check(sffft_plan_t plan);
+
+/* Plan catalog (the candidates of the reference's RUN rows, src/sffft.cu:506-513, plus L = 16384). */
+int sffft_catalog_count(void);
+int sffft_catalog_entry(int index, int* L, char* name, int name_cap);
+int sffft_default_config(int L, char* name, int name_cap);
+
+/* Empirical selector with the semantics of select_candidate / relative_l2 (src/selection.h:13-29):
+ * returns the index of the fastest candidate with finite ms > 0 and finite 0 <= rel_err <= max_error
+ * whose io matches (or io == "any"); ties go to the lower error; -1 when nothing qualifies or the budget
+ * or io is invalid. */
+typedef struct {
+  const char* method;
+  const char* io;
+  const char* config;
+  double ms, rel_err;
+} sffft_candidate_t;
+int sffft_select_candidate(const sffft_candidate_t* candidates, int count, double max_error, const char* io);
+double sffft_relative_l2(double squared_error, double squared_reference);
+
+/* Channel sharding across devices: shard g of G owns channels [h0, h1) (contiguous, sizes differ by at
+ * most one).  No reference counterpart (the reference is single-GPU, src/sffft.cu:490). */
+int sffft_shard_range(int H, int shards, int shard, int* h0, int* h1);
+
+const char* sffft_status_string(int status);
+int sffft_last_cuda_error(void);
+
+/* cuFFT baseline pipeline on the same device (src/sffft.cu:289-305, 365-371): spectrum from the
+ * fp32 filter k_dev [H][L]; run(full=1) = pad -> R2C -> multiply -> C2R -> slice, run(full=0) = core
+ * only (reuses the padded input of the previous full run). */
+typedef struct sffft_baseline* sffft_baseline_t;
+int sffft_baseline_create(sffft_baseline_t* bl, int L, int B, int H, const float* k_dev, int device);
+int sffft_baseline_run(sffft_baseline_t bl, const float* u, float* y, int full, void* stream);
+int sffft_baseline_destroy(sffft_baseline_t bl);
+
+/* Debug: one tcgen05.mma through the fused kernel's layout writers and descriptors (no reference
+ * counterpart).  a_kind: 0 = MN-major 128-B swizzle, 32/64/128 = K-major row pitch; A: 128x16 halves,
+ * B: n x 16 halves (B[n][k]), D: 128 x n raw TMEM words. */
+int sffft_debug_umma_probe(int a_kind, int a_slice, int b_pitch, int b_slice, int n, int acc16,
+                           const unsigned short* A, const unsigned short* B, unsigned int* D);
+
+/* Debug: a kernel waits on a barrier that nothing arrives at, using the same bounded wait as the fused
+ * kernel; returns SFFFT_ERR_TIMEOUT after about limit_us microseconds (1..1e6) with the context intact.
+ * No reference counterpart (the reference has no device-side timeouts). */
+int sffft_debug_wait_timeout(int limit_us);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SFFFT_H_ */

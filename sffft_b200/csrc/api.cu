@@ -1,0 +1,309 @@
+// C ABI of the library (declared in include/sffft.h).
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <limits>
+#include <string>
+#include <vector>
+
+#include "../../include/sffft.h"
+#include "fused_conv.cuh"
+#include "registry.h"
+
+namespace sffft {
+cudaError_t launch_spectrum(float2* Kf, const void* k, bool k_bf16, int H, const int* R, int S, cudaStream_t stream);
+struct Baseline;
+int baseline_create(Baseline** out, int L, int B, int H, const float* k_dev, int device);
+int baseline_run(Baseline* b, const float* u, float* y, int full, cudaStream_t st);
+void baseline_destroy(Baseline* b);
+int umma_probe(int a_kind, int a_slice, int b_pitch, int b_slice, int n, int acc16, const uint16_t* A_host,
+               const uint16_t* B_host, uint32_t* D_host);
+int wait_timeout_probe(int limit_us);
+}  // namespace sffft
+
+using namespace sffft;
+
+struct sffft_plan {
+  const ConvEntry* e;
+  int io, acc, kernel_mode, device, occupancy, smem_launch;
+  uint4* btab;   // cached DFT-matrix image (device), null in legacy mode
+  int* status;   // device status word
+};
+struct sffft_baseline {
+  Baseline* b;
+};
+
+static thread_local int g_last_cuda = 0;
+static int cuda_fail(cudaError_t e) {
+  g_last_cuda = (int)e;
+  return SFFFT_ERR_CUDA;
+}
+
+static const std::vector<const ConvEntry*>& catalog() {
+  static std::vector<const ConvEntry*> all = [] {
+    std::vector<const ConvEntry*> v;
+    const ConvEntry* p;
+    int n = entries_small(&p);
+    for (int i = 0; i < n; i++) v.push_back(p + i);
+    n = entries_mid(&p);
+    for (int i = 0; i < n; i++) v.push_back(p + i);
+    n = entries_large(&p);
+    for (int i = 0; i < n; i++) v.push_back(p + i);
+    return v;
+  }();
+  return all;
+}
+
+// Built-in B200 default per length (the static choice of the plan selector; the CLI's empirical
+// selector can override it from measurements).
+static const char* default_for(int L) {
+  switch (L) {
+    case 128: return "16x16/w4";
+    case 256: return "32x16/w4";
+    case 512: return "32x32/w4";
+    case 1024: return "64x32/w4";
+    case 2048: return "64x64/w4";
+    case 4096: return "32x16x16/w4";
+    case 8192: return "32x32x16/w4";
+    case 16384: return "32x32x32/w4";
+    default: return nullptr;
+  }
+}
+
+static int copy_name(const char* s, char* out, int cap) {
+  if (!out || cap <= 0) return SFFFT_ERR_INVALID_ARGUMENT;
+  if ((int)std::strlen(s) >= cap) return SFFFT_ERR_INVALID_ARGUMENT;
+  std::strcpy(out, s);
+  return SFFFT_OK;
+}
+
+extern "C" {
+
+const char* sffft_status_string(int s) {
+  switch (s) {
+    case SFFFT_OK: return "ok";
+    case SFFFT_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case SFFFT_ERR_UNSUPPORTED: return "unsupported length, plan or data type";
+    case SFFFT_ERR_CUDA: return "CUDA runtime error";
+    case SFFFT_ERR_DEVICE: return "device is not an sm_100 GPU with enough shared memory for the plan";
+    case SFFFT_ERR_TIMEOUT: return "device barrier wait timed out";
+    case SFFFT_ERR_NO_MATCH: return "no candidate meets the error budget";
+    case SFFFT_ERR_ALLOC: return "device allocation failed";
+    default: return "unknown status";
+  }
+}
+
+int sffft_last_cuda_error(void) { return g_last_cuda; }
+
+int sffft_catalog_count(void) { return (int)catalog().size(); }
+
+int sffft_catalog_entry(int index, int* L, char* name, int cap) {
+  if (index < 0 || index >= (int)catalog().size()) return SFFFT_ERR_INVALID_ARGUMENT;
+  if (L) *L = catalog()[index]->L;
+  return name ? copy_name(catalog()[index]->name, name, cap) : SFFFT_OK;
+}
+
+int sffft_default_config(int L, char* name, int cap) {
+  const char* d = default_for(L);
+  if (!d) return SFFFT_ERR_UNSUPPORTED;
+  return copy_name(d, name, cap);
+}
+
+int sffft_plan_create(sffft_plan_t* out, int L, int io, int acc, const char* config, int kernel_mode, int device) {
+  if (!out) return SFFFT_ERR_INVALID_ARGUMENT;
+  *out = nullptr;
+  if ((io != SFFFT_IO_FP32 && io != SFFFT_IO_BF16) || (acc != SFFFT_ACC_FP32 && acc != SFFFT_ACC_FP16) ||
+      (kernel_mode != SFFFT_KERNEL_LEGACY && kernel_mode != SFFFT_KERNEL_CACHED) || device < 0)
+    return SFFFT_ERR_INVALID_ARGUMENT;
+  const char* want = (config && *config) ? config : default_for(L);
+  if (!want) return SFFFT_ERR_UNSUPPORTED;
+  const ConvEntry* e = nullptr;
+  for (const ConvEntry* c : catalog())
+    if (std::strcmp(c->name, want) == 0) e = c;
+  if (!e || e->L != L) return SFFFT_ERR_UNSUPPORTED;
+
+  int ndev = 0;
+  cudaError_t ce = cudaGetDeviceCount(&ndev);
+  if (ce != cudaSuccess) return cuda_fail(ce);
+  if (device >= ndev) return SFFFT_ERR_INVALID_ARGUMENT;
+  if ((ce = cudaSetDevice(device)) != cudaSuccess) return cuda_fail(ce);
+  cudaDeviceProp prop;
+  if ((ce = cudaGetDeviceProperties(&prop, device)) != cudaSuccess) return cuda_fail(ce);
+  if (prop.major != 10 || prop.minor != 0 || (int)prop.sharedMemPerBlockOptin < e->smem_bytes) return SFFFT_ERR_DEVICE;
+
+  const void* fn = e->func[io][acc];
+  if ((ce = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, e->smem_bytes)) != cudaSuccess)
+    return cuda_fail(ce);
+  int occ = 0;
+  if ((ce = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, e->threads, e->smem_bytes)) != cudaSuccess)
+    return cuda_fail(ce);
+  if (occ < 1) return SFFFT_ERR_DEVICE;
+  // Co-resident CTAs must fit the 512 TMEM columns of an SM; otherwise a CTA's tcgen05.alloc would stall
+  // until another CTA frees its columns.  Enlarge the dynamic shared memory request to cap residency.
+  int smem_launch = e->smem_bytes;
+  const int max_res = 512 / e->tmem_cols;
+  if (occ > max_res) {
+    const int per_sm = (int)prop.sharedMemPerMultiprocessor;
+    smem_launch = per_sm / max_res - 1024;
+    if (smem_launch > (int)prop.sharedMemPerBlockOptin) smem_launch = (int)prop.sharedMemPerBlockOptin;
+    if (smem_launch < e->smem_bytes) smem_launch = e->smem_bytes;
+    if ((ce = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_launch)) != cudaSuccess)
+      return cuda_fail(ce);
+    if ((ce = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, e->threads, smem_launch)) != cudaSuccess)
+      return cuda_fail(ce);
+  }
+
+  sffft_plan* p = new sffft_plan();
+  p->e = e; p->io = io; p->acc = acc; p->kernel_mode = kernel_mode; p->device = device;
+  p->occupancy = occ; p->smem_launch = smem_launch; p->btab = nullptr; p->status = nullptr;
+  if ((ce = cudaMalloc(&p->status, sizeof(int))) != cudaSuccess || (ce = cudaMemset(p->status, 0, sizeof(int))) != cudaSuccess) {
+    cudaFree(p->status);
+    delete p;
+    return cuda_fail(ce);
+  }
+  if (kernel_mode == SFFFT_KERNEL_CACHED) {
+    std::vector<uint8_t> img(e->bmat_bytes, 0);
+    e->build_bmat(img.data());
+    if ((ce = cudaMalloc(&p->btab, e->bmat_bytes)) != cudaSuccess ||
+        (ce = cudaMemcpy(p->btab, img.data(), e->bmat_bytes, cudaMemcpyHostToDevice)) != cudaSuccess) {
+      cudaFree(p->btab); cudaFree(p->status);
+      delete p;
+      return cuda_fail(ce);
+    }
+  }
+  *out = p;
+  return SFFFT_OK;
+}
+
+int sffft_plan_destroy(sffft_plan_t p) {
+  if (!p) return SFFFT_ERR_INVALID_ARGUMENT;
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaSetDevice(p->device);
+  cudaFree(p->btab);
+  cudaFree(p->status);
+  cudaSetDevice(prev);
+  delete p;
+  return SFFFT_OK;
+}
+
+int sffft_plan_info(sffft_plan_t p, sffft_plan_info_t* info) {
+  if (!p || !info) return SFFFT_ERR_INVALID_ARGUMENT;
+  const ConvEntry* e = p->e;
+  std::memset(info, 0, sizeof(*info));
+  info->L = e->L; info->N = e->N; info->stages = e->R2 > 1 ? 3 : 2;
+  info->R0 = e->R0; info->R1 = e->R1; info->R2 = e->R2; info->pairs_per_cta = e->G;
+  info->warps = e->W; info->threads = e->threads; info->smem_bytes = p->smem_launch; info->tmem_cols = e->tmem_cols;
+  info->occupancy = p->occupancy; info->io = p->io; info->acc = p->acc; info->kernel_mode = p->kernel_mode;
+  info->device = p->device;
+  std::strncpy(info->config, e->name, sizeof(info->config) - 1);
+  return SFFFT_OK;
+}
+
+static int use_device(int device) {
+  int cur = -1;
+  cudaError_t ce = cudaGetDevice(&cur);
+  if (ce != cudaSuccess) return cuda_fail(ce);
+  if (cur != device && (ce = cudaSetDevice(device)) != cudaSuccess) return cuda_fail(ce);
+  return SFFFT_OK;
+}
+
+int sffft_filter_spectrum(sffft_plan_t p, const void* k, int k_dtype, int H, void* Kf, void* stream) {
+  if (!p || !k || !Kf || H < 1 || (k_dtype != SFFFT_IO_FP32 && k_dtype != SFFFT_IO_BF16)) return SFFFT_ERR_INVALID_ARGUMENT;
+  if (((uintptr_t)Kf & 15) != 0) return SFFFT_ERR_INVALID_ARGUMENT;
+  int rc = use_device(p->device);
+  if (rc) return rc;
+  const int R[3] = {p->e->R0, p->e->R1, p->e->R2};
+  const cudaError_t ce = launch_spectrum((float2*)Kf, k, k_dtype == SFFFT_IO_BF16, H, R, p->e->R2 > 1 ? 3 : 2,
+                                         (cudaStream_t)stream);
+  return ce == cudaSuccess ? SFFFT_OK : cuda_fail(ce);
+}
+
+int sffft_conv(sffft_plan_t p, const void* u, const void* Kf, void* y, int B, int H, void* stream) {
+  if (!p || !u || !Kf || !y || B < 1 || H < 1) return SFFFT_ERR_INVALID_ARGUMENT;
+  if ((((uintptr_t)u | (uintptr_t)y | (uintptr_t)Kf) & 15) != 0) return SFFFT_ERR_INVALID_ARGUMENT;
+  const ConvEntry* e = p->e;
+  const long long pairs = (long long)((B + 1) / 2) * H;
+  const long long grid = (pairs + e->G - 1) / e->G;
+  if ((long long)B * H > std::numeric_limits<int>::max() || grid > std::numeric_limits<int>::max())
+    return SFFFT_ERR_INVALID_ARGUMENT;
+  int rc = use_device(p->device);
+  if (rc) return rc;
+  ConvParams prm;
+  prm.u = u; prm.Kf = (const float*)Kf; prm.btab = p->btab; prm.y = y; prm.status = p->status; prm.B = B; prm.H = H;
+  const cudaError_t ce = e->launch[p->io][p->acc](prm, (int)grid, p->smem_launch, (cudaStream_t)stream);
+  return ce == cudaSuccess ? SFFFT_OK : cuda_fail(ce);
+}
+
+int sffft_plan_check(sffft_plan_t p) {
+  if (!p) return SFFFT_ERR_INVALID_ARGUMENT;
+  int rc = use_device(p->device);
+  if (rc) return rc;
+  cudaError_t ce = cudaDeviceSynchronize();
+  if (ce != cudaSuccess) return cuda_fail(ce);
+  int st = 0;
+  if ((ce = cudaMemcpy(&st, p->status, sizeof(int), cudaMemcpyDeviceToHost)) != cudaSuccess) return cuda_fail(ce);
+  if (st && (ce = cudaMemset(p->status, 0, sizeof(int))) != cudaSuccess) return cuda_fail(ce);
+  return st;
+}
+
+double sffft_relative_l2(double se, double sr) {
+  if (sr > 0) return std::sqrt(se / sr);
+  return se == 0 ? 0 : std::numeric_limits<double>::infinity();
+}
+
+int sffft_select_candidate(const sffft_candidate_t* c, int n, double max_error, const char* io) {
+  if (!io || !std::isfinite(max_error) || max_error <= 0) return -1;
+  if (std::strcmp(io, "fp32") && std::strcmp(io, "bf16") && std::strcmp(io, "any")) return -1;
+  if (n > 0 && !c) return -1;
+  int best = -1;
+  for (int i = 0; i < n; i++) {
+    if (std::strcmp(io, "any") && (!c[i].io || std::strcmp(io, c[i].io))) continue;
+    if (!std::isfinite(c[i].ms) || c[i].ms <= 0 || !std::isfinite(c[i].rel_err) || c[i].rel_err < 0 ||
+        c[i].rel_err > max_error)
+      continue;
+    if (best < 0 || c[i].ms < c[best].ms || (c[i].ms == c[best].ms && c[i].rel_err < c[best].rel_err)) best = i;
+  }
+  return best;
+}
+
+int sffft_shard_range(int H, int shards, int shard, int* h0, int* h1) {
+  if (H < 1 || shards < 1 || shard < 0 || shard >= shards || !h0 || !h1) return SFFFT_ERR_INVALID_ARGUMENT;
+  const int base = H / shards, extra = H % shards;
+  *h0 = shard * base + (shard < extra ? shard : extra);
+  *h1 = *h0 + base + (shard < extra ? 1 : 0);
+  return SFFFT_OK;
+}
+
+int sffft_baseline_create(sffft_baseline_t* out, int L, int B, int H, const float* k_dev, int device) {
+  if (!out) return SFFFT_ERR_INVALID_ARGUMENT;
+  Baseline* b = nullptr;
+  const int rc = baseline_create(&b, L, B, H, k_dev, device);
+  if (rc) return rc;
+  *out = new sffft_baseline{b};
+  return SFFFT_OK;
+}
+
+int sffft_baseline_run(sffft_baseline_t bl, const float* u, float* y, int full, void* stream) {
+  if (!bl || !u || (full && !y)) return SFFFT_ERR_INVALID_ARGUMENT;
+  return baseline_run(bl->b, u, y, full, (cudaStream_t)stream);
+}
+
+int sffft_baseline_destroy(sffft_baseline_t bl) {
+  if (!bl) return SFFFT_ERR_INVALID_ARGUMENT;
+  baseline_destroy(bl->b);
+  delete bl;
+  return SFFFT_OK;
+}
+
+int sffft_debug_umma_probe(int a_kind, int a_slice, int b_pitch, int b_slice, int n, int acc16, const unsigned short* A,
+                           const unsigned short* B, unsigned int* D) {
+  if (!A || !B || !D) return SFFFT_ERR_INVALID_ARGUMENT;
+  return umma_probe(a_kind, a_slice, b_pitch, b_slice, n, acc16, A, B, D);
+}
+
+int sffft_debug_wait_timeout(int limit_us) { return wait_timeout_probe(limit_us); }
+
+}  // extern "C"

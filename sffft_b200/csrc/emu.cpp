@@ -13,6 +13,7 @@
 #include <cmath>
 #include <cstdint>
 #include <cstring>
+#include <stdexcept>
 #include <string>
 #include <vector>
 
@@ -38,6 +39,8 @@ struct HostOps {
   std::vector<uint32_t>* tmem;   // 128 lanes x 512 columns
   int cur_lane;                  // TMEM lane of the emulated thread
   bool acc16;
+  int tmem_cols;                 // columns the kernel allocates
+  size_t data_bytes;             // size of the data buffer (epilogue stores must stay inside)
 
   static uint32_t swz(uint32_t addr, int lt) {
     if (lt == LT_SW128) return addr ^ (((addr >> 7) & 7u) << 4);
@@ -57,6 +60,7 @@ struct HostOps {
       a = start + (uint32_t)(i % 8) * W + (uint32_t)(i / 8) * sbo + (uint32_t)((k / 8) * 16 + (k % 8) * 2);
     }
     a = swz(a, lt);
+    if ((size_t)a + 2 > smem->size()) throw std::out_of_range("MMA operand read outside shared memory");
     uint16_t h; std::memcpy(&h, smem->data() + a, 2);
     return h2f(h);
   }
@@ -64,6 +68,7 @@ struct HostOps {
     const int N = (int)((idesc >> 17) & 63) * 8, M = (int)((idesc >> 24) & 31) * 16;
     const bool amn = (idesc >> 15) & 1, bmn = (idesc >> 16) & 1, f32 = (idesc >> 4) & 1;
     const int col = (int)(d & 0xFFFF);
+    if (col + N > tmem_cols) throw std::out_of_range("MMA accumulator outside the TMEM allocation");
     for (int i = 0; i < M; i++)
       for (int n = 0; n < N; n++) {
         double s = 0;
@@ -81,11 +86,13 @@ struct HostOps {
   }
   void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
     const int lane = (int)(taddr >> 16) + cur_lane % 32, col = (int)(taddr & 0xFFFF);
+    if (lane >= 128 || col + 16 > tmem_cols) throw std::out_of_range("tcgen05.ld outside the TMEM allocation");
     for (int j = 0; j < 16; j++) r[j] = (*tmem)[(size_t)lane * 512 + col + j];
   }
   void tmem_wait() {}
   void st16(uint32_t off, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
     const uint32_t w[4] = {a, b, c, d};
+    if ((off & 15) || (size_t)off + 16 > data_bytes) throw std::out_of_range("epilogue store outside the data buffer");
     std::memcpy(smem->data() + off, w, 16);
   }
   void sincospi(float x, float* s, float* c) {
@@ -130,7 +137,7 @@ int run_plan(const void* u, const float* Kf, void* y, int B, int H) {
   std::vector<uint8_t> smem(P::DATA_BYTES + P::BMAT_BYTES, 0);
   std::vector<uint32_t> tmem(128 * 512, 0);
   hostmath::build_bmat_image<P>(smem.data() + P::DATA_BYTES);
-  HostOps ops{&smem, &tmem, 0, ACC16};
+  HostOps ops{&smem, &tmem, 0, ACC16, P::TMEM_COLS, (size_t)P::DATA_BYTES};
   for (int cta = 0; cta < grid; cta++) {
     std::memset(smem.data(), 0xFF, P::DATA_BYTES);   // poison: stale data must never be read
     for (int tid = 0; tid < P::NT; tid++) load_input<P, TIO>(ops, (const TIO*)u, cta, B, H, tid);
@@ -149,6 +156,7 @@ extern "C" {
 int sffft_emu_conv(const char* config, int io, int acc, const void* u, const float* Kf, void* y, int B, int H) {
   using namespace sffft;
   int rc = 2;
+  try {
 #define SF_EMU_CASE(R0, R1, R2, G, W, NAME)                                                           \
   if (std::string(config) == NAME) {                                                                  \
     using Pl = Plan<R0, R1, R2, G, W>;                                                                \
@@ -159,6 +167,9 @@ int sffft_emu_conv(const char* config, int io, int acc, const void* u, const flo
   }
   SFFFT_CATALOG(SF_EMU_CASE)
 #undef SF_EMU_CASE
+  } catch (const std::exception&) {
+    return 3;
+  }
   return rc;
 }
 }

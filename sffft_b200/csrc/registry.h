@@ -1,0 +1,24 @@
+// Registry of compiled fused-kernel instances, one entry per catalog plan.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace sffft {
+
+struct ConvParams;
+typedef cudaError_t (*ConvLaunchFn)(const ConvParams& prm, int grid, int smem_bytes, cudaStream_t st);
+
+struct ConvEntry {
+  const char* name;            // "64x32/w4"
+  int R0, R1, R2, G, W, N, L, threads, smem_bytes, bmat_bytes, tmem_cols;
+  ConvLaunchFn launch[2][2];   // [io: 0 fp32, 1 bf16][acc: 0 fp32, 1 fp16]
+  const void* func[2][2];      // kernel function pointers (attributes, occupancy)
+  void (*build_bmat)(uint8_t* img);   // host builder of the cached DFT-matrix image
+};
+
+// Each translation unit kernels_<part>.cu registers the catalog entries of its size range.
+int entries_small(const ConvEntry** out);   // N <= 2048
+int entries_mid(const ConvEntry** out);     // N = 4096, 8192
+int entries_large(const ConvEntry** out);   // N >= 16384
+
+}  // namespace sffft

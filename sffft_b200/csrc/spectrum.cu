@@ -1,0 +1,101 @@
+// Filter-spectrum preparation: Kf[h][p] = sum_{n<L} k[h][n] * exp(-2*pi*i*n*f(p)/N) in fp32, written in
+// the plan's digit order (position p = k0*R1*R2 + k1*R2 + k2 holds frequency f = k0 + R0*k1 + R0*R1*k2).
+//
+// Replaces the reference's host zero-padding + cufftExecC2C + permuteK (sfFFT src/sffft.cu:342-344,
+// 365, 283-288, 384) with one kernel launch per digit that works in place in the caller's Kf buffer:
+// stage j loads whole length-R_j vectors of a channel into shared memory, does a direct DFT with an
+// exact twiddle table (sincospif of a reduced rational argument), applies the four-step twiddle
+// w_N^(R0..R_{j-1} * inner * k_j) (the exponent of src/sffft.cu:106-113, unscaled), and writes the
+// vectors back.  Stage 0 reads the real filter (fp32 or bf16), zero-padded to N, directly.
+// Like the reference's prep it runs once per channel and plan, outside the timed convolution.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace sffft {
+
+struct SpecStage {
+  int N, L, R, stride, pre;   // digit radix, stride of the digit, product of the radices before it
+  int vec_per_cta;            // vectors handled by one CTA
+  int twiddle;                // apply the inter-stage twiddle after this digit (not the last digit)
+};
+
+__device__ __forceinline__ float k_to_float(float v) { return v; }
+__device__ __forceinline__ float k_to_float(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+template <class TK, bool FIRST>
+__global__ void __launch_bounds__(256) spectrum_stage_kernel(float2* __restrict__ Kf, const TK* __restrict__ k, SpecStage st) {
+  extern __shared__ float2 sbuf[];
+  float2* tab = sbuf;                 // w_R^q, q in [0, R)
+  float2* x = sbuf + st.R;            // vec_per_cta vectors of R complex values
+  const int R = st.R, VB = st.vec_per_cta, N = st.N;
+  const int vec_per_ch = N / R, cta_per_ch = vec_per_ch / VB;
+  const int h = blockIdx.x / cta_per_ch, v0 = (blockIdx.x % cta_per_ch) * VB;
+  float2* Kh = Kf + (size_t)h * N;
+
+  for (int q = threadIdx.x; q < R; q += blockDim.x) {
+    float s, c;
+    sincospif(-2.0f * (float)q / (float)R, &s, &c);
+    tab[q] = make_float2(c, s);
+  }
+  for (int i = threadIdx.x; i < VB * R; i += blockDim.x) {
+    const int vl = i / R, d = i - vl * R, v = v0 + vl;
+    const int outer = v / st.stride, inner = v - outer * st.stride;
+    const int p = outer * R * st.stride + d * st.stride + inner;
+    float2 val;
+    if constexpr (FIRST) val = make_float2(p < st.L ? k_to_float(k[(size_t)h * st.L + p]) : 0.f, 0.f);
+    else val = Kh[p];
+    x[i] = val;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < VB * R; i += blockDim.x) {
+    const int vl = i / R, kk = i - vl * R, v = v0 + vl;
+    const float2* xv = x + vl * R;
+    float re = 0.f, im = 0.f;
+    for (int d = 0; d < R; d++) {
+      const float2 w = tab[(d * kk) & (R - 1)], a = xv[d];
+      re = fmaf(a.x, w.x, fmaf(-a.y, w.y, re));
+      im = fmaf(a.x, w.y, fmaf(a.y, w.x, im));
+    }
+    const int outer = v / st.stride, inner = v - outer * st.stride;
+    if (st.twiddle) {
+      int e = (int)(((long long)st.pre * inner * kk) & (N - 1));
+      if (e > N / 2) e -= N;
+      float s, c;
+      sincospif(-2.0f * (float)e / (float)N, &s, &c);
+      const float nr = re * c - im * s;
+      im = re * s + im * c;
+      re = nr;
+    }
+    Kh[outer * R * st.stride + kk * st.stride + inner] = make_float2(re, im);
+  }
+}
+
+// Runs the digit stages for radices R[0..S-1] over H channels of a filter of length L = N/2.
+// k_bf16: the filter holds bf16 values instead of fp32.
+cudaError_t launch_spectrum(float2* Kf, const void* k, bool k_bf16, int H, const int* R, int S, cudaStream_t stream) {
+  int N = 1;
+  for (int j = 0; j < S; j++) N *= R[j];
+  int stride = N, pre = 1;
+  for (int j = 0; j < S; j++) {
+    stride /= R[j];
+    SpecStage st;
+    st.N = N; st.L = N / 2; st.R = R[j]; st.stride = stride; st.pre = pre; st.twiddle = (j + 1 < S);
+    const int vec_per_ch = N / R[j];
+    st.vec_per_cta = vec_per_ch < 2048 / R[j] ? vec_per_ch : 2048 / R[j];
+    const int grid = H * (vec_per_ch / st.vec_per_cta);
+    const size_t smem = (size_t)(st.R + st.vec_per_cta * st.R) * sizeof(float2);
+    if (j == 0) {
+      if (k_bf16) spectrum_stage_kernel<__nv_bfloat16, true><<<grid, 256, smem, stream>>>(Kf, (const __nv_bfloat16*)k, st);
+      else spectrum_stage_kernel<float, true><<<grid, 256, smem, stream>>>(Kf, (const float*)k, st);
+    } else {
+      spectrum_stage_kernel<float, false><<<grid, 256, smem, stream>>>(Kf, nullptr, st);
+    }
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    pre *= R[j];
+  }
+  return cudaSuccess;
+}
+
+}  // namespace sffft

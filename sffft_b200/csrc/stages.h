@@ -230,6 +230,9 @@ SF_HD void epilogue_row(Ops& ops, const EpiArgs& ea, int t, int q, int lane) {
 // ---------------------------------------------------------------------------------------------
 // Calls emit(byte_off, radix, phase_index q, which, set) for every fp16 entry of the region;
 // `which`: 0 -> cos(2*pi*q/R), 1 -> -sin(2*pi*q/R), 2 -> +sin(2*pi*q/R); `set` 0 = hi, 1 = lo.
+#ifdef __CUDACC__
+#pragma nv_exec_check_disable
+#endif
 template <class P, class Emit>
 SF_HD void for_each_bmat_entry(Emit& emit, int tid, int nthreads) {
   for (int set = 0; set < P::NSET; set++) {

@@ -1,0 +1,105 @@
+"""ctypes access to the C oracle (oracle/liboracle.so) plus numpy restatements used by the tests.
+
+Test infrastructure only (the product path never imports this)."""
+import ctypes
+import os
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+LIB = os.path.join(ROOT, "oracle", "liboracle.so")
+
+
+class Oracle:
+    def __init__(self):
+        if not os.path.exists(LIB):
+            raise RuntimeError(f"oracle library missing: {LIB} (run `make -C oracle`)")
+        self.lib = ctypes.CDLL(LIB)
+        V, I, D, ULL = ctypes.c_void_p, ctypes.c_int, ctypes.c_double, ctypes.c_ulonglong
+        self.lib.oracle_nrand_stream.argtypes = [ULL, I, V]
+        self.lib.oracle_gen_reference.argtypes = [ULL, I, I, I, D, V, V]
+        self.lib.oracle_gen_profile.argtypes = [ULL, I, I, I, D, I, V, V]
+        self.lib.oracle_direct_conv.argtypes = [V, V, V, I, I, I, I]
+        self.lib.oracle_direct_conv_seqs.argtypes = [V, V, V, I, I, I, V, I, I]
+        self.lib.oracle_max_threads.restype = I
+
+    def nrand(self, seed, n):
+        out = np.zeros(n, np.float64)
+        self.lib.oracle_nrand_stream(seed, n, out.ctypes.data)
+        return out
+
+    def gen_reference(self, B, H, L, seed=0, input_scale=1.0):
+        u = np.zeros((B, H, L), np.float32)
+        k = np.zeros((H, L), np.float32)
+        self.lib.oracle_gen_reference(seed, B, H, L, input_scale, u.ctypes.data, k.ctypes.data)
+        return u, k
+
+    def gen_profile(self, B, H, L, decay=4.0, sqrt_norm=True, seed=0):
+        u = np.zeros((B, H, L), np.float32)
+        k = np.zeros((H, L), np.float32)
+        self.lib.oracle_gen_profile(seed, B, H, L, decay, 1 if sqrt_norm else 0, u.ctypes.data, k.ctypes.data)
+        return u, k
+
+    def direct_conv(self, u, k, threads=0):
+        u = np.ascontiguousarray(u, np.float32)
+        k = np.ascontiguousarray(k, np.float32)
+        B, H, L = u.shape
+        y = np.zeros((B, H, L), np.float64)
+        self.lib.oracle_direct_conv(u.ctypes.data, k.ctypes.data, y.ctypes.data, B, H, L, threads)
+        return y
+
+    def direct_conv_seqs(self, u, k, seqs, threads=0):
+        u = np.ascontiguousarray(u, np.float32)
+        k = np.ascontiguousarray(k, np.float32)
+        B, H, L = u.shape
+        seqs = np.ascontiguousarray(seqs, np.int64)
+        y = np.zeros((len(seqs), L), np.float64)
+        self.lib.oracle_direct_conv_seqs(u.ctypes.data, k.ctypes.data, y.ctypes.data, B, H, L, seqs.ctypes.data,
+                                         len(seqs), threads)
+        return y
+
+    def max_threads(self):
+        return self.lib.oracle_max_threads()
+
+
+def digit_order(radices):
+    """Frequency held at each digit-order position (src/sffft.cu:283-288)."""
+    R0, R1, R2 = (list(radices) + [1, 1])[:3]
+    N = R0 * R1 * R2
+    p = np.arange(N)
+    if R2 > 1:
+        d2 = p % R2
+        d1 = (p // R2) % R1
+        d0 = p // (R1 * R2)
+    else:
+        d2 = 0
+        d1 = p % R1
+        d0 = p // R1
+    return d0 + R0 * (d1 + R1 * d2)
+
+
+def spectrum_digit_order(k, radices):
+    """Unnormalised DFT of the zero-padded filter in digit order, complex128 [H, N] (fp64 restatement of
+    cufftExecC2C + permuteK, src/sffft.cu:344,365,283-288)."""
+    k = np.asarray(k, np.float64)
+    H, L = k.shape
+    Kc = np.fft.fft(np.concatenate([k, np.zeros((H, L))], axis=1), axis=1)
+    return Kc[:, digit_order(radices)]
+
+
+def to_bf16(x):
+    """Round-to-nearest-even fp32 -> bf16, returned as fp32 values."""
+    x = np.ascontiguousarray(x, np.float32)
+    b = x.view(np.uint32).astype(np.uint64)
+    b = (b + 0x7FFF + ((b >> 16) & 1)) >> 16
+    return (b.astype(np.uint32) << 16).view(np.float32).reshape(x.shape)
+
+
+def bf16_bits(x):
+    x = np.ascontiguousarray(x, np.float32)
+    b = x.view(np.uint32).astype(np.uint64)
+    return ((b + 0x7FFF + ((b >> 16) & 1)) >> 16).astype(np.uint16).reshape(x.shape)
+
+
+def bf16_from_bits(b):
+    return (np.asarray(b, np.uint32) << 16).view(np.float32)

@@ -1,0 +1,69 @@
+"""The fused kernel's stage code run on the CPU with an emulated tcgen05 backend (sffft_b200/csrc/emu.cpp),
+against the fp64 oracle.  This checks every plan's shared-memory layouts, UMMA descriptors, pairing,
+twiddles and digit order without a GPU; the GPU parity tests check the same code on B200."""
+import numpy as np
+import pytest
+
+import sffft_b200 as sf
+from tests.conftest import rel_l2
+from tests.oracle_py import bf16_bits, bf16_from_bits, spectrum_digit_order, to_bf16
+
+TOL = {("fp32", "fp32"): 5e-4, ("bf16", "fp32"): 3e-3, ("fp32", "fp16"): 1e-3, ("bf16", "fp16"): 4e-3}
+
+
+def radices(name):
+    return [int(x) for x in name.split("/")[0].split("x")]
+
+
+def run_case(oracle, name, B, H, io="fp32", acc="fp32", seed=0):
+    R = radices(name)
+    L = int(np.prod(R)) // 2
+    u, k = oracle.gen_profile(B, H, L, decay=4.0, sqrt_norm=True, seed=seed + 1)
+    if io == "bf16":
+        u, k = to_bf16(u), to_bf16(k)
+    Kc = spectrum_digit_order(k, R)
+    Kf = np.stack([Kc.real, Kc.imag], -1).astype(np.float32)
+    if io == "bf16":
+        y = bf16_from_bits(sf.emu_conv(name, bf16_bits(u), Kf, io="bf16", acc=acc)).reshape(u.shape)
+    else:
+        y = sf.emu_conv(name, u, Kf, io="fp32", acc=acc)
+    ref = oracle.direct_conv(u, k)
+    return rel_l2(y, ref)
+
+
+CATALOG = [n for L, n in sf.catalog()]
+
+
+@pytest.mark.parametrize("name", [n for n in CATALOG if int(np.prod(radices(n))) <= 8192])
+def test_every_plan_fp32(oracle, name):
+    N = int(np.prod(radices(name)))
+    B, H = (3, 2) if N <= 4096 else (2, 1)
+    assert run_case(oracle, name, B, H) <= TOL[("fp32", "fp32")]
+
+
+def test_largest_plan(oracle):
+    assert run_case(oracle, "32x32x32/w4", 1, 1) <= TOL[("fp32", "fp32")]
+
+
+@pytest.mark.parametrize("name", ["16x16/w4", "64x32/w4", "32x16x16/w4"])
+@pytest.mark.parametrize("io,acc", [("bf16", "fp32"), ("fp32", "fp16"), ("bf16", "fp16")])
+def test_io_and_accumulation_modes(oracle, name, io, acc):
+    assert run_case(oracle, name, 2, 1, io=io, acc=acc) <= TOL[(io, acc)]
+
+
+def test_odd_batch_and_partial_ctas(oracle):
+    # B=5 leaves one unpaired sequence per channel; H=3 with G=8 pairs per CTA leaves a partial CTA
+    assert run_case(oracle, "16x16/w4", 5, 3) <= 5e-4
+    assert run_case(oracle, "32x32/w4", 1, 5) <= 5e-4
+
+
+def test_zero_and_impulse_inputs():
+    L = 128
+    u = np.zeros((2, 1, L), np.float32)
+    Kf = np.zeros((1, 2 * L, 2), np.float32)
+    assert not sf.emu_conv("16x16/w4", u, Kf).any()
+    # impulse filter k = delta: Kf = 1 everywhere -> y = u (to fp16-pipeline accuracy)
+    rng = np.random.default_rng(3)
+    u = rng.standard_normal((2, 1, L)).astype(np.float32)
+    Kf[..., 0] = 1.0
+    assert rel_l2(sf.emu_conv("16x16/w4", u, Kf), u) < 5e-4
