@@ -6,7 +6,7 @@ CPU (this container, where /root/reference exists):
   own src/sffft.cu built in place, and records the first draws of its nrand() for three seeds.
 
 GPU box (the harness binary travels with the repository):
-    python tests/golden/make_golden.py results
+    python tests/golden/make_golden.py results [OUT_DIR]
   runs the unmodified reference benchmark (ref_harness run ...) and records its RESULT/SELECT rows on B200.
 """
 import json
@@ -38,15 +38,18 @@ RUNS = [
 ]
 
 
-def results():
+def results(out_dir=HERE):
     rows = []
     for args in RUNS:
         p = subprocess.run([HARNESS, "run"] + args, capture_output=True, text=True, timeout=1200)
         rows.append({"args": args, "exit": p.returncode, "stdout": p.stdout})
-    with open(os.path.join(HERE, "ref_results_b200.json"), "w") as f:
+    with open(os.path.join(out_dir, "ref_results_b200.json"), "w") as f:
         json.dump({"source": "unmodified reference benchmark (src/sffft.cu main) built for sm_100a, run on B200",
                    "runs": rows}, f, indent=1)
 
 
 if __name__ == "__main__":
-    {"rng": rng, "results": results}[sys.argv[1]]()
+    if sys.argv[1] == "rng":
+        rng()
+    else:
+        results(sys.argv[2] if len(sys.argv) > 2 else HERE)
