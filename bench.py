@@ -1,0 +1,330 @@
+"""Benchmark of the fused causal long convolution (BASELINE.json metric: ms per B=8 x H=768 batch and
+fraction of the HBM / tensor roofline).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--L 1024] [--io fp32]
+    torchrun --nproc-per-node N bench.py --gpus N ...      (one rank per GPU)
+
+Workload (default): BASELINE.json configs[1] -- B=8, H=768 channels per GPU, L=1024, fp32 I/O, fp32
+accumulation, u ~ N(0,1), k = N(0,1) exp(-4n/L)/sqrt(L).  A step is one sffft_conv launch over the
+GPU's batch.  With N GPUs each rank owns its own 768-channel slice of an N*768-channel batch (channel
+sharding, weak scaling, no collective on the data path); `value` is the whole job's ms per 8 x 768 batch
+= max-over-ranks step time / N.  Inputs rotate over four independent sets (u, y, Kf) of ~63 MB each so that
+every step reads from HBM, not from the 126 MB L2.
+
+--impl reference times the reference's CPU path for the same metric -- the fp64 direct causal convolution
+(sfFFT src/sffft.cu:376-378, restated in oracle/oracle.c) on all host cores -- on a bounded sample of
+sequences per step, scaled to a full batch; under torchrun only rank 0 runs it.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "ms/batch and % of roofline, B=8×H=768, L=128–8192, fp32/bf16 I/O"
+UNIT = "ms/batch"
+GB10_PUBLISHED_MS = {(1024, "fp32"): 0.459, (1024, "bf16"): 0.440, (128, "fp32"): 0.033, (4096, "bf16"): 1.342,
+                     (8192, "bf16"): 3.434, (8192, "fp32"): 4.184}
+NSETS = 4
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        p = json.load(open(path))
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+def flops_per_seq(radices):
+    N = 1
+    for r in radices:
+        N *= r
+    return 4 * radices[0] * N + 16 * N * sum(radices[1:])
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--L", type=int, default=1024)
+    ap.add_argument("--B", type=int, default=8)
+    ap.add_argument("--H", type=int, default=768)
+    ap.add_argument("--io", default="fp32", choices=["fp32", "bf16"])
+    ap.add_argument("--acc", default="fp32", choices=["fp32", "fp16"])
+    ap.add_argument("--config", default=None)
+    ap.add_argument("--e2e-steps", type=int, default=10)
+    return ap.parse_args()
+
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        time.sleep(0.3)
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.2)
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        loaded = [s for s in sm if smax and s > 0.5 * smax] or sm
+        return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def make_inputs(torch, dev, B, H, L, io, seed):
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    u = torch.randn((B, H, L), device=dev, generator=g)
+    n = torch.arange(L, device=dev, dtype=torch.float32)
+    k = torch.randn((H, L), device=dev, generator=g) * torch.exp(-4.0 * n / L) / L ** 0.5
+    if io == "bf16":
+        u, k = u.to(torch.bfloat16), k.to(torch.bfloat16)
+    return u, k
+
+
+def cpu_baseline_run(args, budget_s=15.0):
+    """fp64 direct convolution of a bounded sample on all host cores; returns (ms per full batch, info)."""
+    import numpy as np
+
+    from tests.oracle_py import Oracle
+    oracle = Oracle()
+    B, H, L = args.B, args.H, args.L
+    rng = np.random.default_rng(0)
+    u = rng.standard_normal((B, H, L)).astype(np.float32)
+    k = (rng.standard_normal((H, L)) * np.exp(-4.0 * np.arange(L) / L) / np.sqrt(L)).astype(np.float32)
+    total = B * H
+    # size the sample to roughly budget_s of work from a short calibration
+    t0 = time.perf_counter()
+    oracle.direct_conv_seqs(u, k, np.arange(min(64, total)))
+    per_seq = (time.perf_counter() - t0) / min(64, total)
+    n = int(max(64, min(total, budget_s / max(per_seq, 1e-9))))
+    seqs = np.linspace(0, total - 1, n).astype(np.int64)
+    t0 = time.perf_counter()
+    oracle.direct_conv_seqs(u, k, seqs)
+    dt = time.perf_counter() - t0
+    ms_batch = dt * 1e3 * total / n
+    return ms_batch, {"cores": oracle.max_threads(), "sample": f"{n} of {total} sequences (B={B} H={H} L={L}), "
+                      f"fp64 direct causal convolution, scaled to the full batch", "seconds": round(dt, 2)}
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return
+    ms_steps = []
+    for _ in range(max(1, args.warmup // 3)):
+        cpu_baseline_run(args, budget_s=2.0)
+    for _ in range(args.steps if args.steps <= 5 else 5):
+        ms, info = cpu_baseline_run(args, budget_s=10.0)
+        ms_steps.append(ms)
+    value = statistics.median(ms_steps)
+    line = {"impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": args.gpus,
+            "steps": len(ms_steps), "warmup": max(1, args.warmup // 3), "ms_per_step": round(value, 4),
+            "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+            "data": "synthetic", "config": {"workload": f"causal long conv B={args.B} H={args.H} L={args.L}",
+                                            "B": args.B, "H": args.H, "L": args.L, "io": args.io},
+            "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": info["cores"], "kind": "port",
+                             "sample": info["sample"]},
+            "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    world, rank, local = dist_setup(args)
+    if args.impl == "reference":
+        run_reference(args, world, rank)
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+        return
+
+    import numpy as np
+    import torch
+    import sffft_b200 as sf
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    B, H, L = args.B, args.H, args.L
+    plan = sf.Plan(L, io=args.io, acc=args.acc, config=args.config, device=local)
+    stream = torch.cuda.current_stream(dev)
+    sets = []
+    for s in range(NSETS):
+        u, k = make_inputs(torch, dev, B, H, L, args.io, seed=1000 * rank + s)
+        Kf = plan.filter_spectrum(k, stream=stream)
+        sets.append((u, Kf, torch.empty_like(u)))
+    torch.cuda.synchronize(dev)
+
+    def step(i):
+        u, Kf, y = sets[i % NSETS]
+        st = plan.conv_ptr(u.data_ptr(), Kf.data_ptr(), y.data_ptr(), B, H, stream)
+        if st:
+            raise sf.SffftError(st, "conv")
+
+    for i in range(args.warmup):
+        step(i)
+    plan.check()
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier(device_ids=[local])
+
+    clocks = ClockSampler(local)
+    clocks.start()
+    barrier()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        step(i)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    ms_total = e0.elapsed_time(e1)
+    clk = clocks.stop()
+    plan.check()
+    ms_step = ms_total / args.steps
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([ms_step], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_step = float(t.item())
+
+    # end to end through the C ABI with host buffers: H2D of u, the fused conv, D2H of y, every step
+    u_h = torch.empty((B, H, L), dtype=sets[0][0].dtype, pin_memory=True)
+    u_h.copy_(sets[0][0].cpu())
+    y_h = torch.empty_like(u_h, pin_memory=True)
+    u_d, Kf_d, y_d = sets[0]
+    for _ in range(2):
+        u_d.copy_(u_h, non_blocking=True)
+        plan.conv(u_d, Kf_d, y_d, stream=stream)
+        y_h.copy_(y_d, non_blocking=True)
+    torch.cuda.synchronize(dev)
+    barrier()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for _ in range(args.e2e_steps):
+        u_d.copy_(u_h, non_blocking=True)
+        plan.conv(u_d, Kf_d, y_d, stream=stream)
+        y_h.copy_(y_d, non_blocking=True)
+    f1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_step = f0.elapsed_time(f1) / args.e2e_steps
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([e2e_step], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_step = float(t.item())
+
+    if rank == 0:
+        s_io = 4 if args.io == "fp32" else 2
+        N = 2 * L
+        alg_bytes = 2 * B * H * L * s_io + H * N * 8
+        alg_flops = B * H * flops_per_seq(plan.radices)
+        hbm, tc, src = peaks()
+        t_hbm, t_tc = alg_bytes / (hbm * 1e9), alg_flops / (tc * 1e12)
+        bound = "hbm" if t_hbm >= t_tc else "tensor"
+        if bound == "hbm":
+            achieved, peak, unit = alg_bytes / (ms_step * 1e-3) / 1e9, hbm, "GB/s"
+        else:
+            achieved, peak, unit = alg_flops / (ms_step * 1e-3) / 1e12, tc, "TFLOP/s"
+        traffic = None
+        tp = os.path.join(ROOT, "profiles", "traffic.json")
+        if os.path.exists(tp):
+            tj = json.load(open(tp))
+            traffic = tj.get(f"{plan.config}|{args.io}|{L}|{B}x{H}")
+        cpu_ms, cpu_info = (None, None)
+        if world == 1:
+            cpu_ms, cpu_info = cpu_baseline_run(args)
+        value = ms_step / world
+        pub = GB10_PUBLISHED_MS.get((L, args.io)) if (B, H, args.acc) == (8, 768, "fp32") else None
+        line = {
+            "metric": METRIC, "value": round(value, 5), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": False, "scaling": "weak",
+            "vs_baseline": round(value / pub, 4) if pub else None, "dtype": "f16",
+            "data": "synthetic (seeded torch.randn u; k = N(0,1) exp(-4n/L)/sqrt(L))",
+            "config": {"workload": f"BASELINE configs[1]: causal long conv B={B} H={H} per GPU, L={L}, "
+                                   f"{args.io} I/O, {args.acc} accumulation",
+                       "plan": plan.config, "B": B, "H_per_gpu": H, "H_total": H * world, "L": L, "io": args.io,
+                       "acc": args.acc, "occupancy": plan.info["occupancy"], "smem_bytes": plan.info["smem_bytes"],
+                       "parallelism": f"channel-sharded x{world}, no collective on the data path",
+                       "l2": f"{NSETS} rotating input/output/spectrum sets of {alg_bytes / 1e6:.0f} MB each "
+                             f"(> 126 MB L2 in aggregate)",
+                       "vs_baseline_ref": "reference GB10 published ms/batch (README.md:29-35)" if pub else None},
+            "roofline": {"bound": bound, "achieved": round(achieved, 2), "peak": peak, "unit": unit,
+                         "frac": round(achieved / peak, 4), "traffic": traffic,
+                         "peak_source": f"{src} (MEASURED_PEAKS.json)" if src == "measured" else src,
+                         "algorithmic_bytes": alg_bytes, "algorithmic_flops": alg_flops,
+                         "t_roof_ms": round(max(t_hbm, t_tc) * 1e3, 5)},
+            "e2e": {"value": round(e2e_step / world, 5), "unit": UNIT, "h2d_bytes_per_step": u_h.numel() * u_h.element_size(),
+                    "d2h_bytes_per_step": y_h.numel() * y_h.element_size(),
+                    "path": "pinned host u -> H2D -> sffft_conv (C ABI) -> D2H y, per step"},
+            "gpu_launches": args.steps * world,
+            "clocks": clk,
+        }
+        if cpu_ms is not None:
+            line["cpu_baseline"] = {"value": round(cpu_ms, 3), "unit": UNIT, "cores": cpu_info["cores"], "kind": "port",
+                                    "sample": cpu_info["sample"]}
+        print(json.dumps(line), flush=True)
+    plan.close()
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
