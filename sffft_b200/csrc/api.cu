@@ -27,7 +27,7 @@ using namespace sffft;
 
 struct sffft_plan {
   const ConvEntry* e;
-  int io, acc, kernel_mode, device, occupancy, smem_launch;
+  int io, acc, kernel_mode, device, occupancy, smem_launch, sms;
   uint4* btab;   // cached DFT-matrix image (device), null in legacy mode
   int* status;   // device status word
 };
@@ -131,33 +131,24 @@ int sffft_plan_create(sffft_plan_t* out, int L, int io, int acc, const char* con
   if ((ce = cudaSetDevice(device)) != cudaSuccess) return cuda_fail(ce);
   cudaDeviceProp prop;
   if ((ce = cudaGetDeviceProperties(&prop, device)) != cudaSuccess) return cuda_fail(ce);
-  if (prop.major != 10 || prop.minor != 0 || (int)prop.sharedMemPerBlockOptin < e->smem_bytes) return SFFFT_ERR_DEVICE;
+  const int need = e->smem_bytes[io];
+  if (prop.major != 10 || prop.minor != 0 || (int)prop.sharedMemPerBlockOptin < need) return SFFFT_ERR_DEVICE;
 
+  // The kernel is persistent with one CTA per SM (the grid never exceeds the SM count).  Requesting
+  // more than half of an SM's shared memory keeps the block scheduler from placing two CTAs on one SM.
+  int smem_launch = need;
+  const int half = (int)prop.sharedMemPerMultiprocessor / 2 + 1024;
+  if (smem_launch < half) smem_launch = half;
+  if (smem_launch > (int)prop.sharedMemPerBlockOptin) smem_launch = (int)prop.sharedMemPerBlockOptin;
   const void* fn = e->func[io][acc];
-  if ((ce = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, e->smem_bytes)) != cudaSuccess)
+  if ((ce = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_launch)) != cudaSuccess)
     return cuda_fail(ce);
-  int occ = 0;
-  if ((ce = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, e->threads, e->smem_bytes)) != cudaSuccess)
-    return cuda_fail(ce);
-  if (occ < 1) return SFFFT_ERR_DEVICE;
-  // Co-resident CTAs must fit the 512 TMEM columns of an SM; otherwise a CTA's tcgen05.alloc would stall
-  // until another CTA frees its columns.  Enlarge the dynamic shared memory request to cap residency.
-  int smem_launch = e->smem_bytes;
-  const int max_res = 512 / e->tmem_cols;
-  if (occ > max_res) {
-    const int per_sm = (int)prop.sharedMemPerMultiprocessor;
-    smem_launch = per_sm / max_res - 1024;
-    if (smem_launch > (int)prop.sharedMemPerBlockOptin) smem_launch = (int)prop.sharedMemPerBlockOptin;
-    if (smem_launch < e->smem_bytes) smem_launch = e->smem_bytes;
-    if ((ce = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_launch)) != cudaSuccess)
-      return cuda_fail(ce);
-    if ((ce = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, e->threads, smem_launch)) != cudaSuccess)
-      return cuda_fail(ce);
-  }
+  const int occ = 1;
 
   sffft_plan* p = new sffft_plan();
   p->e = e; p->io = io; p->acc = acc; p->kernel_mode = kernel_mode; p->device = device;
-  p->occupancy = occ; p->smem_launch = smem_launch; p->btab = nullptr; p->status = nullptr;
+  p->occupancy = occ; p->smem_launch = smem_launch; p->sms = prop.multiProcessorCount;
+  p->btab = nullptr; p->status = nullptr;
   if ((ce = cudaMalloc(&p->status, sizeof(int))) != cudaSuccess || (ce = cudaMemset(p->status, 0, sizeof(int))) != cudaSuccess) {
     cudaFree(p->status);
     delete p;
@@ -195,7 +186,8 @@ int sffft_plan_info(sffft_plan_t p, sffft_plan_info_t* info) {
   std::memset(info, 0, sizeof(*info));
   info->L = e->L; info->N = e->N; info->stages = e->R2 > 1 ? 3 : 2;
   info->R0 = e->R0; info->R1 = e->R1; info->R2 = e->R2; info->pairs_per_cta = e->G;
-  info->warps = e->W; info->threads = e->threads; info->smem_bytes = p->smem_launch; info->tmem_cols = e->tmem_cols;
+  info->warps = e->W; info->threads = e->threads; info->smem_bytes = e->smem_bytes[p->io];
+  info->tmem_cols = e->tmem_cols[p->io];
   info->occupancy = p->occupancy; info->io = p->io; info->acc = p->acc; info->kernel_mode = p->kernel_mode;
   info->device = p->device;
   std::strncpy(info->config, e->name, sizeof(info->config) - 1);
@@ -226,14 +218,16 @@ int sffft_conv(sffft_plan_t p, const void* u, const void* Kf, void* y, int B, in
   if ((((uintptr_t)u | (uintptr_t)y | (uintptr_t)Kf) & 15) != 0) return SFFFT_ERR_INVALID_ARGUMENT;
   const ConvEntry* e = p->e;
   const long long pairs = (long long)((B + 1) / 2) * H;
-  const long long grid = (pairs + e->G - 1) / e->G;
-  if ((long long)B * H > std::numeric_limits<int>::max() || grid > std::numeric_limits<int>::max())
+  const long long groups = (pairs + e->G - 1) / e->G;
+  if ((long long)B * H > std::numeric_limits<int>::max() || groups > std::numeric_limits<int>::max())
     return SFFFT_ERR_INVALID_ARGUMENT;
+  const int grid = (int)(groups < p->sms ? groups : p->sms);
   int rc = use_device(p->device);
   if (rc) return rc;
   ConvParams prm;
   prm.u = u; prm.Kf = (const float*)Kf; prm.btab = p->btab; prm.y = y; prm.status = p->status; prm.B = B; prm.H = H;
-  const cudaError_t ce = e->launch[p->io][p->acc](prm, (int)grid, p->smem_launch, (cudaStream_t)stream);
+  prm.ngroups = (int)groups;
+  const cudaError_t ce = e->launch[p->io][p->acc](prm, grid, p->smem_launch, (cudaStream_t)stream);
   return ce == cudaSuccess ? SFFFT_OK : cuda_fail(ce);
 }
 

@@ -36,6 +36,7 @@ static inline uint32_t bf16_from_float(float f) {
 
 struct HostOps {
   std::vector<uint8_t>* smem;
+  uint32_t base;                 // byte offset of the data buffer that st16 writes
   std::vector<uint32_t>* tmem;   // 128 lanes x 512 columns
   int cur_lane;                  // TMEM lane of the emulated thread
   bool acc16;
@@ -68,7 +69,7 @@ struct HostOps {
     const int N = (int)((idesc >> 17) & 63) * 8, M = (int)((idesc >> 24) & 31) * 16;
     const bool amn = (idesc >> 15) & 1, bmn = (idesc >> 16) & 1, f32 = (idesc >> 4) & 1;
     const int col = (int)(d & 0xFFFF);
-    if (col + N > tmem_cols) throw std::out_of_range("MMA accumulator outside the TMEM allocation");
+    if (col + N > tmem_cols || col < 0) throw std::out_of_range("MMA accumulator outside the TMEM allocation");
     for (int i = 0; i < M; i++)
       for (int n = 0; n < N; n++) {
         double s = 0;
@@ -93,7 +94,7 @@ struct HostOps {
   void st16(uint32_t off, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
     const uint32_t w[4] = {a, b, c, d};
     if ((off & 15) || (size_t)off + 16 > data_bytes) throw std::out_of_range("epilogue store outside the data buffer");
-    std::memcpy(smem->data() + off, w, 16);
+    std::memcpy(smem->data() + base + off, w, 16);
   }
   void sincospi(float x, float* s, float* c) {
     *s = (float)std::sin(M_PI * (double)x);
@@ -107,8 +108,8 @@ struct HostOps {
     float f; std::memcpy(&f, &w, 4); return f;
   }
   void ldK(const float* p, float (&k)[4]) { for (int e = 0; e < 4; e++) k[e] = p[e]; }
-  void load8(const float* p, float* v) { for (int e = 0; e < 8; e++) v[e] = p[e]; }
-  void load8(const uint16_t* p, float* v) {
+  void lds8(const float* p, float* v) { for (int e = 0; e < 8; e++) v[e] = p[e]; }
+  void lds8(const uint16_t* p, float* v) {
     for (int e = 0; e < 8; e++) { uint32_t b = (uint32_t)p[e] << 16; std::memcpy(&v[e], &b, 4); }
   }
   void store1(float* p, float v) { *p = v; }
@@ -116,33 +117,55 @@ struct HostOps {
 };
 
 template <int SID, class P, class TIO, bool ACC16>
-void run_stage_emu(HostOps& ops, const EpiArgs& ea0) {
-  issue_stage<P, ACC16, SID>(ops, 0u, 0u, (uint32_t)P::DATA_BYTES);
-  EpiArgs ea = ea0;
-  ea.tmem = 0;
+void run_stage_emu(HostOps& ops, const EpiArgs& ea, uint32_t data_s, uint32_t bmat_s) {
+  issue_stage<P, ACC16, SID>(ops, ea.tmem, data_s, bmat_s);
+  constexpr int C = epi_chunks<P, SID>();
   for (int t = 0; t < P::tiles(SID); t++)
-    for (int q = 0; q < 4; q++)
-      for (int lane = 0; lane < 32; lane++) {
-        ops.cur_lane = lane;
-        epilogue_row<P, TIO, ACC16, SID>(ops, ea, t, q, lane);
-      }
-  if constexpr (SID + 1 < 2 * P::S) run_stage_emu<SID + 1, P, TIO, ACC16>(ops, ea0);
+    for (int c = 0; c < C; c++)
+      for (int q = 0; q < 4; q++)
+        for (int lane = 0; lane < 32; lane++) {
+          ops.cur_lane = lane;
+          epilogue_unit<P, TIO, ACC16, SID>(ops, ea, t, c, q, lane);
+        }
+  if constexpr (SID + 1 < 2 * P::S) run_stage_emu<SID + 1, P, TIO, ACC16>(ops, ea, data_s, bmat_s);
 }
 
+// Emulates the persistent kernel's per-group flow: the producer's staging of each chunk of the group's
+// input stream (absent sequences are not copied), conversion, then the 2S stages, alternating between
+// the kernel's data / TMEM slots.
 template <class P, class TIO, bool ACC16>
 int run_plan(const void* u, const float* Kf, void* y, int B, int H) {
+  using SH = Shape<P, (int)sizeof(TIO)>;
   const int PB = (B + 1) / 2;
   const long long pairs = (long long)PB * H;
-  const int grid = (int)((pairs + P::G - 1) / P::G);
-  std::vector<uint8_t> smem(P::DATA_BYTES + P::BMAT_BYTES, 0);
+  const int ngroups = (int)((pairs + P::G - 1) / P::G);
+  std::vector<uint8_t> smem(SH::STAGE_OFF, 0);
   std::vector<uint32_t> tmem(128 * 512, 0);
-  hostmath::build_bmat_image<P>(smem.data() + P::DATA_BYTES);
-  HostOps ops{&smem, &tmem, 0, ACC16, P::TMEM_COLS, (size_t)P::DATA_BYTES};
-  for (int cta = 0; cta < grid; cta++) {
-    std::memset(smem.data(), 0xFF, P::DATA_BYTES);   // poison: stale data must never be read
-    for (int tid = 0; tid < P::NT; tid++) load_input<P, TIO>(ops, (const TIO*)u, cta, B, H, tid);
-    EpiArgs ea{0u, Kf, y, B, H, cta};
-    run_stage_emu<0, P, TIO, ACC16>(ops, ea);
+  hostmath::build_bmat_image<P>(smem.data());
+  std::vector<uint8_t> chunk(SH::CHUNK);
+  constexpr int SEQB = P::L * (int)sizeof(TIO);
+  const TIO* uu = (const TIO*)u;
+  for (int group = 0; group < ngroups; group++) {
+    const int slot = group % SH::NSLOT;
+    const uint32_t dbase = (uint32_t)(SH::DATA_OFF + slot * P::DATA_BYTES);
+    HostOps ops{&smem, dbase, &tmem, 0, ACC16, SH::TMEM_ALLOC, (size_t)P::DATA_BYTES};
+    std::memset(smem.data() + dbase, 0xFF, P::DATA_BYTES);   // poison: stale data must never be read
+    for (int c = 0; c < SH::CPG; c++) {
+      std::memset(chunk.data(), 0xEE, chunk.size());
+      const long long b0 = (long long)c * SH::CHUNK;
+      for (long long b = b0; b < b0 + SH::CHUNK; b += (SEQB < SH::CHUNK ? SEQB : SH::CHUNK)) {
+        const int j = (int)(b / SEQB);
+        const PairInfo pi = pair_info(group, j >> 1, P::G, B, H, P::L);
+        const long long off = (j & 1) ? pi.off1 : pi.off0;
+        const int len = SEQB < SH::CHUNK ? SEQB : SH::CHUNK;
+        if (off >= 0) std::memcpy(chunk.data() + (b - b0), uu + off + (b - (long long)j * SEQB) / (int)sizeof(TIO), len);
+      }
+      for (int tid = 0; tid < 64; tid++)
+        convert_chunk<P, TIO>(ops, (const TIO*)chunk.data(), (long long)c * (SH::CHUNK / (int)sizeof(TIO)),
+                              SH::CHUNK / (int)sizeof(TIO), group, B, H, tid, 64);
+    }
+    EpiArgs ea{(uint32_t)(slot * P::TMEM_COLS), Kf, y, B, H, group};
+    run_stage_emu<0, P, TIO, ACC16>(ops, ea, dbase, 0u);
   }
   return 0;
 }

@@ -1,19 +1,23 @@
-// The fused causal-convolution kernel for sm_100a.
+// The fused causal-convolution kernel for sm_100a (persistent, warp-specialised).
 //
-// Replaces the reference kernel fftconv<Plan,W,TIO,TAcc,CACHED> (sfFFT src/sffft.cu:243-280).
-// One CTA = G pairs of sequences (two batch elements of one channel per pair); the whole working set
-// (4*N*G bytes of fp16 data + DFT matrices) stays in shared memory, accumulators live in TMEM.
+// Replaces the reference kernel fftconv<Plan,W,TIO,TAcc,CACHED> (sfFFT src/sffft.cu:243-280): the same
+// four-step transform, spectrum multiply and inverse, but one CTA per SM loops over "groups" of G pairs of
+// sequences (two batch elements of one channel per pair) with three roles:
 //
-//   setup     warp 0 allocates TMEM; thread 32 initialises the mbarrier; all threads fill the DFT
-//             matrices (copy of a cached table, or computed with sincospif: "legacy")
-//   input     u (fp32 / bf16) -> fp16 hi+lo, first-stage A operand (MN-major, 128-B swizzle)
-//   stages    for sid in 0..2S-1: thread 0 issues the stage's tcgen05.mma's and commits to the
-//             mbarrier; every thread waits (bounded), reads its TMEM lane, applies twiddle / spectrum
-//             / scale, and writes the next stage's A operand in place (or y for the last stage).
-//   teardown  warp 0 frees TMEM.
+//   warp 0 (producer)  streams each group's raw u into a shared-memory staging ring with 1-D bulk
+//                      copies (cp.async.bulk, completion through mbarrier transaction counts) and
+//                      prefetches the group's spectrum rows into L2;
+//   warp 1 (MMA)       allocates TMEM and, for every stage of every group, issues the stage's
+//                      tcgen05.mma's once the compute warps have written its A operand, then commits to
+//                      that group's "stage done" mbarrier;
+//   warps 2.. (compute) convert staged u to the first-stage operand (fp16 hi + lo) and run every stage's
+//                      epilogue: TMEM -> registers -> twiddle / spectrum / scale -> the next stage's operand
+//                      in shared memory (or y in global memory).
 //
-// A barrier wait that exceeds its limit records SFFFT_ERR_TIMEOUT in *status and the CTA skips the
-// remaining stages (still freeing TMEM), so a broken pipeline reports an error instead of hanging.
+// Two groups are in flight when their data buffers and TMEM regions fit ("slots"); the compute warps
+// alternate between them, so while they finish one group's stage the tensor core runs the other's.
+// Every wait is bounded: after kWaitLimitNs a role records SFFFT_ERR_TIMEOUT in *status, raises a shared
+// abort flag that ends the other roles' loops, drains its own bulk copies and the CTA frees its TMEM.
 #pragma once
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -30,7 +34,8 @@ constexpr unsigned long long kWaitLimitNs = 1000000000ull;   // 1 s per barrier 
 __device__ __forceinline__ float bf16_bits_to_float(uint32_t bits16) { return __uint_as_float(bits16 << 16); }
 
 struct DevOps {
-  uint8_t* sm;   // 1024-B aligned base of the data buffer (generic pointer)
+  uint8_t* sm;   // base of the data buffer the epilogue / conversion writes (generic pointer)
+  bool acc16;
   __device__ __forceinline__ void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
     mma_f16_ss(d, a, b, idesc, acc);
   }
@@ -46,23 +51,17 @@ struct DevOps {
   }
   __device__ __forceinline__ float lo16f(uint32_t w) { return __half2float(__ushort_as_half((unsigned short)(w & 0xFFFFu))); }
   __device__ __forceinline__ float hi16f(uint32_t w) { return __half2float(__ushort_as_half((unsigned short)(w >> 16))); }
-  template <bool ACC16>
-  __device__ __forceinline__ float acc_val_t(uint32_t w) {
-    if constexpr (ACC16) return lo16f(w);
-    else return __uint_as_float(w);
-  }
-  bool acc16;
   __device__ __forceinline__ float acc_val(uint32_t w) { return acc16 ? lo16f(w) : __uint_as_float(w); }
   __device__ __forceinline__ void ldK(const float* p, float (&k)[4]) {
     const float4 v = __ldg(reinterpret_cast<const float4*>(p));
     k[0] = v.x; k[1] = v.y; k[2] = v.z; k[3] = v.w;
   }
-  __device__ __forceinline__ void load8(const float* p, float* v) {
-    const float4 a = __ldg(reinterpret_cast<const float4*>(p)), b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+  __device__ __forceinline__ void lds8(const float* p, float* v) {
+    const float4 a = reinterpret_cast<const float4*>(p)[0], b = reinterpret_cast<const float4*>(p)[1];
     v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
   }
-  __device__ __forceinline__ void load8(const __nv_bfloat16* p, float* v) {
-    const uint4 q = __ldg(reinterpret_cast<const uint4*>(p));
+  __device__ __forceinline__ void lds8(const __nv_bfloat16* p, float* v) {
+    const uint4 q = *reinterpret_cast<const uint4*>(p);
     const uint32_t w[4] = {q.x, q.y, q.z, q.w};
     for (int e = 0; e < 4; e++) { v[2 * e] = bf16_bits_to_float(w[e] & 0xFFFFu); v[2 * e + 1] = bf16_bits_to_float(w[e] >> 16); }
   }
@@ -77,10 +76,7 @@ struct BmatEmitDev {
     sincospif(2.0f * (float)q / (float)R, &s, &c);
     const float v = which == 0 ? c : (which == 1 ? -s : s);
     __half h = __float2half_rn(v);
-    if (set == 1) {
-      // low part of the fp16 hi+lo split (the residual of the fp32 value)
-      h = __float2half_rn(v - __half2float(h));
-    }
+    if (set == 1) h = __float2half_rn(v - __half2float(h));   // low part of the fp16 hi+lo split
     *reinterpret_cast<__half*>(base + off) = h;
   }
 };
@@ -92,73 +88,255 @@ struct ConvParams {
   void* y;
   int* status;
   int B, H;
+  int ngroups;           // ceil(pairs / G), pairs = ceil(B/2) * H
 };
 
+// ---- extra PTX used only by the persistent kernel ----
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// Bounded wait that also gives up when another role has aborted.
+__device__ __forceinline__ bool wait_phase(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (global_ns() - t0 > kWaitLimitNs) { *abort_flag = 1; return false; }
+  }
+}
+
+template <class P, bool ACC16, int SID>
+__device__ __forceinline__ void issue_sid(DevOps& ops, uint32_t tmem, uint32_t data_s, uint32_t bmat_s) {
+  issue_stage<P, ACC16, SID>(ops, tmem, data_s, bmat_s);
+}
+
+template <class P, bool ACC16>
+__device__ void issue_any(int sid, DevOps& ops, uint32_t tmem, uint32_t data_s, uint32_t bmat_s) {
+  switch (sid) {
+    case 0: issue_sid<P, ACC16, 0>(ops, tmem, data_s, bmat_s); break;
+    case 1: issue_sid<P, ACC16, 1>(ops, tmem, data_s, bmat_s); break;
+    case 2: issue_sid<P, ACC16, 2>(ops, tmem, data_s, bmat_s); break;
+    case 3: issue_sid<P, ACC16, 3>(ops, tmem, data_s, bmat_s); break;
+    default:
+      if constexpr (P::S == 3) {
+        if (sid == 4) issue_sid<P, ACC16, 4>(ops, tmem, data_s, bmat_s);
+        else issue_sid<P, ACC16, 5>(ops, tmem, data_s, bmat_s);
+      }
+  }
+}
+
 template <class P, class TIO, bool ACC16, int SID>
-__device__ __forceinline__ bool run_stages(DevOps& ops, const EpiArgs& ea, uint32_t tmem, uint32_t data_s,
-                                           uint32_t bmat_s, uint64_t* bar, int* status) {
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  if (tid == 0) {
-    tc_fence_after();
-    issue_stage<P, ACC16, SID>(ops, tmem, data_s, bmat_s);
-    mma_commit(bar);
-  }
-  bool ok = mbar_wait_bounded(bar, (uint32_t)(SID & 1), kWaitLimitNs);
-  ok = __syncthreads_and(ok) != 0;
-  if (!ok) {
-    if (tid == 0) atomicExch(status, SFFFT_ERR_TIMEOUT);
-    return false;
-  }
-  tc_fence_after();
-  {
-    constexpr int T = P::tiles(SID);
-    const int q = warp & 3;
-    for (int t = warp >> 2; t < T; t += P::W / 4) epilogue_row<P, TIO, ACC16, SID>(ops, ea, t, q, lane);
-  }
-  fence_async_smem();
-  tc_fence_before();
-  __syncthreads();
-  if constexpr (SID + 1 < 2 * P::S) return run_stages<P, TIO, ACC16, SID + 1>(ops, ea, tmem, data_s, bmat_s, bar, status);
-  return true;
+__device__ __forceinline__ void epi_sid(DevOps& ops, const EpiArgs& ea, int q, int wi, int nwq, int lane) {
+  constexpr int C = epi_chunks<P, SID>(), U = P::tiles(SID) * C;
+  for (int u = wi; u < U; u += nwq) epilogue_unit<P, TIO, ACC16, SID>(ops, ea, u / C, u - (u / C) * C, q, lane);
 }
 
 template <class P, class TIO, bool ACC16>
-__global__ void __launch_bounds__(P::NT, 1) fused_conv_kernel(ConvParams prm) {
+__device__ void epi_any(int sid, DevOps& ops, const EpiArgs& ea, int q, int wi, int nwq, int lane) {
+  switch (sid) {
+    case 0: epi_sid<P, TIO, ACC16, 0>(ops, ea, q, wi, nwq, lane); break;
+    case 1: epi_sid<P, TIO, ACC16, 1>(ops, ea, q, wi, nwq, lane); break;
+    case 2: epi_sid<P, TIO, ACC16, 2>(ops, ea, q, wi, nwq, lane); break;
+    case 3: epi_sid<P, TIO, ACC16, 3>(ops, ea, q, wi, nwq, lane); break;
+    default:
+      if constexpr (P::S == 3) {
+        if (sid == 4) epi_sid<P, TIO, ACC16, 4>(ops, ea, q, wi, nwq, lane);
+        else epi_sid<P, TIO, ACC16, 5>(ops, ea, q, wi, nwq, lane);
+      }
+  }
+}
+
+template <class P, class TIO, bool ACC16>
+__global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kernel(ConvParams prm) {
+  using SH = Shape<P, sizeof(TIO)>;
+  constexpr int S2 = 2 * P::S, TPG = SH::TPG, NSLOT = SH::NSLOT, NCH = SH::NCH;
+  constexpr int CE = SH::CHUNK / (int)sizeof(TIO);               // elements per chunk
+  constexpr int SEQB = P::L * (int)sizeof(TIO);                   // bytes per sequence
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* bmat = sm + P::DATA_BYTES;
-  uint64_t* bar = reinterpret_cast<uint64_t*>(bmat + P::BMAT_BYTES);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 1);
-  const int tid = threadIdx.x, warp = tid >> 5;
+  uint8_t* bmat = sm;
+  uint8_t* stage = sm + SH::STAGE_OFF;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + SH::BAR_OFF);
+  uint64_t* full = bars;                  // [NCH]  staged chunk landed
+  uint64_t* empty = bars + NCH;           // [NCH]  staged chunk consumed
+  uint64_t* a_ready = bars + 2 * NCH;     // [2]    compute warps wrote a stage operand
+  uint64_t* mma_done = bars + 2 * NCH + 2;// [2]    a stage's MMAs completed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * NCH + 4);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 2 * NCH + 5);
 
-  if (warp == 0) { tmem_alloc(tmem_slot, P::TMEM_COLS); tmem_relinquish(); }
-  if (tid == 32) { mbar_init(bar, 1); fence_mbar_init(); }
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int ni = (int)blockIdx.x < prm.ngroups ? (prm.ngroups - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x : 0;
 
+  if (warp == 1) { tmem_alloc(tmem_slot, SH::TMEM_ALLOC); tmem_relinquish(); }
+  if (tid == 0) {
+    for (int i = 0; i < NCH; i++) { mbar_init(full + i, 1); mbar_init(empty + i, SH::WC * 32); }
+    for (int l = 0; l < 2; l++) { mbar_init(a_ready + l, SH::WC * 32); mbar_init(mma_done + l, 1); }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
   if (prm.btab) {
     const uint4* src = prm.btab;
     uint4* dst = reinterpret_cast<uint4*>(bmat);
-    for (int i = tid; i < P::BMAT_BYTES / 16; i += P::NT) dst[i] = __ldg(src + i);
+    for (int i = tid; i < P::BMAT_BYTES / 16; i += SH::NT) dst[i] = __ldg(src + i);
   } else {
     BmatEmitDev emit{bmat};
-    for_each_bmat_entry<P>(emit, tid, P::NT);
+    for_each_bmat_entry<P>(emit, tid, SH::NT);
   }
-
-  DevOps ops{sm, ACC16};
-  load_input<P, TIO>(ops, reinterpret_cast<const TIO*>(prm.u), blockIdx.x, prm.B, prm.H, tid);
-
   fence_async_smem();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  const TIO* u = reinterpret_cast<const TIO*>(prm.u);
 
-  EpiArgs ea{tmem, prm.Kf, prm.y, prm.B, prm.H, (int)blockIdx.x};
-  run_stages<P, TIO, ACC16, 0>(ops, ea, tmem, smem_u32(sm), smem_u32(bmat), bar, prm.status);
+  if (warp == 0) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      long long cc = 0;
+      for (int gi = 0; gi < ni && !*abort_flag; gi++) {
+        const int group = (int)blockIdx.x + gi * (int)gridDim.x;
+        {
+          const PairInfo a = pair_info(group, 0, P::G, prm.B, prm.H, P::L);
+          const PairInfo b = pair_info(group, P::G - 1, P::G, prm.B, prm.H, P::L);
+          if (a.h >= 0) prefetch_l2(prm.Kf + 2ll * a.h * P::N, P::N * 8);
+          if (b.h >= 0 && b.h != a.h) prefetch_l2(prm.Kf + 2ll * b.h * P::N, P::N * 8);
+        }
+        for (int c = 0; c < SH::CPG; c++, cc++) {
+          const int slot = (int)(cc % NCH);
+          const long long use = cc / NCH;
+          if (use > 0 && !wait_phase(empty + slot, (uint32_t)((use - 1) & 1), abort_flag)) break;
+          uint8_t* dst = stage + slot * SH::CHUNK;
+          // stream bytes [c*CHUNK, (c+1)*CHUNK) of the group's 2G sequences
+          const long long b0 = (long long)c * SH::CHUNK;
+          uint32_t total = 0;
+          if (SEQB >= SH::CHUNK) {
+            const int j = (int)(b0 / SEQB);
+            const PairInfo pi = pair_info(group, j >> 1, P::G, prm.B, prm.H, P::L);
+            if (((j & 1) ? pi.off1 : pi.off0) >= 0) total = SH::CHUNK;
+          } else {
+            const int j0 = (int)(b0 / SEQB);
+            for (int jj = 0; jj < SH::CHUNK / SEQB; jj++) {
+              const PairInfo pi = pair_info(group, (j0 + jj) >> 1, P::G, prm.B, prm.H, P::L);
+              if ((((j0 + jj) & 1) ? pi.off1 : pi.off0) >= 0) total += SEQB;
+            }
+          }
+          mbar_arrive_expect_tx(full + slot, total);
+          if (SEQB >= SH::CHUNK) {
+            const int j = (int)(b0 / SEQB);
+            const PairInfo pi = pair_info(group, j >> 1, P::G, prm.B, prm.H, P::L);
+            const long long off = (j & 1) ? pi.off1 : pi.off0;
+            if (off >= 0) bulk_g2s(dst, u + off + (b0 - (long long)j * SEQB) / (int)sizeof(TIO), SH::CHUNK, full + slot);
+          } else {
+            const int j0 = (int)(b0 / SEQB);
+            for (int jj = 0; jj < SH::CHUNK / SEQB; jj++) {
+              const PairInfo pi = pair_info(group, (j0 + jj) >> 1, P::G, prm.B, prm.H, P::L);
+              const long long off = ((j0 + jj) & 1) ? pi.off1 : pi.off0;
+              if (off >= 0) bulk_g2s(dst + jj * SEQB, u + off, SEQB, full + slot);
+            }
+          }
+        }
+      }
+      // drain: every issued copy has landed before the CTA can exit
+      const long long first = cc > NCH ? cc - NCH : 0;
+      for (long long d = first; d < cc; d++) {
+        const int slot = (int)(d % NCH);
+        const uint64_t t0 = global_ns();
+        while (!mbar_try_wait(full + slot, (uint32_t)((d / NCH) & 1)) && global_ns() - t0 < kWaitLimitNs) {
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      DevOps ops{sm, ACC16};
+      uint32_t ar_phase[2] = {0, 0};
+      int issued[2] = {0, 0};
+      const int rounds = (ni + NSLOT - 1) / NSLOT;
+      for (int k = 0; k < rounds * TPG && !*abort_flag; k++) {
+        const int j = k % TPG;
+        if (j == TPG - 1) continue;   // after the last epilogue there is no MMA
+        for (int l = 0; l < NSLOT; l++) {
+          const int gi = NSLOT * (k / TPG) + l;
+          if (gi >= ni) continue;
+          if (!wait_phase(a_ready + l, ar_phase[l], abort_flag)) break;
+          ar_phase[l] ^= 1;
+          tc_fence_after();
+          issue_any<P, ACC16>(j, ops, tmem + (uint32_t)(l * P::TMEM_COLS),
+                              smem_u32(sm + SH::DATA_OFF + l * P::DATA_BYTES), smem_u32(bmat));
+          mma_commit(mma_done + l);
+          issued[l]++;
+        }
+      }
+      // make sure no MMA is still writing TMEM when the CTA frees it
+      for (int l = 0; l < NSLOT; l++) {
+        if (!issued[l]) continue;
+        const uint64_t t0 = global_ns();
+        while (!mbar_try_wait(mma_done + l, (uint32_t)((issued[l] - 1) & 1)) && global_ns() - t0 < kWaitLimitNs) {
+        }
+      }
+    }
+  } else {
+    // ---------------- compute warps ----------------
+    const int wc = warp - 2, q = warp & 3, wi = wc >> 2, nwq = SH::WC / 4, ctid = tid - 64;
+    uint32_t md_phase[2] = {0, 0};
+    const int rounds = (ni + NSLOT - 1) / NSLOT;
+    bool ok = true;
+    for (int k = 0; k < rounds * TPG && ok; k++) {
+      const int j = k % TPG;
+      for (int l = 0; l < NSLOT && ok; l++) {
+        const int gi = NSLOT * (k / TPG) + l;
+        if (gi >= ni) continue;
+        const int group = (int)blockIdx.x + gi * (int)gridDim.x;
+        DevOps ops{sm + SH::DATA_OFF + l * P::DATA_BYTES, ACC16};
+        if (j == 0) {
+          for (int c = 0; c < SH::CPG; c++) {
+            const long long cc = (long long)gi * SH::CPG + c;
+            const int slot = (int)(cc % NCH);
+            if (!wait_phase(full + slot, (uint32_t)((cc / NCH) & 1), abort_flag)) { ok = false; break; }
+            convert_chunk<P, TIO>(ops, reinterpret_cast<const TIO*>(stage + slot * SH::CHUNK), (long long)c * CE, CE, group,
+                                  prm.B, prm.H, ctid, SH::WC * 32);
+            mbar_arrive(empty + slot);
+          }
+          if (!ok) break;
+          fence_async_smem();
+          tc_fence_before();
+          mbar_arrive(a_ready + l);
+        } else {
+          const int sid = j - 1;
+          if (!wait_phase(mma_done + l, md_phase[l], abort_flag)) { ok = false; break; }
+          md_phase[l] ^= 1;
+          tc_fence_after();
+          EpiArgs ea{tmem + (uint32_t)(l * P::TMEM_COLS), prm.Kf, prm.y, prm.B, prm.H, group};
+          epi_any<P, TIO, ACC16>(sid, ops, ea, q, wi, nwq, lane);
+          tc_fence_before();
+          if (sid < S2 - 1) {
+            fence_async_smem();
+            mbar_arrive(a_ready + l);
+          }
+        }
+      }
+    }
+  }
 
+  if (tid == 0 && *abort_flag) atomicExch(prm.status, SFFFT_ERR_TIMEOUT);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 0) tmem_dealloc(tmem, P::TMEM_COLS);
+  if (warp == 1) tmem_dealloc(tmem, SH::TMEM_ALLOC);
 }
 
 }  // namespace sffft

@@ -11,7 +11,7 @@ namespace sffft {
 
 template <class P, class TIO, bool ACC16>
 cudaError_t launch_conv(const ConvParams& prm, int grid, int smem_bytes, cudaStream_t st) {
-  fused_conv_kernel<P, TIO, ACC16><<<grid, P::NT, smem_bytes, st>>>(prm);
+  fused_conv_kernel<P, TIO, ACC16><<<grid, Shape<P, sizeof(TIO)>::NT, smem_bytes, st>>>(prm);
   return cudaGetLastError();
 }
 
@@ -20,7 +20,13 @@ ConvEntry make_entry(const char* name) {
   ConvEntry e;
   e.name = name;
   e.R0 = P::R0; e.R1 = P::R1; e.R2 = P::R2; e.G = P::G; e.W = P::W; e.N = P::N; e.L = P::L;
-  e.threads = P::NT; e.smem_bytes = P::SMEM_BYTES; e.bmat_bytes = P::BMAT_BYTES; e.tmem_cols = P::TMEM_COLS;
+  using S4 = Shape<P, 4>;
+  using S2 = Shape<P, 2>;
+  e.threads = S4::NT; e.bmat_bytes = P::BMAT_BYTES;
+  e.smem_bytes[0] = S4::SMEM; e.smem_bytes[1] = S2::SMEM;
+  e.tmem_cols[0] = S4::TMEM_ALLOC; e.tmem_cols[1] = S2::TMEM_ALLOC;
+  e.slots[0] = S4::NSLOT; e.slots[1] = S2::NSLOT;
+  e.stage_chunks[0] = S4::NCH; e.stage_chunks[1] = S2::NCH;
   e.launch[0][0] = &launch_conv<P, float, false>;
   e.launch[0][1] = &launch_conv<P, float, true>;
   e.launch[1][0] = &launch_conv<P, __nv_bfloat16, false>;

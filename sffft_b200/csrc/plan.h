@@ -124,6 +124,33 @@ struct Plan {
   static_assert(W == 4 || W == 8, "4 or 8 warps");
 };
 
+// Resources of the persistent kernel for plan P and I/O element size SIO:
+//   1 producer warp (bulk copies of u into a staging ring), 1 MMA warp, WC = 2W compute warps;
+//   NSLOT groups in flight (each with a data buffer and a TMEM accumulator region), 2 when both fit;
+//   an input staging ring of NCH chunks of CHUNK bytes (up to two groups ahead).
+template <class P, int SIO>
+struct Shape {
+  static constexpr int WC = 2 * P::W;
+  static constexpr int NT = 32 * (WC + 2);
+  static constexpr int GIN = 2 * P::G * P::L * SIO;                 // input bytes per group
+  static constexpr int CHUNK = GIN < 8192 ? GIN : 8192;
+  static constexpr int CPG = GIN / CHUNK;                           // chunks per group
+  static constexpr int CAP = 227 * 1024 - 1024 - 512;               // dynamic smem minus align slack, barriers
+  static constexpr bool TWO = 2 * P::TMEM_COLS <= 512 && P::BMAT_BYTES + 2 * P::DATA_BYTES + 2 * CHUNK <= CAP;
+  static constexpr int NSLOT = TWO ? 2 : 1;
+  static constexpr int DATA_OFF = P::BMAT_BYTES;
+  static constexpr int STAGE_OFF = DATA_OFF + NSLOT * P::DATA_BYTES;
+  static constexpr int STAGE_MAX = ((CAP - STAGE_OFF) / CHUNK) * CHUNK;
+  static constexpr int STAGE = 2 * GIN < STAGE_MAX ? 2 * GIN : STAGE_MAX;
+  static constexpr int NCH = STAGE / CHUNK;
+  static constexpr int BAR_OFF = STAGE_OFF + STAGE;
+  static constexpr int SMEM = BAR_OFF + 512 + 1024;
+  static constexpr int TMEM_ALLOC = NSLOT * P::TMEM_COLS;
+  static constexpr int TPG = 2 * P::S + 1;                          // tasks per group: convert + 2S epilogues
+  static_assert(NCH >= 2, "staging ring needs two chunks");
+  static_assert(2 * NCH + 8 <= 64, "barrier area");
+};
+
 // Row pitch of the K-major A operand of the inverse last-digit stage (re | im halves of a row).
 SF_HD constexpr int kmaj_data_pitch(int R) { return 4 * R > 128 ? 128 : 4 * R; }
 

@@ -7,6 +7,8 @@
 //   ops.pack2(lo, hi)                                        two floats -> f16x2 (round to nearest)
 //   ops.acc_val(raw)                                         TMEM word -> float (fp32 or fp16 accumulator)
 //   ops.ldK(p)                                               four floats (two complex) of the spectrum
+//   ops.lds8(p, v)                                           eight staged input values (TIO) -> float
+//   ops.store1(p, v)                                         one output value (TIO)
 //
 // Algorithm per pair (reference: sfFFT src/sffft.cu:137-280, restated for tcgen05 and pairing):
 //   forward digits 0..S-1, each: DFT_R along the digit, x 1/sqrt(R), then the four-step twiddle
@@ -37,28 +39,31 @@ SF_HD PairInfo pair_info(int cta, int g, int G, int B, int H, int L) {
 }
 
 // ---------------------------------------------------------------------------------------------
-// Input: u (two real sequences per pair) -> first-stage A operand, fp16 hi + lo split.
+// Input conversion: raw u (two real sequences per pair) -> first-stage A operand, fp16 hi + lo split.
 //   element (row m = g*V0 + v, K-row plane*R0 + n0 [hi] / plane*R0 + R0/2 + n0 [lo]), n = n0*V0 + v.
+// A group's input is the stream of its 2G sequences (sequence j = 2*g + plane, element n at j*L + n);
+// convert_chunk handles the stream elements [e0, e0 + ne) staged at `chunk` (raw TIO values).
 // ---------------------------------------------------------------------------------------------
 template <class P, class TIO, class Ops>
-SF_HD void load_input(Ops& ops, const TIO* u, int cta, int B, int H, int tid) {
-  constexpr int V0 = P::N / P::R0, CH = P::L / 8, MB0 = P::MB(0);
-  for (int idx = tid; idx < P::G * 2 * CH; idx += P::NT) {
-    const int g = idx / (2 * CH), rem = idx - g * 2 * CH, plane = rem / CH, c = rem - plane * CH;
-    const PairInfo pi = pair_info(cta, g, P::G, B, H, P::L);
-    const long long off = plane == 0 ? pi.off0 : pi.off1;
+SF_HD void convert_chunk(Ops& ops, const TIO* chunk, long long e0, int ne, int group, int B, int H, int tid,
+                         int nthreads) {
+  constexpr int V0 = P::N / P::R0, MB0 = P::MB(0);
+  for (int i = tid * 8; i < ne; i += nthreads * 8) {
+    const long long e = e0 + i;
+    const int j = (int)(e / P::L), n = (int)(e - (long long)j * P::L), g = j >> 1, plane = j & 1;
+    const PairInfo pi = pair_info(group, g, P::G, B, H, P::L);
+    const bool present = (plane == 0 ? pi.off0 : pi.off1) >= 0;
     float v[8];
-    if (off >= 0) ops.load8(u + off + c * 8, v);
+    if (present) ops.lds8(chunk + i, v);
     else {
-      for (int e = 0; e < 8; e++) v[e] = 0.f;
+      for (int q = 0; q < 8; q++) v[q] = 0.f;
     }
     uint32_t hi[4], lo[4];
-    for (int e = 0; e < 4; e++) {
-      hi[e] = ops.pack2(v[2 * e], v[2 * e + 1]);
-      lo[e] = ops.pack2(v[2 * e] - ops.lo16f(hi[e]), v[2 * e + 1] - ops.hi16f(hi[e]));
+    for (int q = 0; q < 4; q++) {
+      hi[q] = ops.pack2(v[2 * q], v[2 * q + 1]);
+      lo[q] = ops.pack2(v[2 * q] - ops.lo16f(hi[q]), v[2 * q + 1] - ops.hi16f(hi[q]));
     }
-    const int n = c * 8, n0 = n / V0, vv = n - n0 * V0, m = g * V0 + vv;
-    const int k = plane * P::R0 + n0;
+    const int n0 = n / V0, vv = n - n0 * V0, m = g * V0 + vv, k = plane * P::R0 + n0;
     ops.st16(mn_off(m, k, MB0), hi[0], hi[1], hi[2], hi[3]);
     ops.st16(mn_off(m, k + P::R0 / 2, MB0), lo[0], lo[1], lo[2], lo[3]);
   }
@@ -118,24 +123,33 @@ SF_HD float tw_arg(int e) {
 // Epilogue for stage SID: one thread per TMEM lane (row r = t*128 + q*32 + lane of tile t).
 // ---------------------------------------------------------------------------------------------
 struct EpiArgs {
-  uint32_t tmem;
+  uint32_t tmem;        // TMEM base of the group's accumulator slot
   const float* Kf;      // [H][N] complex fp32, digit order
   void* y;              // output base (TIO*)
-  int B, H, cta;
+  int B, H, cta;        // cta: the group index (pairs cta*G .. cta*G + G - 1)
 };
 
+// Number of 16-column chunks an epilogue thread reads per row in stage SID (the last inverse stage only
+// needs time rows n0 < R0/2).
+template <class P, int SID>
+SF_HD constexpr int epi_chunks() {
+  return SID == 2 * P::S - 1 ? (P::R0 / 2 < 16 ? 1 : P::R0 / 32) : P::rad(SID) / 16;
+}
+
+// One epilogue unit: TMEM lane row r = t*128 + q*32 + lane of tile t, columns [16c, 16c + 16) of both
+// the real and the imaginary half.  ea.tmem is the TMEM base of the group's accumulator slot.
 template <class P, class TIO, bool ACC16, int SID, class Ops>
-SF_HD void epilogue_row(Ops& ops, const EpiArgs& ea, int t, int q, int lane) {
+SF_HD void epilogue_unit(Ops& ops, const EpiArgs& ea, int t, int c, int q, int lane) {
   constexpr int S = P::S, R = P::rad(SID), N = P::N, RPP = N / R;   // rows per pair
   constexpr bool OUT = (SID == 2 * S - 1), SPEC = (SID == S - 1);
-  constexpr int NOUT = OUT ? (P::R0 / 2 < 16 ? 16 : P::R0 / 2) : R;  // columns to read
   constexpr float SC = (R == 16) ? 0.25f : (R == 64 ? 0.125f : 0.17677669529663687f);
-  const int r = t * 128 + q * 32 + lane, g = r / RPP, rr = r - g * RPP;
-  const uint32_t taddr = ea.tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(t * 2 * R);
+  const int r = t * 128 + q * 32 + lane, g = r / RPP, rr = r - g * RPP, c0 = 16 * c;
+  const uint32_t taddr = ea.tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(t * 2 * R + c0);
 
-  // thread-specific twiddle exponent e(c) = ta*c + tb, next-stage write target (m0, kre)
+  // thread-specific twiddle exponent e(col) = ta*col + tb and next-stage write target (m0, kre)
   int ta = 0, tb = 0, m0 = 0, kre = 0;
-  long long yo0 = -1, yo1 = -1; int vv = 0;
+  long long yo0 = -1, yo1 = -1;
+  int vv = 0;
   const float* Kp = nullptr;
   if constexpr (SID == 0) {
     if constexpr (S == 2) { ta = rr; m0 = g * P::R0; kre = rr; }
@@ -145,7 +159,7 @@ SF_HD void epilogue_row(Ops& ops, const EpiArgs& ea, int t, int q, int lane) {
     ta = P::R0 * n2; m0 = g * P::R0 * P::R1 + k0 * P::R1; kre = n2;
   } else if constexpr (SPEC) {
     const PairInfo pi = pair_info(ea.cta, g, P::G, ea.B, ea.H, P::L);
-    Kp = ea.Kf + 2 * ((long long)(pi.h < 0 ? 0 : pi.h) * N + (long long)rr * R);
+    Kp = ea.Kf + 2 * ((long long)(pi.h < 0 ? 0 : pi.h) * N + (long long)rr * R + c0);
   } else if constexpr (SID == S) {
     if constexpr (S == 2) { ta = -rr; m0 = g * P::R1; kre = rr; }
     else { const int k0 = rr / P::R1, k1 = rr - k0 * P::R1; ta = -P::R0 * k1; m0 = g * P::R0 * P::R2 + k0 * P::R2; kre = k1; }
@@ -159,68 +173,71 @@ SF_HD void epilogue_row(Ops& ops, const EpiArgs& ea, int t, int q, int lane) {
     yo0 = pi.off0; yo1 = pi.off1;
   }
 
-  float t_re = SC, t_im = 0.f, w_re = 1.f, w_im = 0.f;
+  // spectrum values are fetched before the accumulator so their latency overlaps the TMEM read
+  float kk[32];
+  if constexpr (SPEC) {
+    for (int j = 0; j < 16; j += 2) {
+      float k4[4];
+      ops.ldK(Kp + 2 * j, k4);
+      kk[2 * j] = k4[0]; kk[2 * j + 1] = k4[1]; kk[2 * j + 2] = k4[2]; kk[2 * j + 3] = k4[3];
+    }
+  }
+  uint32_t raw_re[16], raw_im[16];
+  ops.tmem_ld16(taddr, raw_re);
+  ops.tmem_ld16(taddr + (uint32_t)R, raw_im);
+  ops.tmem_wait();
+
+  float o_re[16], o_im[16];
   constexpr bool TW = !SPEC && !OUT;
   if constexpr (TW) {
-    float s, c;
-    ops.sincospi(tw_arg<N>(ta), &s, &c); w_re = c; w_im = s;
-    if (tb != 0) { ops.sincospi(tw_arg<N>(tb), &s, &c); t_re = SC * c; t_im = SC * s; }
+    float s, cs, w_re, w_im;
+    ops.sincospi(tw_arg<N>(ta), &s, &cs);
+    w_re = cs; w_im = s;
+    ops.sincospi(tw_arg<N>(ta * c0 + tb), &s, &cs);
+    float t_re = SC * cs, t_im = SC * s;
+    for (int j = 0; j < 16; j++) {
+      const float a = ops.acc_val(raw_re[j]), b = ops.acc_val(raw_im[j]);
+      o_re[j] = a * t_re - b * t_im;
+      o_im[j] = a * t_im + b * t_re;
+      const float nr = t_re * w_re - t_im * w_im;
+      t_im = t_re * w_im + t_im * w_re;
+      t_re = nr;
+    }
+  } else if constexpr (SPEC) {
+    for (int j = 0; j < 16; j++) {
+      const float a = ops.acc_val(raw_re[j]) * SC, b = ops.acc_val(raw_im[j]) * SC;
+      o_re[j] = a * kk[2 * j] - b * kk[2 * j + 1];
+      o_im[j] = a * kk[2 * j + 1] + b * kk[2 * j];
+    }
+  } else {
+    for (int j = 0; j < 16; j++) { o_re[j] = ops.acc_val(raw_re[j]) * SC; o_im[j] = ops.acc_val(raw_im[j]) * SC; }
   }
 
-  for (int c0 = 0; c0 < NOUT; c0 += 16) {
-    uint32_t raw_re[16], raw_im[16];
-    ops.tmem_ld16(taddr + (uint32_t)c0, raw_re);
-    ops.tmem_ld16(taddr + (uint32_t)(R + c0), raw_im);
-    ops.tmem_wait();
-    float o_re[16], o_im[16];
-    if constexpr (TW) {
-      for (int j = 0; j < 16; j++) {
-        const float a = ops.acc_val(raw_re[j]), b = ops.acc_val(raw_im[j]);
-        o_re[j] = a * t_re - b * t_im;
-        o_im[j] = a * t_im + b * t_re;
-        const float nr = t_re * w_re - t_im * w_im;
-        t_im = t_re * w_im + t_im * w_re; t_re = nr;
+  if constexpr (OUT) {
+    TIO* y = (TIO*)ea.y;
+    constexpr int V0 = N / P::R0;
+    for (int j = 0; j < 16; j++) {
+      const int n0 = c0 + j;
+      if (n0 < P::R0 / 2) {
+        if (yo0 >= 0) ops.store1(y + yo0 + (long long)n0 * V0 + vv, o_re[j]);
+        if (yo1 >= 0) ops.store1(y + yo1 + (long long)n0 * V0 + vv, o_im[j]);
       }
-    } else if constexpr (SPEC) {
-      for (int j = 0; j < 16; j += 2) {
-        float kk[4];
-        ops.ldK(Kp + 2 * (c0 + j), kk);
-        for (int e = 0; e < 2; e++) {
-          const float a = ops.acc_val(raw_re[j + e]) * SC, b = ops.acc_val(raw_im[j + e]) * SC;
-          o_re[j + e] = a * kk[2 * e] - b * kk[2 * e + 1];
-          o_im[j + e] = a * kk[2 * e + 1] + b * kk[2 * e];
-        }
-      }
-    } else {
-      for (int j = 0; j < 16; j++) { o_re[j] = ops.acc_val(raw_re[j]) * SC; o_im[j] = ops.acc_val(raw_im[j]) * SC; }
     }
-
-    if constexpr (OUT) {
-      TIO* y = (TIO*)ea.y;
-      constexpr int V0 = N / P::R0;
-      for (int j = 0; j < 16; j++) {
-        const int n0 = c0 + j;
-        if (n0 < P::R0 / 2) {
-          if (yo0 >= 0) ops.store1(y + yo0 + (long long)n0 * V0 + vv, o_re[j]);
-          if (yo1 >= 0) ops.store1(y + yo1 + (long long)n0 * V0 + vv, o_im[j]);
-        }
-      }
+  } else {
+    uint32_t pr[8], pim[8];
+    for (int e = 0; e < 8; e++) { pr[e] = ops.pack2(o_re[2 * e], o_re[2 * e + 1]); pim[e] = ops.pack2(o_im[2 * e], o_im[2 * e + 1]); }
+    if constexpr (SPEC) {
+      constexpr int RWS = P::rows(SID + 1);
+      ops.st16(kmaj_data_off(r, c0, R, RWS), pr[0], pr[1], pr[2], pr[3]);
+      ops.st16(kmaj_data_off(r, c0 + 8, R, RWS), pr[4], pr[5], pr[6], pr[7]);
+      ops.st16(kmaj_data_off(r, R + c0, R, RWS), pim[0], pim[1], pim[2], pim[3]);
+      ops.st16(kmaj_data_off(r, R + c0 + 8, R, RWS), pim[4], pim[5], pim[6], pim[7]);
     } else {
-      uint32_t pr[8], pim[8];
-      for (int e = 0; e < 8; e++) { pr[e] = ops.pack2(o_re[2 * e], o_re[2 * e + 1]); pim[e] = ops.pack2(o_im[2 * e], o_im[2 * e + 1]); }
-      if constexpr (SPEC) {
-        constexpr int RWS = P::rows(SID + 1);
-        ops.st16(kmaj_data_off(r, c0, R, RWS), pr[0], pr[1], pr[2], pr[3]);
-        ops.st16(kmaj_data_off(r, c0 + 8, R, RWS), pr[4], pr[5], pr[6], pr[7]);
-        ops.st16(kmaj_data_off(r, R + c0, R, RWS), pim[0], pim[1], pim[2], pim[3]);
-        ops.st16(kmaj_data_off(r, R + c0 + 8, R, RWS), pim[4], pim[5], pim[6], pim[7]);
-      } else {
-        constexpr int MBn = P::MB(SID + 1), Rn = P::rad(SID + 1);
-        ops.st16(mn_off(m0 + c0, kre, MBn), pr[0], pr[1], pr[2], pr[3]);
-        ops.st16(mn_off(m0 + c0 + 8, kre, MBn), pr[4], pr[5], pr[6], pr[7]);
-        ops.st16(mn_off(m0 + c0, Rn + kre, MBn), pim[0], pim[1], pim[2], pim[3]);
-        ops.st16(mn_off(m0 + c0 + 8, Rn + kre, MBn), pim[4], pim[5], pim[6], pim[7]);
-      }
+      constexpr int MBn = P::MB(SID + 1), Rn = P::rad(SID + 1);
+      ops.st16(mn_off(m0 + c0, kre, MBn), pr[0], pr[1], pr[2], pr[3]);
+      ops.st16(mn_off(m0 + c0 + 8, kre, MBn), pr[4], pr[5], pr[6], pr[7]);
+      ops.st16(mn_off(m0 + c0, Rn + kre, MBn), pim[0], pim[1], pim[2], pim[3]);
+      ops.st16(mn_off(m0 + c0 + 8, Rn + kre, MBn), pim[4], pim[5], pim[6], pim[7]);
     }
   }
 }
