@@ -36,6 +36,10 @@ struct sffft_baseline {
 };
 
 static thread_local int g_last_cuda = 0;
+#ifdef SFFFT_TRACE
+static unsigned long long* g_trace = nullptr;
+extern "C" void sffft_debug_set_trace(void* buf) { g_trace = (unsigned long long*)buf; }
+#endif
 static int cuda_fail(cudaError_t e) {
   g_last_cuda = (int)e;
   return SFFFT_ERR_CUDA;
@@ -227,6 +231,9 @@ int sffft_conv(sffft_plan_t p, const void* u, const void* Kf, void* y, int B, in
   ConvParams prm;
   prm.u = u; prm.Kf = (const float*)Kf; prm.btab = p->btab; prm.y = y; prm.status = p->status; prm.B = B; prm.H = H;
   prm.ngroups = (int)groups;
+#ifdef SFFFT_TRACE
+  prm.trace = g_trace;
+#endif
   const cudaError_t ce = e->launch[p->io][p->acc](prm, grid, p->smem_launch, (cudaStream_t)stream);
   return ce == cudaSuccess ? SFFFT_OK : cuda_fail(ce);
 }

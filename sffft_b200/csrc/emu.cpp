@@ -114,10 +114,45 @@ struct HostOps {
   }
   void store1(float* p, float v) { *p = v; }
   void store1(uint16_t* p, float v) { *p = (uint16_t)bf16_from_float(v); }
+  void store4(float* p, const float* v) { for (int i = 0; i < 4; i++) p[i] = v[i]; }
+  void store4(uint16_t* p, const float* v) { for (int i = 0; i < 4; i++) p[i] = (uint16_t)bf16_from_float(v[i]); }
+  void st4(uint32_t off, float v) {
+    if ((off & 3) || (size_t)off + 4 > data_bytes) throw std::out_of_range("staged output outside the data buffer");
+    std::memcpy(smem->data() + base + off, &v, 4);
+  }
+  void ld4_staged(uint32_t off, uint32_t rot, float* v) {
+    if ((off & 15) || (size_t)off + 16 > data_bytes) throw std::out_of_range("staged read outside the data buffer");
+    float w[4];
+    std::memcpy(w, smem->data() + base + off, 16);
+    for (int i = 0; i < 4; i++) v[i] = w[i ^ (int)rot];
+  }
+  int n_tw;
+  void tw(int e, float* re, float* im) {
+    e &= (n_tw - 1);
+    const double a = -2.0 * M_PI * (double)e / (double)n_tw;
+    *re = (float)std::cos(a);
+    *im = (float)std::sin(a);
+  }
+  void twiddle16(const float* a, const float* b, float t0r, float t0i, float wr, float wi, uint32_t* pr, uint32_t* pim) {
+    float tr = t0r, ti = t0i;
+    for (int q = 0; q < 8; q++) {
+      float x[2], z[2];
+      for (int e = 0; e < 2; e++) {
+        const int j = 2 * q + e;
+        x[e] = a[j] * tr - b[j] * ti;
+        z[e] = a[j] * ti + b[j] * tr;
+        const float nr = tr * wr - ti * wi;
+        ti = tr * wi + ti * wr;
+        tr = nr;
+      }
+      pr[q] = pack2(x[0], x[1]);
+      pim[q] = pack2(z[0], z[1]);
+    }
+  }
 };
 
 template <int SID, class P, class TIO, bool ACC16>
-void run_stage_emu(HostOps& ops, const EpiArgs& ea, uint32_t data_s, uint32_t bmat_s) {
+void run_stage_emu(HostOps& ops, const EpiArgs& ea, const GroupPairs& gp, uint32_t data_s, uint32_t bmat_s) {
   issue_stage<P, ACC16, SID>(ops, ea.tmem, data_s, bmat_s);
   constexpr int C = epi_chunks<P, SID>();
   for (int t = 0; t < P::tiles(SID); t++)
@@ -125,9 +160,11 @@ void run_stage_emu(HostOps& ops, const EpiArgs& ea, uint32_t data_s, uint32_t bm
       for (int q = 0; q < 4; q++)
         for (int lane = 0; lane < 32; lane++) {
           ops.cur_lane = lane;
-          epilogue_unit<P, TIO, ACC16, SID>(ops, ea, t, c, q, lane);
+          epilogue_unit<P, TIO, ACC16, SID>(ops, ea, gp, t, c, q, lane);
         }
-  if constexpr (SID + 1 < 2 * P::S) run_stage_emu<SID + 1, P, TIO, ACC16>(ops, ea, data_s, bmat_s);
+  if constexpr (SID == 2 * P::S - 1 && P::S == 3)
+    for (int tid = 0; tid < 64; tid++) copy_out_staged<P, TIO>(ops, ea, gp, tid, 64);
+  if constexpr (SID + 1 < 2 * P::S) run_stage_emu<SID + 1, P, TIO, ACC16>(ops, ea, gp, data_s, bmat_s);
 }
 
 // Emulates the persistent kernel's per-group flow: the producer's staging of each chunk of the group's
@@ -148,24 +185,25 @@ int run_plan(const void* u, const float* Kf, void* y, int B, int H) {
   for (int group = 0; group < ngroups; group++) {
     const int slot = group % SH::NSLOT;
     const uint32_t dbase = (uint32_t)(SH::DATA_OFF + slot * P::DATA_BYTES);
-    HostOps ops{&smem, dbase, &tmem, 0, ACC16, SH::TMEM_ALLOC, (size_t)P::DATA_BYTES};
+    HostOps ops{&smem, dbase, &tmem, 0, ACC16, SH::TMEM_ALLOC, (size_t)P::DATA_BYTES, P::N};
+    const GroupPairs gp = group_pairs(group, P::G, B, H);
     std::memset(smem.data() + dbase, 0xFF, P::DATA_BYTES);   // poison: stale data must never be read
     for (int c = 0; c < SH::CPG; c++) {
       std::memset(chunk.data(), 0xEE, chunk.size());
       const long long b0 = (long long)c * SH::CHUNK;
       for (long long b = b0; b < b0 + SH::CHUNK; b += (SEQB < SH::CHUNK ? SEQB : SH::CHUNK)) {
         const int j = (int)(b / SEQB);
-        const PairInfo pi = pair_info(group, j >> 1, P::G, B, H, P::L);
+        const PairInfo pi = gp.get(j >> 1, P::L);
         const long long off = (j & 1) ? pi.off1 : pi.off0;
         const int len = SEQB < SH::CHUNK ? SEQB : SH::CHUNK;
         if (off >= 0) std::memcpy(chunk.data() + (b - b0), uu + off + (b - (long long)j * SEQB) / (int)sizeof(TIO), len);
       }
       for (int tid = 0; tid < 64; tid++)
-        convert_chunk<P, TIO>(ops, (const TIO*)chunk.data(), (long long)c * (SH::CHUNK / (int)sizeof(TIO)),
-                              SH::CHUNK / (int)sizeof(TIO), group, B, H, tid, 64);
+        convert_chunk<P, TIO>(ops, (const TIO*)chunk.data(), c * (SH::CHUNK / (int)sizeof(TIO)),
+                              SH::CHUNK / (int)sizeof(TIO), gp, tid, 64);
     }
     EpiArgs ea{(uint32_t)(slot * P::TMEM_COLS), Kf, y, B, H, group};
-    run_stage_emu<0, P, TIO, ACC16>(ops, ea, dbase, 0u);
+    run_stage_emu<0, P, TIO, ACC16>(ops, ea, gp, dbase, 0u);
   }
   return 0;
 }

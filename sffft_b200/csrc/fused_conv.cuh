@@ -33,9 +33,31 @@ constexpr unsigned long long kWaitLimitNs = 1000000000ull;   // 1 s per barrier 
 
 __device__ __forceinline__ float bf16_bits_to_float(uint32_t bits16) { return __uint_as_float(bits16 << 16); }
 
+typedef unsigned long long u64;
+__device__ __forceinline__ u64 pk2(float lo, float hi) {
+  u64 r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void up2(u64 v, float& lo, float& hi) { asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v)); }
+// Blackwell packed fp32 arithmetic: two independent IEEE fp32 lanes per instruction.
+__device__ __forceinline__ u64 fma2(u64 a, u64 b, u64 c) {
+  u64 d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ u64 mul2(u64 a, u64 b) {
+  u64 d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
 struct DevOps {
   uint8_t* sm;   // base of the data buffer the epilogue / conversion writes (generic pointer)
   bool acc16;
+  const float2* tw_lo;   // w_N^e, e in [0, 64)
+  const float2* tw_hi;   // w_N^(64 h), h in [0, N/64)
+  int n_tw;              // transform size N
   __device__ __forceinline__ void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
     mma_f16_ss(d, a, b, idesc, acc);
   }
@@ -45,7 +67,7 @@ struct DevOps {
     *reinterpret_cast<uint4*>(sm + off) = make_uint4(a, b, c, d);
   }
   __device__ __forceinline__ void sincospi(float x, float* s, float* c) { sincospif(x, s, c); }
-  __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  __device__ __forceinline__ uint32_t pack2(float lo, float hi) const {
     __half2 h = __floats2half2_rn(lo, hi);
     return *reinterpret_cast<uint32_t*>(&h);
   }
@@ -67,6 +89,47 @@ struct DevOps {
   }
   __device__ __forceinline__ void store1(float* p, float v) { *p = v; }
   __device__ __forceinline__ void store1(__nv_bfloat16* p, float v) { *p = __float2bfloat16(v); }
+  __device__ __forceinline__ void store4(float* p, const float* v) { *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]); }
+  __device__ __forceinline__ void store4(__nv_bfloat16* p, const float* v) {
+    __nv_bfloat162 a = __floats2bfloat162_rn(v[0], v[1]), b = __floats2bfloat162_rn(v[2], v[3]);
+    *reinterpret_cast<uint2*>(p) = make_uint2(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&b));
+  }
+  __device__ __forceinline__ void st4(uint32_t off, float v) { *reinterpret_cast<float*>(sm + off) = v; }
+  __device__ __forceinline__ void ld4_staged(uint32_t off, uint32_t rot, float* v) {
+    const float4 q = *reinterpret_cast<const float4*>(sm + off);
+    const float w[4] = {q.x, q.y, q.z, q.w};
+    for (int i = 0; i < 4; i++) v[i] = w[i ^ (int)rot];
+  }
+  // w_N^e for any integer e (reduced mod N), from the two-level table: w^(64 h) * w^l
+  __device__ __forceinline__ void tw(int e, float* re, float* im) const {
+    e &= (n_tw - 1);
+    const float2 h = tw_hi[e >> 6], l = tw_lo[e & 63];
+    *re = h.x * l.x - h.y * l.y;
+    *im = h.x * l.y + h.y * l.x;
+  }
+  // 16 complex values (a + ib) times t0 * w^j, j = 0..15, rounded to fp16 pairs; two elements per f32x2 op.
+  __device__ __forceinline__ void twiddle16(const float* a, const float* b, float t0r, float t0i, float wr, float wi,
+                                            uint32_t* pr, uint32_t* pim) const {
+    const float t1r = t0r * wr - t0i * wi, t1i = t0r * wi + t0i * wr;
+    const float w2r = wr * wr - wi * wi, w2i = 2.f * wr * wi;
+    u64 TR = pk2(t0r, t1r), TI = pk2(t0i, t1i);
+    const u64 W2R = pk2(w2r, w2r), W2I = pk2(w2i, w2i), NW2I = pk2(-w2i, -w2i), NEG = pk2(-1.f, -1.f);
+#pragma unroll
+    for (int q = 0; q < 8; q++) {
+      const u64 A = pk2(a[2 * q], a[2 * q + 1]), B = pk2(b[2 * q], b[2 * q + 1]);
+      const u64 NTI = mul2(TI, NEG);
+      const u64 ORE = fma2(B, NTI, mul2(A, TR));
+      const u64 OIM = fma2(A, TI, mul2(B, TR));
+      float x0, x1, z0, z1;
+      up2(ORE, x0, x1);
+      up2(OIM, z0, z1);
+      pr[q] = pack2(x0, x1);
+      pim[q] = pack2(z0, z1);
+      const u64 TRn = fma2(TI, NW2I, mul2(TR, W2R));
+      TI = fma2(TI, W2R, mul2(TR, W2I));
+      TR = TRn;
+    }
+  }
 };
 
 struct BmatEmitDev {
@@ -89,7 +152,23 @@ struct ConvParams {
   int* status;
   int B, H;
   int ngroups;           // ceil(pairs / G), pairs = ceil(B/2) * H
+#ifdef SFFFT_TRACE
+  unsigned long long* trace;   // debug builds only: [grid][3 roles][kTraceLen] globaltimer stamps
+#endif
 };
+
+#ifdef SFFFT_TRACE
+constexpr int kTraceLen = 2048;
+#define SFFFT_STAMP(role, idx)                                                                         \
+  do {                                                                                                 \
+    if (prm.trace && (idx) < kTraceLen)                                                                \
+      prm.trace[((size_t)blockIdx.x * 3 + (role)) * kTraceLen + (idx)] = global_ns();                  \
+  } while (0)
+#else
+#define SFFFT_STAMP(role, idx) \
+  do {                         \
+  } while (0)
+#endif
 
 // ---- extra PTX used only by the persistent kernel ----
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
@@ -140,24 +219,30 @@ __device__ void issue_any(int sid, DevOps& ops, uint32_t tmem, uint32_t data_s, 
 }
 
 template <class P, class TIO, bool ACC16, int SID>
-__device__ __forceinline__ void epi_sid(DevOps& ops, const EpiArgs& ea, int q, int wi, int nwq, int lane) {
+__device__ __forceinline__ void epi_sid(DevOps& ops, const EpiArgs& ea, const GroupPairs& gp, int q, int wi, int nwq,
+                                        int lane) {
   constexpr int C = epi_chunks<P, SID>(), U = P::tiles(SID) * C;
-  for (int u = wi; u < U; u += nwq) epilogue_unit<P, TIO, ACC16, SID>(ops, ea, u / C, u - (u / C) * C, q, lane);
+  for (int u = wi; u < U; u += nwq) epilogue_unit<P, TIO, ACC16, SID>(ops, ea, gp, u / C, u - (u / C) * C, q, lane);
 }
 
 template <class P, class TIO, bool ACC16>
-__device__ void epi_any(int sid, DevOps& ops, const EpiArgs& ea, int q, int wi, int nwq, int lane) {
+__device__ void epi_any(int sid, DevOps& ops, const EpiArgs& ea, const GroupPairs& gp, int q, int wi, int nwq, int lane) {
   switch (sid) {
-    case 0: epi_sid<P, TIO, ACC16, 0>(ops, ea, q, wi, nwq, lane); break;
-    case 1: epi_sid<P, TIO, ACC16, 1>(ops, ea, q, wi, nwq, lane); break;
-    case 2: epi_sid<P, TIO, ACC16, 2>(ops, ea, q, wi, nwq, lane); break;
-    case 3: epi_sid<P, TIO, ACC16, 3>(ops, ea, q, wi, nwq, lane); break;
+    case 0: epi_sid<P, TIO, ACC16, 0>(ops, ea, gp, q, wi, nwq, lane); break;
+    case 1: epi_sid<P, TIO, ACC16, 1>(ops, ea, gp, q, wi, nwq, lane); break;
+    case 2: epi_sid<P, TIO, ACC16, 2>(ops, ea, gp, q, wi, nwq, lane); break;
+    case 3: epi_sid<P, TIO, ACC16, 3>(ops, ea, gp, q, wi, nwq, lane); break;
     default:
       if constexpr (P::S == 3) {
-        if (sid == 4) epi_sid<P, TIO, ACC16, 4>(ops, ea, q, wi, nwq, lane);
-        else epi_sid<P, TIO, ACC16, 5>(ops, ea, q, wi, nwq, lane);
+        if (sid == 4) epi_sid<P, TIO, ACC16, 4>(ops, ea, gp, q, wi, nwq, lane);
+        else epi_sid<P, TIO, ACC16, 5>(ops, ea, gp, q, wi, nwq, lane);
       }
   }
+}
+
+// Named barrier over the compute warps only (id 1; id 0 is __syncthreads).
+__device__ __forceinline__ void compute_bar(int nthreads) {
+  asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
 }
 
 template <class P, class TIO, bool ACC16>
@@ -196,6 +281,16 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
     BmatEmitDev emit{bmat};
     for_each_bmat_entry<P>(emit, tid, SH::NT);
   }
+  float2* tw_lo = reinterpret_cast<float2*>(sm + SH::TW_OFF);
+  float2* tw_hi = tw_lo + 64;
+  for (int i = tid; i < 64 + P::N / 64; i += SH::NT) {
+    // exact arguments: w_N^e = exp(-2 pi i e / N) with e reduced to (-N/2, N/2]
+    int e = i < 64 ? i : 64 * (i - 64);
+    if (e > P::N / 2) e -= P::N;
+    float sn, cs;
+    sincospif(-2.0f * (float)e / (float)P::N, &sn, &cs);
+    tw_lo[i] = make_float2(cs, sn);
+  }
   fence_async_smem();
   tc_fence_before();
   __syncthreads();
@@ -209,41 +304,43 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
       long long cc = 0;
       for (int gi = 0; gi < ni && !*abort_flag; gi++) {
         const int group = (int)blockIdx.x + gi * (int)gridDim.x;
+        const GroupPairs gp = group_pairs(group, P::G, prm.B, prm.H);
         {
-          const PairInfo a = pair_info(group, 0, P::G, prm.B, prm.H, P::L);
-          const PairInfo b = pair_info(group, P::G - 1, P::G, prm.B, prm.H, P::L);
+          const PairInfo a = gp.get(0, P::L), b = gp.get(P::G - 1, P::L);
           if (a.h >= 0) prefetch_l2(prm.Kf + 2ll * a.h * P::N, P::N * 8);
           if (b.h >= 0 && b.h != a.h) prefetch_l2(prm.Kf + 2ll * b.h * P::N, P::N * 8);
         }
         for (int c = 0; c < SH::CPG; c++, cc++) {
           const int slot = (int)(cc % NCH);
           const long long use = cc / NCH;
+          SFFFT_STAMP(0, (int)(2 * cc));
           if (use > 0 && !wait_phase(empty + slot, (uint32_t)((use - 1) & 1), abort_flag)) break;
+          SFFFT_STAMP(0, (int)(2 * cc + 1));
           uint8_t* dst = stage + slot * SH::CHUNK;
           // stream bytes [c*CHUNK, (c+1)*CHUNK) of the group's 2G sequences
           const long long b0 = (long long)c * SH::CHUNK;
           uint32_t total = 0;
           if (SEQB >= SH::CHUNK) {
             const int j = (int)(b0 / SEQB);
-            const PairInfo pi = pair_info(group, j >> 1, P::G, prm.B, prm.H, P::L);
+            const PairInfo pi = gp.get(j >> 1, P::L);
             if (((j & 1) ? pi.off1 : pi.off0) >= 0) total = SH::CHUNK;
           } else {
             const int j0 = (int)(b0 / SEQB);
             for (int jj = 0; jj < SH::CHUNK / SEQB; jj++) {
-              const PairInfo pi = pair_info(group, (j0 + jj) >> 1, P::G, prm.B, prm.H, P::L);
+              const PairInfo pi = gp.get((j0 + jj) >> 1, P::L);
               if ((((j0 + jj) & 1) ? pi.off1 : pi.off0) >= 0) total += SEQB;
             }
           }
           mbar_arrive_expect_tx(full + slot, total);
           if (SEQB >= SH::CHUNK) {
             const int j = (int)(b0 / SEQB);
-            const PairInfo pi = pair_info(group, j >> 1, P::G, prm.B, prm.H, P::L);
+            const PairInfo pi = gp.get(j >> 1, P::L);
             const long long off = (j & 1) ? pi.off1 : pi.off0;
             if (off >= 0) bulk_g2s(dst, u + off + (b0 - (long long)j * SEQB) / (int)sizeof(TIO), SH::CHUNK, full + slot);
           } else {
             const int j0 = (int)(b0 / SEQB);
             for (int jj = 0; jj < SH::CHUNK / SEQB; jj++) {
-              const PairInfo pi = pair_info(group, (j0 + jj) >> 1, P::G, prm.B, prm.H, P::L);
+              const PairInfo pi = gp.get((j0 + jj) >> 1, P::L);
               const long long off = ((j0 + jj) & 1) ? pi.off1 : pi.off0;
               if (off >= 0) bulk_g2s(dst + jj * SEQB, u + off, SEQB, full + slot);
             }
@@ -262,9 +359,11 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      DevOps ops{sm, ACC16};
+      DevOps ops{sm, ACC16, nullptr, nullptr, P::N};
       uint32_t ar_phase[2] = {0, 0};
       int issued[2] = {0, 0};
+      int nmma = 0;
+      (void)nmma;
       const int rounds = (ni + NSLOT - 1) / NSLOT;
       for (int k = 0; k < rounds * TPG && !*abort_flag; k++) {
         const int j = k % TPG;
@@ -272,12 +371,16 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
         for (int l = 0; l < NSLOT; l++) {
           const int gi = NSLOT * (k / TPG) + l;
           if (gi >= ni) continue;
+          SFFFT_STAMP(1, 3 * nmma);
           if (!wait_phase(a_ready + l, ar_phase[l], abort_flag)) break;
+          SFFFT_STAMP(1, 3 * nmma + 1);
           ar_phase[l] ^= 1;
           tc_fence_after();
           issue_any<P, ACC16>(j, ops, tmem + (uint32_t)(l * P::TMEM_COLS),
                               smem_u32(sm + SH::DATA_OFF + l * P::DATA_BYTES), smem_u32(bmat));
           mma_commit(mma_done + l);
+          SFFFT_STAMP(1, 3 * nmma + 2);
+          nmma++;
           issued[l]++;
         }
       }
@@ -295,39 +398,53 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
     uint32_t md_phase[2] = {0, 0};
     const int rounds = (ni + NSLOT - 1) / NSLOT;
     bool ok = true;
+    int ntask = 0;
+    (void)ntask;
     for (int k = 0; k < rounds * TPG && ok; k++) {
       const int j = k % TPG;
       for (int l = 0; l < NSLOT && ok; l++) {
         const int gi = NSLOT * (k / TPG) + l;
         if (gi >= ni) continue;
         const int group = (int)blockIdx.x + gi * (int)gridDim.x;
-        DevOps ops{sm + SH::DATA_OFF + l * P::DATA_BYTES, ACC16};
+        const GroupPairs gp = group_pairs(group, P::G, prm.B, prm.H);
+        DevOps ops{sm + SH::DATA_OFF + l * P::DATA_BYTES, ACC16, tw_lo, tw_hi, P::N};
+        if (lane == 0 && wc == 0) SFFFT_STAMP(2, 3 * ntask);
         if (j == 0) {
           for (int c = 0; c < SH::CPG; c++) {
             const long long cc = (long long)gi * SH::CPG + c;
             const int slot = (int)(cc % NCH);
             if (!wait_phase(full + slot, (uint32_t)((cc / NCH) & 1), abort_flag)) { ok = false; break; }
-            convert_chunk<P, TIO>(ops, reinterpret_cast<const TIO*>(stage + slot * SH::CHUNK), (long long)c * CE, CE, group,
-                                  prm.B, prm.H, ctid, SH::WC * 32);
+            convert_chunk<P, TIO>(ops, reinterpret_cast<const TIO*>(stage + slot * SH::CHUNK), c * CE, CE, gp, ctid,
+                                  SH::WC * 32);
             mbar_arrive(empty + slot);
           }
           if (!ok) break;
           fence_async_smem();
           tc_fence_before();
           mbar_arrive(a_ready + l);
+          if (lane == 0 && wc == 0) { SFFFT_STAMP(2, 3 * ntask + 1); SFFFT_STAMP(2, 3 * ntask + 2); }
         } else {
           const int sid = j - 1;
           if (!wait_phase(mma_done + l, md_phase[l], abort_flag)) { ok = false; break; }
           md_phase[l] ^= 1;
+          if (lane == 0 && wc == 0) SFFFT_STAMP(2, 3 * ntask + 1);
           tc_fence_after();
           EpiArgs ea{tmem + (uint32_t)(l * P::TMEM_COLS), prm.Kf, prm.y, prm.B, prm.H, group};
-          epi_any<P, TIO, ACC16>(sid, ops, ea, q, wi, nwq, lane);
+          epi_any<P, TIO, ACC16>(sid, ops, ea, gp, q, wi, nwq, lane);
           tc_fence_before();
+          if (P::S == 3 && sid == S2 - 1) {
+            // 3-stage plans stage the outputs in shared memory; all compute warps then copy them out coalesced
+            compute_bar(SH::WC * 32);
+            copy_out_staged<P, TIO>(ops, ea, gp, ctid, SH::WC * 32);
+            compute_bar(SH::WC * 32);
+          }
           if (sid < S2 - 1) {
             fence_async_smem();
             mbar_arrive(a_ready + l);
           }
+          if (lane == 0 && wc == 0) SFFFT_STAMP(2, 3 * ntask + 2);
         }
+        ntask++;
       }
     }
   }

@@ -135,7 +135,8 @@ struct Shape {
   static constexpr int GIN = 2 * P::G * P::L * SIO;                 // input bytes per group
   static constexpr int CHUNK = GIN < 8192 ? GIN : 8192;
   static constexpr int CPG = GIN / CHUNK;                           // chunks per group
-  static constexpr int CAP = 227 * 1024 - 1024 - 512;               // dynamic smem minus align slack, barriers
+  static constexpr int TW_BYTES = ((64 + P::N / 64) * 8 + 127) / 128 * 128;   // two-level twiddle table
+  static constexpr int CAP = 227 * 1024 - 1024 - 512 - TW_BYTES;    // dynamic smem minus align slack, barriers
   static constexpr bool TWO = 2 * P::TMEM_COLS <= 512 && P::BMAT_BYTES + 2 * P::DATA_BYTES + 2 * CHUNK <= CAP;
   static constexpr int NSLOT = TWO ? 2 : 1;
   static constexpr int DATA_OFF = P::BMAT_BYTES;
@@ -143,7 +144,8 @@ struct Shape {
   static constexpr int STAGE_MAX = ((CAP - STAGE_OFF) / CHUNK) * CHUNK;
   static constexpr int STAGE = 2 * GIN < STAGE_MAX ? 2 * GIN : STAGE_MAX;
   static constexpr int NCH = STAGE / CHUNK;
-  static constexpr int BAR_OFF = STAGE_OFF + STAGE;
+  static constexpr int TW_OFF = STAGE_OFF + STAGE;
+  static constexpr int BAR_OFF = TW_OFF + TW_BYTES;
   static constexpr int SMEM = BAR_OFF + 512 + 1024;
   static constexpr int TMEM_ALLOC = NSLOT * P::TMEM_COLS;
   static constexpr int TPG = 2 * P::S + 1;                          // tasks per group: convert + 2S epilogues

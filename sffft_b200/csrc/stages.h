@@ -8,7 +8,10 @@
 //   ops.acc_val(raw)                                         TMEM word -> float (fp32 or fp16 accumulator)
 //   ops.ldK(p)                                               four floats (two complex) of the spectrum
 //   ops.lds8(p, v)                                           eight staged input values (TIO) -> float
-//   ops.store1(p, v)                                         one output value (TIO)
+//   ops.store1(p, v) / ops.store4(p, v[4])                   output values (TIO) to global memory
+//   ops.tw(e, &re, &im)                                      w_N^e from the CTA's twiddle table
+//   ops.twiddle16(a, b, t0r, t0i, wr, wi, pr, pim)           16 complex values x t0*w^j -> fp16 pairs
+//   ops.st4(off, v) / ops.ld4_staged(off, rot, v)            staged fp32 outputs (3-stage plans)
 //
 // Algorithm per pair (reference: sfFFT src/sffft.cu:137-280, restated for tcgen05 and pairing):
 //   forward digits 0..S-1, each: DFT_R along the digit, x 1/sqrt(R), then the four-step twiddle
@@ -25,6 +28,30 @@ struct PairInfo {
   long long off0, off1;   // element offsets of the two sequences in u / y, or -1 when absent
   int h;                  // channel (spectrum row), -1 when the pair slot is empty
 };
+
+// Pair bookkeeping of one group with 32-bit arithmetic: one division per group, then pair g is found
+// by stepping from the group's first pair (pairs never exceed B*H <= INT_MAX).
+struct GroupPairs {
+  int h0, j0, PB, B, H;
+  SF_HD PairInfo get(int g, int L) const {
+    int j = j0 + g, h = h0;
+    while (j >= PB) { j -= PB; h++; }
+    PairInfo pi;
+    if (h >= H) { pi.off0 = pi.off1 = -1; pi.h = -1; return pi; }
+    pi.h = h;
+    pi.off0 = ((long long)(2 * j) * H + h) * L;
+    pi.off1 = (2 * j + 1 < B) ? ((long long)(2 * j + 1) * H + h) * L : -1;
+    return pi;
+  }
+};
+SF_HD GroupPairs group_pairs(int group, int G, int B, int H) {
+  GroupPairs gp;
+  gp.PB = (B + 1) / 2; gp.B = B; gp.H = H;
+  const int first = group * G;
+  gp.h0 = first / gp.PB;
+  gp.j0 = first - gp.h0 * gp.PB;
+  return gp;
+}
 
 SF_HD PairInfo pair_info(int cta, int g, int G, int B, int H, int L) {
   const int PB = (B + 1) / 2;
@@ -45,13 +72,11 @@ SF_HD PairInfo pair_info(int cta, int g, int G, int B, int H, int L) {
 // convert_chunk handles the stream elements [e0, e0 + ne) staged at `chunk` (raw TIO values).
 // ---------------------------------------------------------------------------------------------
 template <class P, class TIO, class Ops>
-SF_HD void convert_chunk(Ops& ops, const TIO* chunk, long long e0, int ne, int group, int B, int H, int tid,
-                         int nthreads) {
+SF_HD void convert_chunk(Ops& ops, const TIO* chunk, int e0, int ne, const GroupPairs& gp, int tid, int nthreads) {
   constexpr int V0 = P::N / P::R0, MB0 = P::MB(0);
   for (int i = tid * 8; i < ne; i += nthreads * 8) {
-    const long long e = e0 + i;
-    const int j = (int)(e / P::L), n = (int)(e - (long long)j * P::L), g = j >> 1, plane = j & 1;
-    const PairInfo pi = pair_info(group, g, P::G, B, H, P::L);
+    const int e = e0 + i, j = e / P::L, n = e - j * P::L, g = j >> 1, plane = j & 1;
+    const PairInfo pi = gp.get(g, P::L);
     const bool present = (plane == 0 ? pi.off0 : pi.off1) >= 0;
     float v[8];
     if (present) ops.lds8(chunk + i, v);
@@ -72,6 +97,10 @@ SF_HD void convert_chunk(Ops& ops, const TIO* chunk, long long e0, int ne, int g
 // ---------------------------------------------------------------------------------------------
 // MMA issue for stage SID (one thread)
 // ---------------------------------------------------------------------------------------------
+// Descriptor with its start-address field advanced by `bytes` (shared-memory addresses stay below 2^18,
+// so the 14-bit field never carries into the next one).
+SF_HD uint64_t sdesc_add(uint64_t desc, uint32_t bytes) { return desc + (uint64_t)(bytes >> 4); }
+
 template <class P, bool ACC16, int SID, class Ops>
 SF_HD void issue_stage(Ops& ops, uint32_t tmem, uint32_t data_s, uint32_t bmat_s) {
   constexpr int R = P::rad(SID), T = P::tiles(SID), NSL = R / 16;
@@ -79,32 +108,32 @@ SF_HD void issue_stage(Ops& ops, uint32_t tmem, uint32_t data_s, uint32_t bmat_s
   constexpr bool B0 = (SID == 0 && P::R0 == 16);
   constexpr int HS = P::R0 >= 32 ? P::R0 / 32 : 1;           // B K-slices per first-stage half
   constexpr uint32_t idesc = make_idesc(128, 2 * R, !ACC16, !KM, false);
+  constexpr int RB = kmaj_data_pitch(R), MBs = P::MB(SID);
+  const uint64_t a_base = KM ? make_sdesc(data_s, 16, 8 * RB, lt_for_pitch(RB)) : make_sdesc(data_s, 1024, MBs * 1024, LT_SW128);
+  const uint64_t b_base = B0 ? make_sdesc(bmat_s, 16, 8 * 32, LT_SW32) : make_sdesc(bmat_s, 16, 16 * R, lt_for_pitch(2 * R));
   for (int t = 0; t < T; t++) {
     for (int p = 0; p < 2; p++) {
       for (int j = 0; j < NSL; j++) {
         const int ks = p * NSL + j;
-        uint64_t ad;
+        uint32_t aoff;
         if constexpr (KM) {
-          constexpr int RB = kmaj_data_pitch(R);
           const uint32_t colblk = R == 64 ? (uint32_t)((ks >> 2) * P::rows(SID) * 128) : 0u;
-          const uint32_t start = data_s + colblk + (uint32_t)(t * 128 * RB) + (uint32_t)(32 * (R == 64 ? (ks & 3) : ks));
-          ad = make_sdesc(start, 16, 8 * RB, lt_for_pitch(RB));
+          aoff = colblk + (uint32_t)(t * 128 * RB) + (uint32_t)(32 * (R == 64 ? (ks & 3) : ks));
         } else {
-          constexpr int MB = P::MB(SID);
-          ad = make_sdesc(data_s + (uint32_t)((2 * ks * MB + 2 * t) << 10), 1024, MB * 1024, LT_SW128);
+          aoff = (uint32_t)((2 * ks * MBs + 2 * t) << 10);
         }
+        const uint64_t ad = sdesc_add(a_base, aoff);
         for (int sp = 0; sp < P::NSET; sp++) {
-          uint64_t bd;
+          uint32_t boff;
           if constexpr (B0) {
             // duplicated-K blocks [-Fi', Fr', Fi']: forward real plane -> window 1, imag plane -> window 0
-            bd = make_sdesc(bmat_s + (uint32_t)(P::b0_off(sp) + (p == 0 ? 1 : 0) * 16 * 32), 16, 8 * 32, LT_SW32);
+            boff = (uint32_t)(P::b0_off(sp) + (p == 0 ? 1 : 0) * 16 * 32);
           } else {
             const int w = INV ? (p == 0 ? 1 : 0) : (p == 0 ? 3 : 2);
             const int bj = SID == 0 ? (j % HS) : j;
-            bd = make_sdesc(bmat_s + (uint32_t)(P::slot_off(R, sp) + w * R * 2 * R + 32 * bj), 16, 16 * R,
-                            lt_for_pitch(2 * R));
+            boff = (uint32_t)(P::slot_off(R, sp) + w * R * 2 * R + 32 * bj);
           }
-          ops.mma(tmem + (uint32_t)(t * 2 * R), ad, bd, idesc, (uint32_t)((p | j | sp) != 0));
+          ops.mma(tmem + (uint32_t)(t * 2 * R), ad, sdesc_add(b_base, boff), idesc, (uint32_t)((p | j | sp) != 0));
         }
       }
     }
@@ -138,8 +167,24 @@ SF_HD constexpr int epi_chunks() {
 
 // One epilogue unit: TMEM lane row r = t*128 + q*32 + lane of tile t, columns [16c, 16c + 16) of both
 // the real and the imaginary half.  ea.tmem is the TMEM base of the group's accumulator slot.
+// Byte offsets of the 16-byte runs (m, k) and (m + 8, k) in an MN-major 128-B-swizzled operand (m % 8 == 0).
+SF_HD void mn_off2(int m, int k, int MB, uint32_t* o0, uint32_t* o1) {
+  const uint32_t kb = (uint32_t)((k >> 3) * MB) << 10;
+  const uint32_t kr = (uint32_t)((k & 7) << 7), xk = (uint32_t)(k & 7);
+  const uint32_t m8 = (uint32_t)(m >> 3), m8b = m8 + 1;
+  *o0 = kb + kr + ((m8 >> 3) << 10) + (((m8 & 7) ^ xk) << 4);
+  *o1 = kb + kr + ((m8b >> 3) << 10) + (((m8b & 7) ^ xk) << 4);
+}
+
+// Position of output element e (sequence-major over the group) in the swizzled fp32 staging of a
+// 3-stage plan's output: the word index's low 5 bits are XOR-ed with bits 5..9, so the stride-R2 writes
+// of a warp hit 32 different banks.
+SF_HD uint32_t out_stage_word(int e) { return (uint32_t)(e ^ ((e >> 5) & 31)); }
+
+// One epilogue unit: TMEM lane row r = t*128 + q*32 + lane of tile t, columns [16c, 16c + 16) of both
+// the real and the imaginary half.  ea.tmem is the TMEM base of the group's accumulator slot.
 template <class P, class TIO, bool ACC16, int SID, class Ops>
-SF_HD void epilogue_unit(Ops& ops, const EpiArgs& ea, int t, int c, int q, int lane) {
+SF_HD void epilogue_unit(Ops& ops, const EpiArgs& ea, const GroupPairs& gp, int t, int c, int q, int lane) {
   constexpr int S = P::S, R = P::rad(SID), N = P::N, RPP = N / R;   // rows per pair
   constexpr bool OUT = (SID == 2 * S - 1), SPEC = (SID == S - 1);
   constexpr float SC = (R == 16) ? 0.25f : (R == 64 ? 0.125f : 0.17677669529663687f);
@@ -147,35 +192,29 @@ SF_HD void epilogue_unit(Ops& ops, const EpiArgs& ea, int t, int c, int q, int l
   const uint32_t taddr = ea.tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(t * 2 * R + c0);
 
   // thread-specific twiddle exponent e(col) = ta*col + tb and next-stage write target (m0, kre)
-  int ta = 0, tb = 0, m0 = 0, kre = 0;
-  long long yo0 = -1, yo1 = -1;
-  int vv = 0;
-  const float* Kp = nullptr;
+  int ta = 0, tb = 0, m0 = 0, kre = 0, vv = 0;
   if constexpr (SID == 0) {
     if constexpr (S == 2) { ta = rr; m0 = g * P::R0; kre = rr; }
     else { const int n1 = rr / P::R2, n2 = rr - n1 * P::R2; ta = rr; m0 = g * P::R0 * P::R2 + n2 * P::R0; kre = n1; }
   } else if constexpr (S == 3 && SID == 1) {
     const int n2 = rr / P::R0, k0 = rr - n2 * P::R0;
     ta = P::R0 * n2; m0 = g * P::R0 * P::R1 + k0 * P::R1; kre = n2;
-  } else if constexpr (SPEC) {
-    const PairInfo pi = pair_info(ea.cta, g, P::G, ea.B, ea.H, P::L);
-    Kp = ea.Kf + 2 * ((long long)(pi.h < 0 ? 0 : pi.h) * N + (long long)rr * R + c0);
-  } else if constexpr (SID == S) {
-    if constexpr (S == 2) { ta = -rr; m0 = g * P::R1; kre = rr; }
-    else { const int k0 = rr / P::R1, k1 = rr - k0 * P::R1; ta = -P::R0 * k1; m0 = g * P::R0 * P::R2 + k0 * P::R2; kre = k1; }
+  } else if constexpr (SID == S && S == 2) {
+    ta = -rr; m0 = g * P::R1; kre = rr;
+  } else if constexpr (SID == S && S == 3) {
+    const int k0 = rr / P::R1, k1 = rr - k0 * P::R1; ta = -P::R0 * k1; m0 = g * P::R0 * P::R2 + k0 * P::R2; kre = k1;
   } else if constexpr (S == 3 && SID == S + 1) {
     const int k0 = rr / P::R2, n2 = rr - k0 * P::R2;
     ta = -k0 * P::R2; tb = -k0 * n2; m0 = g * P::R1 * P::R2 + n2 * P::R1; kre = k0;
-  } else {  // OUT
+  } else if constexpr (OUT) {
     if constexpr (S == 2) vv = rr;
     else { const int n2 = rr / P::R1, n1 = rr - n2 * P::R1; vv = n1 * P::R2 + n2; }
-    const PairInfo pi = pair_info(ea.cta, g, P::G, ea.B, ea.H, P::L);
-    yo0 = pi.off0; yo1 = pi.off1;
   }
 
-  // spectrum values are fetched before the accumulator so their latency overlaps the TMEM read
   float kk[32];
   if constexpr (SPEC) {
+    const PairInfo pi = gp.get(g, P::L);
+    const float* Kp = ea.Kf + 2 * ((long long)(pi.h < 0 ? 0 : pi.h) * N + (long long)rr * R + c0);
     for (int j = 0; j < 16; j += 2) {
       float k4[4];
       ops.ldK(Kp + 2 * j, k4);
@@ -186,59 +225,83 @@ SF_HD void epilogue_unit(Ops& ops, const EpiArgs& ea, int t, int c, int q, int l
   ops.tmem_ld16(taddr, raw_re);
   ops.tmem_ld16(taddr + (uint32_t)R, raw_im);
   ops.tmem_wait();
-
-  float o_re[16], o_im[16];
-  constexpr bool TW = !SPEC && !OUT;
-  if constexpr (TW) {
-    float s, cs, w_re, w_im;
-    ops.sincospi(tw_arg<N>(ta), &s, &cs);
-    w_re = cs; w_im = s;
-    ops.sincospi(tw_arg<N>(ta * c0 + tb), &s, &cs);
-    float t_re = SC * cs, t_im = SC * s;
-    for (int j = 0; j < 16; j++) {
-      const float a = ops.acc_val(raw_re[j]), b = ops.acc_val(raw_im[j]);
-      o_re[j] = a * t_re - b * t_im;
-      o_im[j] = a * t_im + b * t_re;
-      const float nr = t_re * w_re - t_im * w_im;
-      t_im = t_re * w_im + t_im * w_re;
-      t_re = nr;
-    }
-  } else if constexpr (SPEC) {
-    for (int j = 0; j < 16; j++) {
-      const float a = ops.acc_val(raw_re[j]) * SC, b = ops.acc_val(raw_im[j]) * SC;
-      o_re[j] = a * kk[2 * j] - b * kk[2 * j + 1];
-      o_im[j] = a * kk[2 * j + 1] + b * kk[2 * j];
-    }
-  } else {
-    for (int j = 0; j < 16; j++) { o_re[j] = ops.acc_val(raw_re[j]) * SC; o_im[j] = ops.acc_val(raw_im[j]) * SC; }
-  }
+  float a[16], b[16];
+  for (int j = 0; j < 16; j++) { a[j] = ops.acc_val(raw_re[j]); b[j] = ops.acc_val(raw_im[j]); }
 
   if constexpr (OUT) {
-    TIO* y = (TIO*)ea.y;
-    constexpr int V0 = N / P::R0;
-    for (int j = 0; j < 16; j++) {
-      const int n0 = c0 + j;
-      if (n0 < P::R0 / 2) {
-        if (yo0 >= 0) ops.store1(y + yo0 + (long long)n0 * V0 + vv, o_re[j]);
-        if (yo1 >= 0) ops.store1(y + yo1 + (long long)n0 * V0 + vv, o_im[j]);
+    if constexpr (S == 2) {
+      const PairInfo pi = gp.get(g, P::L);
+      TIO* y = (TIO*)ea.y;
+      constexpr int V0 = N / P::R0;
+      for (int j = 0; j < 16; j++) {
+        const int n0 = c0 + j;
+        if (n0 < P::R0 / 2) {
+          if (pi.off0 >= 0) ops.store1(y + pi.off0 + (long long)n0 * V0 + vv, a[j] * SC);
+          if (pi.off1 >= 0) ops.store1(y + pi.off1 + (long long)n0 * V0 + vv, b[j] * SC);
+        }
+      }
+    } else {
+      // 3-stage plans: stage the pair's outputs in the (now free) data buffer; copied out coalesced
+      constexpr int V0 = N / P::R0;
+      for (int j = 0; j < 16; j++) {
+        const int n0 = c0 + j;
+        if (n0 < P::R0 / 2) {
+          const int n = n0 * V0 + vv;
+          ops.st4(out_stage_word(g * 2 * P::L + n) * 4, a[j] * SC);
+          ops.st4(out_stage_word(g * 2 * P::L + P::L + n) * 4, b[j] * SC);
+        }
       }
     }
-  } else {
-    uint32_t pr[8], pim[8];
-    for (int e = 0; e < 8; e++) { pr[e] = ops.pack2(o_re[2 * e], o_re[2 * e + 1]); pim[e] = ops.pack2(o_im[2 * e], o_im[2 * e + 1]); }
-    if constexpr (SPEC) {
-      constexpr int RWS = P::rows(SID + 1);
-      ops.st16(kmaj_data_off(r, c0, R, RWS), pr[0], pr[1], pr[2], pr[3]);
-      ops.st16(kmaj_data_off(r, c0 + 8, R, RWS), pr[4], pr[5], pr[6], pr[7]);
-      ops.st16(kmaj_data_off(r, R + c0, R, RWS), pim[0], pim[1], pim[2], pim[3]);
-      ops.st16(kmaj_data_off(r, R + c0 + 8, R, RWS), pim[4], pim[5], pim[6], pim[7]);
-    } else {
-      constexpr int MBn = P::MB(SID + 1), Rn = P::rad(SID + 1);
-      ops.st16(mn_off(m0 + c0, kre, MBn), pr[0], pr[1], pr[2], pr[3]);
-      ops.st16(mn_off(m0 + c0 + 8, kre, MBn), pr[4], pr[5], pr[6], pr[7]);
-      ops.st16(mn_off(m0 + c0, Rn + kre, MBn), pim[0], pim[1], pim[2], pim[3]);
-      ops.st16(mn_off(m0 + c0 + 8, Rn + kre, MBn), pim[4], pim[5], pim[6], pim[7]);
+    return;
+  }
+
+  uint32_t pr[8], pim[8];
+  if constexpr (SPEC) {
+    for (int j = 0; j < 16; j += 2) {
+      float o_re[2], o_im[2];
+      for (int e = 0; e < 2; e++) {
+        const float x = a[j + e] * SC, z = b[j + e] * SC;
+        o_re[e] = x * kk[2 * (j + e)] - z * kk[2 * (j + e) + 1];
+        o_im[e] = x * kk[2 * (j + e) + 1] + z * kk[2 * (j + e)];
+      }
+      pr[j / 2] = ops.pack2(o_re[0], o_re[1]);
+      pim[j / 2] = ops.pack2(o_im[0], o_im[1]);
     }
+    constexpr int RWS = P::rows(SID + 1);
+    ops.st16(kmaj_data_off(r, c0, R, RWS), pr[0], pr[1], pr[2], pr[3]);
+    ops.st16(kmaj_data_off(r, c0 + 8, R, RWS), pr[4], pr[5], pr[6], pr[7]);
+    ops.st16(kmaj_data_off(r, R + c0, R, RWS), pim[0], pim[1], pim[2], pim[3]);
+    ops.st16(kmaj_data_off(r, R + c0 + 8, R, RWS), pim[4], pim[5], pim[6], pim[7]);
+  } else {
+    float t0r, t0i, wr, wi;
+    ops.tw(ta * c0 + tb, &t0r, &t0i);
+    ops.tw(ta, &wr, &wi);
+    ops.twiddle16(a, b, t0r * SC, t0i * SC, wr, wi, pr, pim);
+    constexpr int MBn = P::MB(SID + 1), Rn = P::rad(SID + 1);
+    uint32_t o0, o1;
+    mn_off2(m0 + c0, kre, MBn, &o0, &o1);
+    constexpr uint32_t IMOFF = (uint32_t)(Rn / 8) * MBn * 1024;   // K-row Rn + kre is Rn/8 groups further
+    ops.st16(o0, pr[0], pr[1], pr[2], pr[3]);
+    ops.st16(o1, pr[4], pr[5], pr[6], pr[7]);
+    ops.st16(o0 + IMOFF, pim[0], pim[1], pim[2], pim[3]);
+    ops.st16(o1 + IMOFF, pim[4], pim[5], pim[6], pim[7]);
+  }
+}
+
+// Copy-out of a 3-stage plan's staged outputs (after every epilogue thread has staged its values):
+// thread i moves 4 consecutive elements of the group's 2G sequences to y with one 16- or 8-byte store.
+template <class P, class TIO, class Ops>
+SF_HD void copy_out_staged(Ops& ops, const EpiArgs& ea, const GroupPairs& gp, int tid, int nthreads) {
+  TIO* y = (TIO*)ea.y;
+  const int total = P::G * 2 * P::L;
+  for (int e = tid * 4; e < total; e += nthreads * 4) {
+    const int seq = e / P::L, n = e - seq * P::L;
+    const PairInfo pi = gp.get(seq >> 1, P::L);
+    const long long off = (seq & 1) ? pi.off1 : pi.off0;
+    float v[4];
+    const uint32_t w = out_stage_word(e);            // e % 4 == 0: the 4 words share one XOR value
+    ops.ld4_staged((w & ~3u) * 4, (w ^ (uint32_t)e) & 3u, v);
+    if (off >= 0) ops.store4(y + off + n, v);
   }
 }
 
