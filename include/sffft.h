@@ -30,6 +30,7 @@ extern "C" {
 #define SFFFT_ERR_TIMEOUT 5
 #define SFFFT_ERR_NO_MATCH 6
 #define SFFFT_ERR_ALLOC 7
+#define SFFFT_ERR_SCRATCH_LIMIT 8 /* problem too large for sffft_conv_noalloc's fixed scratch */
 
 #define SFFFT_IO_FP32 0
 #define SFFFT_IO_BF16 1
@@ -108,6 +109,20 @@ int sffft_baseline_destroy(sffft_baseline_t bl);
  * B: n x 16 halves (B[n][k]), D: 128 x n raw TMEM words. */
 int sffft_debug_umma_probe(int a_kind, int a_slice, int b_pitch, int b_slice, int n, int acc16,
                            const unsigned short* A, const unsigned short* B, unsigned int* D);
+
+/* Allocation-free convolution, for callers that cannot allocate device memory while they run (an
+ * inference-engine plugin whose execute step must not allocate, a process whose device memory is all
+ * reserved by another allocator).  No counterpart in the reference.  The caller passes u [B][H][L], the
+ * real filter k [H][L] (k_dtype fp32 or bf16) and y; the filter spectrum and a status word live in a fixed
+ * array inside the library (16 MiB of spectrum, i.e. H * 2L * 8 bytes <= 16 MiB, plus 256 bytes), which
+ * every GPU that loads the library holds until the process exits.  Larger problems return
+ * SFFFT_ERR_SCRATCH_LIMIT without launching anything.  Uses the built-in plan for L with DFT matrices built
+ * in-kernel; results equal sffft_filter_spectrum + sffft_conv on a "legacy" plan.  The first call on a
+ * device sets up that device (looks up the array's device address, sets kernel attributes); make it
+ * before any stream capture.  All calls on a device share the array, so calls whose work overlaps on the
+ * GPU race.  sync != 0 waits for the stream and returns the kernel's device-side status. */
+int sffft_conv_noalloc(int L, int io, int acc, const void* u, const void* k, int k_dtype, void* y, int B, int H,
+                       void* stream, int sync);
 
 /* Debug: a kernel waits on a barrier that nothing arrives at, using the same bounded wait as the fused
  * kernel; returns SFFFT_ERR_TIMEOUT after about limit_us microseconds (1..1e6) with the context intact.

@@ -95,6 +95,7 @@ const char* sffft_status_string(int s) {
     case SFFFT_ERR_TIMEOUT: return "device barrier wait timed out";
     case SFFFT_ERR_NO_MATCH: return "no candidate meets the error budget";
     case SFFFT_ERR_ALLOC: return "device allocation failed";
+    case SFFFT_ERR_SCRATCH_LIMIT: return "problem exceeds the fixed scratch of the allocation-free entry point";
     default: return "unknown status";
   }
 }

@@ -9,3 +9,4 @@
 #define SFFFT_ERR_TIMEOUT 5            // a device-side barrier wait exceeded its limit
 #define SFFFT_ERR_NO_MATCH 6           // selector found no candidate within the error budget
 #define SFFFT_ERR_ALLOC 7              // device allocation failed
+#define SFFFT_ERR_SCRATCH_LIMIT 8      // problem too large for the allocation-free entry point's scratch
