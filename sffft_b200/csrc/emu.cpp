@@ -108,6 +108,13 @@ struct HostOps {
     float f; std::memcpy(&f, &w, 4); return f;
   }
   void ldK(const float* p, float (&k)[4]) { for (int e = 0; e < 4; e++) k[e] = p[e]; }
+  const uint8_t* kst_lo = nullptr;   // staged spectrum region of the current group
+  const uint8_t* kst_hi = nullptr;
+  void ldsK(const void* p, float (&k)[4]) {
+    const uint8_t* b = (const uint8_t*)p;
+    if (b < kst_lo || b + 16 > kst_hi) throw std::out_of_range("staged spectrum read outside the staged rows");
+    std::memcpy(k, p, 16);
+  }
   void lds8(const float* p, float* v) { for (int e = 0; e < 8; e++) v[e] = p[e]; }
   void lds8(const uint16_t* p, float* v) {
     for (int e = 0; e < 8; e++) { uint32_t b = (uint32_t)p[e] << 16; std::memcpy(&v[e], &b, 4); }
@@ -180,12 +187,13 @@ int run_plan(const void* u, const float* Kf, void* y, int B, int H) {
   std::vector<uint32_t> tmem(128 * 512, 0);
   hostmath::build_bmat_image<P>(smem.data());
   std::vector<uint8_t> chunk(SH::CHUNK);
+  std::vector<uint8_t> kst;
   constexpr int SEQB = P::L * (int)sizeof(TIO);
   const TIO* uu = (const TIO*)u;
   for (int group = 0; group < ngroups; group++) {
     const int slot = group % SH::NSLOT;
     const uint32_t dbase = (uint32_t)(SH::DATA_OFF + slot * P::DATA_BYTES);
-    HostOps ops{&smem, dbase, &tmem, 0, ACC16, SH::TMEM_ALLOC, (size_t)P::DATA_BYTES, P::N};
+    HostOps ops{&smem, dbase, &tmem, 0, ACC16, SH::TMEM_ALLOC, (size_t)P::DATA_BYTES, nullptr, nullptr, P::N};
     const GroupPairs gp = group_pairs(group, P::G, B, H);
     std::memset(smem.data() + dbase, 0xFF, P::DATA_BYTES);   // poison: stale data must never be read
     for (int c = 0; c < SH::CPG; c++) {
@@ -202,7 +210,30 @@ int run_plan(const void* u, const float* Kf, void* y, int B, int H) {
         convert_chunk<P, TIO>(ops, (const TIO*)chunk.data(), c * (SH::CHUNK / (int)sizeof(TIO)),
                               SH::CHUNK / (int)sizeof(TIO), gp, tid, 64);
     }
-    EpiArgs ea{(uint32_t)(slot * P::TMEM_COLS), Kf, y, B, H, group};
+    EpiArgs ea{(uint32_t)(slot * P::TMEM_COLS), Kf, y, B, H, group, nullptr, 0};
+    // the loader warp's staging of the group's spectrum rows (same swizzle as the device)
+    if constexpr (SH::KSLOT > 0) {
+      const int hf = gp.get(0, P::L).h;
+      int hl = hf;
+      for (int g = P::G - 1; g > 0; g--) {
+        const int h = gp.get(g, P::L).h;
+        if (h >= 0) { hl = h; break; }
+      }
+      if (hf >= 0 && hl - hf + 1 <= SH::KC) {
+        kst.assign((size_t)SH::KC * SH::KROW, 0xEE);
+        constexpr int PPR = P::RL / 2;
+        for (int ci = 0; ci <= hl - hf; ci++)
+          for (int o = 0; o < SH::KROW / 16; o++) {
+            const int rr = o / PPR, rem = o - rr * PPR;
+            std::memcpy(kst.data() + (size_t)ci * SH::KROW + kstage_off<P::N, P::RL>(rr, rem >> 3, rem & 7),
+                        (const uint8_t*)(Kf + 2ll * (hf + ci) * P::N) + 16 * o, 16);
+          }
+        ea.kst = kst.data();
+        ea.khf = hf;
+        ops.kst_lo = kst.data();
+        ops.kst_hi = kst.data() + (size_t)(hl - hf + 1) * SH::KROW;
+      }
+    }
     run_stage_emu<0, P, TIO, ACC16>(ops, ea, gp, dbase, 0u);
   }
   return 0;

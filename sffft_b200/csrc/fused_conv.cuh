@@ -74,6 +74,10 @@ struct DevOps {
   __device__ __forceinline__ float lo16f(uint32_t w) { return __half2float(__ushort_as_half((unsigned short)(w & 0xFFFFu))); }
   __device__ __forceinline__ float hi16f(uint32_t w) { return __half2float(__ushort_as_half((unsigned short)(w >> 16))); }
   __device__ __forceinline__ float acc_val(uint32_t w) { return acc16 ? lo16f(w) : __uint_as_float(w); }
+  __device__ __forceinline__ void ldsK(const void* p, float (&k)[4]) {
+    const float4 v = *reinterpret_cast<const float4*>(p);
+    k[0] = v.x; k[1] = v.y; k[2] = v.z; k[3] = v.w;
+  }
   __device__ __forceinline__ void ldK(const float* p, float (&k)[4]) {
     const float4 v = __ldg(reinterpret_cast<const float4*>(p));
     k[0] = v.x; k[1] = v.y; k[2] = v.z; k[3] = v.w;
@@ -153,7 +157,7 @@ struct ConvParams {
   int B, H;
   int ngroups;           // ceil(pairs / G), pairs = ceil(B/2) * H
 #ifdef SFFFT_TRACE
-  unsigned long long* trace;   // debug builds only: [grid][3 roles][kTraceLen] globaltimer stamps
+  unsigned long long* trace;   // debug builds only: [grid][3 roles][kTraceLen] SM clock stamps
 #endif
 };
 
@@ -162,7 +166,7 @@ constexpr int kTraceLen = 2048;
 #define SFFFT_STAMP(role, idx)                                                                         \
   do {                                                                                                 \
     if (prm.trace && (idx) < kTraceLen)                                                                \
-      prm.trace[((size_t)blockIdx.x * 3 + (role)) * kTraceLen + (idx)] = global_ns();                  \
+      prm.trace[((size_t)blockIdx.x * 3 + (role)) * kTraceLen + (idx)] = clock64();                    \
   } while (0)
 #else
 #define SFFFT_STAMP(role, idx) \
@@ -260,8 +264,12 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
   uint64_t* empty = bars + NCH;           // [NCH]  staged chunk consumed
   uint64_t* a_ready = bars + 2 * NCH;     // [2]    compute warps wrote a stage operand
   uint64_t* mma_done = bars + 2 * NCH + 2;// [2]    a stage's MMAs completed
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * NCH + 4);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 2 * NCH + 5);
+  uint64_t* k_full = bars + 2 * NCH + 4;  // [2]    spectrum rows staged
+  uint64_t* k_empty = bars + 2 * NCH + 6; // [2]    staged spectrum consumed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * NCH + 8);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 2 * NCH + 9);
+  int* kinfo = reinterpret_cast<int*>(bars + 2 * NCH + 10);   // [2] first staged channel, or -1
+  uint8_t* kstage = sm + SH::K_OFF;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int ni = (int)blockIdx.x < prm.ngroups ? (prm.ngroups - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x : 0;
@@ -269,7 +277,10 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
   if (warp == 1) { tmem_alloc(tmem_slot, SH::TMEM_ALLOC); tmem_relinquish(); }
   if (tid == 0) {
     for (int i = 0; i < NCH; i++) { mbar_init(full + i, 1); mbar_init(empty + i, SH::WC * 32); }
-    for (int l = 0; l < 2; l++) { mbar_init(a_ready + l, SH::WC * 32); mbar_init(mma_done + l, 1); }
+    for (int l = 0; l < 2; l++) {
+      mbar_init(a_ready + l, SH::WC * 32); mbar_init(mma_done + l, 1);
+      mbar_init(k_full + l, 32); mbar_init(k_empty + l, SH::WC * 32);
+    }
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -300,54 +311,59 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
 
   if (warp == 0) {
     // ---------------- producer ----------------
-    if (lane == 0) {
-      long long cc = 0;
-      for (int gi = 0; gi < ni && !*abort_flag; gi++) {
-        const int group = (int)blockIdx.x + gi * (int)gridDim.x;
-        const GroupPairs gp = group_pairs(group, P::G, prm.B, prm.H);
-        {
-          const PairInfo a = gp.get(0, P::L), b = gp.get(P::G - 1, P::L);
-          if (a.h >= 0) prefetch_l2(prm.Kf + 2ll * a.h * P::N, P::N * 8);
-          if (b.h >= 0 && b.h != a.h) prefetch_l2(prm.Kf + 2ll * b.h * P::N, P::N * 8);
-        }
-        for (int c = 0; c < SH::CPG; c++, cc++) {
-          const int slot = (int)(cc % NCH);
-          const long long use = cc / NCH;
-          SFFFT_STAMP(0, (int)(2 * cc));
-          if (use > 0 && !wait_phase(empty + slot, (uint32_t)((use - 1) & 1), abort_flag)) break;
-          SFFFT_STAMP(0, (int)(2 * cc + 1));
-          uint8_t* dst = stage + slot * SH::CHUNK;
-          // stream bytes [c*CHUNK, (c+1)*CHUNK) of the group's 2G sequences
-          const long long b0 = (long long)c * SH::CHUNK;
-          uint32_t total = 0;
-          if (SEQB >= SH::CHUNK) {
-            const int j = (int)(b0 / SEQB);
-            const PairInfo pi = gp.get(j >> 1, P::L);
-            if (((j & 1) ? pi.off1 : pi.off0) >= 0) total = SH::CHUNK;
-          } else {
-            const int j0 = (int)(b0 / SEQB);
-            for (int jj = 0; jj < SH::CHUNK / SEQB; jj++) {
-              const PairInfo pi = gp.get((j0 + jj) >> 1, P::L);
-              if ((((j0 + jj) & 1) ? pi.off1 : pi.off0) >= 0) total += SEQB;
-            }
-          }
-          mbar_arrive_expect_tx(full + slot, total);
-          if (SEQB >= SH::CHUNK) {
-            const int j = (int)(b0 / SEQB);
-            const PairInfo pi = gp.get(j >> 1, P::L);
-            const long long off = (j & 1) ? pi.off1 : pi.off0;
-            if (off >= 0) bulk_g2s(dst, u + off + (b0 - (long long)j * SEQB) / (int)sizeof(TIO), SH::CHUNK, full + slot);
-          } else {
-            const int j0 = (int)(b0 / SEQB);
-            for (int jj = 0; jj < SH::CHUNK / SEQB; jj++) {
-              const PairInfo pi = gp.get((j0 + jj) >> 1, P::L);
-              const long long off = ((j0 + jj) & 1) ? pi.off1 : pi.off0;
-              if (off >= 0) bulk_g2s(dst + jj * SEQB, u + off, SEQB, full + slot);
-            }
-          }
-        }
+    // A chunk holds one piece of a sequence or several whole sequences; each piece is one bulk copy,
+    // issued by its own lane so the warp issues a chunk's copies together.
+    constexpr int NP = SEQB >= SH::CHUNK ? 1 : SH::CHUNK / SEQB;
+    static_assert(NP <= 32, "one copy per producer lane");
+    long long cc = 0;
+    bool run = true;
+    for (int gi = 0; gi < ni && run; gi++) {
+      const int group = (int)blockIdx.x + gi * (int)gridDim.x;
+      const GroupPairs gp = group_pairs(group, P::G, prm.B, prm.H);
+      if (lane == 0) {
+        const PairInfo a = gp.get(0, P::L), b = gp.get(P::G - 1, P::L);
+        if (a.h >= 0) prefetch_l2(prm.Kf + 2ll * a.h * P::N, P::N * 8);
+        if (b.h >= 0 && b.h != a.h) prefetch_l2(prm.Kf + 2ll * b.h * P::N, P::N * 8);
       }
-      // drain: every issued copy has landed before the CTA can exit
+      for (int c = 0; c < SH::CPG; c++, cc++) {
+        const int slot = (int)(cc % NCH);
+        const long long use = cc / NCH;
+        if (lane == 0) SFFFT_STAMP(0, (int)(3 * cc));
+        if (use > 0) {
+          bool ok = lane == 0 ? wait_phase(empty + slot, (uint32_t)((use - 1) & 1), abort_flag) : true;
+          ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+          if (!ok) { run = false; break; }
+        }
+        if (lane == 0) SFFFT_STAMP(0, (int)(3 * cc + 1));
+        // stream bytes [c*CHUNK, (c+1)*CHUNK) of the group's 2G sequences
+        const long long b0 = (long long)c * SH::CHUNK;
+        uint32_t bytes = 0;
+        const TIO* src = nullptr;
+        uint8_t* dst = stage + slot * SH::CHUNK;
+        if (lane < NP) {
+          const int j = (int)(b0 / SEQB) + lane;
+          const PairInfo pi = gp.get(j >> 1, P::L);
+          const long long off = (j & 1) ? pi.off1 : pi.off0;
+          if (off >= 0) {
+            if (NP == 1) {
+              bytes = SH::CHUNK;
+              src = u + off + (b0 - (long long)j * SEQB) / (int)sizeof(TIO);
+            } else {
+              bytes = SEQB;
+              src = u + off;
+              dst += lane * SEQB;
+            }
+          }
+        }
+        const uint32_t total = __reduce_add_sync(0xffffffffu, bytes);
+        if (lane == 0) mbar_arrive_expect_tx(full + slot, total);
+        __syncwarp();
+        if (bytes) bulk_g2s(dst, src, bytes, full + slot);
+        if (lane == 0) SFFFT_STAMP(0, (int)(3 * cc + 2));
+      }
+    }
+    // drain: every issued copy has landed before the CTA can exit
+    if (lane == 0) {
       const long long first = cc > NCH ? cc - NCH : 0;
       for (long long d = first; d < cc; d++) {
         const int slot = (int)(d % NCH);
@@ -392,9 +408,60 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
         }
       }
     }
+  } else if (warp == 2) {
+    // ---------------- spectrum loader ----------------
+    // Copies each group's spectrum rows (coalesced 16-byte loads) into a staging slot in the swizzled
+    // order the spectrum epilogue reads; a group whose pairs span more than KC channels is marked -1 and
+    // its epilogue reads Kf from global memory instead.
+    if constexpr (SH::KSLOT > 0) {
+      constexpr int NPIECE = SH::KROW / 16, PPR = P::RL / 2;   // 16-byte pieces per row of the last digit
+      for (int gi = 0; gi < ni; gi++) {
+        const int ks = gi % SH::KSLOT, use = gi / SH::KSLOT;
+        if (use > 0) {
+          bool okw = lane == 0 ? wait_phase(k_empty + ks, (uint32_t)((use - 1) & 1), abort_flag) : true;
+          okw = __shfl_sync(0xffffffffu, okw ? 1 : 0, 0) != 0;
+          if (!okw) break;
+        }
+        const int group = (int)blockIdx.x + gi * (int)gridDim.x;
+        const GroupPairs gp = group_pairs(group, P::G, prm.B, prm.H);
+        const int hf = gp.get(0, P::L).h;
+        int hl = hf;
+        for (int g = P::G - 1; g > 0; g--) {
+          const int h = gp.get(g, P::L).h;
+          if (h >= 0) { hl = h; break; }
+        }
+        const bool staged = hf >= 0 && hl - hf + 1 <= SH::KC;
+        if (staged) {
+          uint8_t* kb = kstage + ks * SH::KC * SH::KROW;
+          for (int ci = 0; ci <= hl - hf; ci++) {
+            const uint4* src = reinterpret_cast<const uint4*>(prm.Kf + 2ll * (hf + ci) * P::N);
+            uint8_t* dst = kb + ci * SH::KROW;
+            for (int o0 = 0; o0 < NPIECE; o0 += 256) {
+              uint4 v[8];
+#pragma unroll
+              for (int q2 = 0; q2 < 8; q2++) {
+                const int o = o0 + q2 * 32 + lane;
+                v[q2] = o < NPIECE ? __ldg(src + o) : make_uint4(0, 0, 0, 0);
+              }
+#pragma unroll
+              for (int q2 = 0; q2 < 8; q2++) {
+                const int o = o0 + q2 * 32 + lane;
+                if (o < NPIECE) {
+                  const int rr = o / PPR, rem = o - rr * PPR;
+                  *reinterpret_cast<uint4*>(dst + kstage_off<P::N, P::RL>(rr, rem >> 3, rem & 7)) = v[q2];
+                }
+              }
+            }
+          }
+        }
+        if (lane == 0) kinfo[ks] = staged ? hf : -1;
+        __syncwarp();
+        mbar_arrive(k_full + ks);
+      }
+    }
   } else {
     // ---------------- compute warps ----------------
-    const int wc = warp - 2, q = warp & 3, wi = wc >> 2, nwq = SH::WC / 4, ctid = tid - 64;
+    const int wc = warp - SH::CW0, q = warp & 3, wi = wc >> 2, nwq = SH::WC / 4, ctid = tid - 32 * SH::CW0;
     uint32_t md_phase[2] = {0, 0};
     const int rounds = (ni + NSLOT - 1) / NSLOT;
     bool ok = true;
@@ -410,27 +477,54 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
         DevOps ops{sm + SH::DATA_OFF + l * P::DATA_BYTES, ACC16, tw_lo, tw_hi, P::N};
         if (lane == 0 && wc == 0) SFFFT_STAMP(2, 3 * ntask);
         if (j == 0) {
-          for (int c = 0; c < SH::CPG; c++) {
-            const long long cc = (long long)gi * SH::CPG + c;
-            const int slot = (int)(cc % NCH);
-            if (!wait_phase(full + slot, (uint32_t)((cc / NCH) & 1), abort_flag)) { ok = false; break; }
-            convert_chunk<P, TIO>(ops, reinterpret_cast<const TIO*>(stage + slot * SH::CHUNK), c * CE, CE, gp, ctid,
-                                  SH::WC * 32);
-            mbar_arrive(empty + slot);
+          if constexpr (SH::CPG <= NCH) {
+            // the whole group fits the ring: wait for all of it, then convert in one pass
+            for (int c = 0; c < SH::CPG && ok; c++) {
+              const long long cc = (long long)gi * SH::CPG + c;
+              if (!wait_phase(full + (int)(cc % NCH), (uint32_t)((cc / NCH) & 1), abort_flag)) ok = false;
+            }
+            if (!ok) break;
+            if (lane == 0 && wc == 0) SFFFT_STAMP(2, 3 * ntask + 1);
+#pragma unroll
+            for (int c = 0; c < SH::CPG; c++) {
+              const int slot = (int)(((long long)gi * SH::CPG + c) % NCH);
+              convert_chunk<P, TIO>(ops, reinterpret_cast<const TIO*>(stage + slot * SH::CHUNK), c * CE, CE, gp, ctid,
+                                    SH::WC * 32);
+            }
+            for (int c = 0; c < SH::CPG; c++) mbar_arrive(empty + (int)(((long long)gi * SH::CPG + c) % NCH));
+          } else {
+            for (int c = 0; c < SH::CPG; c++) {
+              const long long cc = (long long)gi * SH::CPG + c;
+              const int slot = (int)(cc % NCH);
+              if (!wait_phase(full + slot, (uint32_t)((cc / NCH) & 1), abort_flag)) { ok = false; break; }
+              if (c == SH::CPG - 1 && lane == 0 && wc == 0) SFFFT_STAMP(2, 3 * ntask + 1);
+              convert_chunk<P, TIO>(ops, reinterpret_cast<const TIO*>(stage + slot * SH::CHUNK), c * CE, CE, gp, ctid,
+                                    SH::WC * 32);
+              mbar_arrive(empty + slot);
+            }
           }
           if (!ok) break;
           fence_async_smem();
           tc_fence_before();
           mbar_arrive(a_ready + l);
-          if (lane == 0 && wc == 0) { SFFFT_STAMP(2, 3 * ntask + 1); SFFFT_STAMP(2, 3 * ntask + 2); }
+          if (lane == 0 && wc == 0) SFFFT_STAMP(2, 3 * ntask + 2);
         } else {
           const int sid = j - 1;
           if (!wait_phase(mma_done + l, md_phase[l], abort_flag)) { ok = false; break; }
           md_phase[l] ^= 1;
           if (lane == 0 && wc == 0) SFFFT_STAMP(2, 3 * ntask + 1);
           tc_fence_after();
-          EpiArgs ea{tmem + (uint32_t)(l * P::TMEM_COLS), prm.Kf, prm.y, prm.B, prm.H, group};
+          EpiArgs ea{tmem + (uint32_t)(l * P::TMEM_COLS), prm.Kf, prm.y, prm.B, prm.H, group, nullptr, 0};
+          const bool kst = SH::KSLOT > 0 && sid == P::S - 1;
+          constexpr int KS = SH::KSLOT > 0 ? SH::KSLOT : 1;
+          const int ks = gi % KS;
+          if (kst) {
+            if (!wait_phase(k_full + ks, (uint32_t)((gi / KS) & 1), abort_flag)) { ok = false; break; }
+            const int hf = kinfo[ks];
+            if (hf >= 0) { ea.kst = kstage + ks * SH::KC * SH::KROW; ea.khf = hf; }
+          }
           epi_any<P, TIO, ACC16>(sid, ops, ea, gp, q, wi, nwq, lane);
+          if (kst) mbar_arrive(k_empty + ks);
           tc_fence_before();
           if (P::S == 3 && sid == S2 - 1) {
             // 3-stage plans stage the outputs in shared memory; all compute warps then copy them out coalesced

@@ -125,13 +125,15 @@ struct Plan {
 };
 
 // Resources of the persistent kernel for plan P and I/O element size SIO:
-//   1 producer warp (bulk copies of u into a staging ring), 1 MMA warp, WC = 2W compute warps;
+//   1 producer warp (bulk copies of u into a staging ring), 1 MMA warp, 1 spectrum-loader warp,
+//   WC = 2W compute warps;
 //   NSLOT groups in flight (each with a data buffer and a TMEM accumulator region), 2 when both fit;
 //   an input staging ring of NCH chunks of CHUNK bytes (up to two groups ahead).
 template <class P, int SIO>
 struct Shape {
   static constexpr int WC = 2 * P::W;
-  static constexpr int NT = 32 * (WC + 2);
+  static constexpr int CW0 = 3;                                     // first compute warp
+  static constexpr int NT = 32 * (WC + CW0);
   static constexpr int GIN = 2 * P::G * P::L * SIO;                 // input bytes per group
   static constexpr int CHUNK = GIN < 8192 ? GIN : 8192;
   static constexpr int CPG = GIN / CHUNK;                           // chunks per group
@@ -144,13 +146,21 @@ struct Shape {
   static constexpr int STAGE_MAX = ((CAP - STAGE_OFF) / CHUNK) * CHUNK;
   static constexpr int STAGE = 2 * GIN < STAGE_MAX ? 2 * GIN : STAGE_MAX;
   static constexpr int NCH = STAGE / CHUNK;
-  static constexpr int TW_OFF = STAGE_OFF + STAGE;
+  // spectrum staging: KSLOT slots of KC channel rows (N complex fp32 each), filled by the loader warp in a
+  // swizzled [chunk][row][16 B ^ row%8] order; groups spanning more than KC channels read Kf from global
+  static constexpr int KROW = P::N * 8;
+  static constexpr int KLEFT = CAP - (STAGE_OFF + STAGE);
+  static constexpr int KC2 = KLEFT / (2 * KROW) < P::G ? KLEFT / (2 * KROW) : P::G;
+  static constexpr int KSLOT = KC2 >= 1 ? 2 : (KLEFT >= KROW ? 1 : 0);
+  static constexpr int KC = KSLOT == 2 ? KC2 : KSLOT;
+  static constexpr int K_OFF = STAGE_OFF + STAGE;
+  static constexpr int TW_OFF = K_OFF + KSLOT * KC * KROW;
   static constexpr int BAR_OFF = TW_OFF + TW_BYTES;
   static constexpr int SMEM = BAR_OFF + 512 + 1024;
   static constexpr int TMEM_ALLOC = NSLOT * P::TMEM_COLS;
   static constexpr int TPG = 2 * P::S + 1;                          // tasks per group: convert + 2S epilogues
   static_assert(NCH >= 2, "staging ring needs two chunks");
-  static_assert(2 * NCH + 8 <= 64, "barrier area");
+  static_assert(2 * NCH + 16 <= 64, "barrier area");
 };
 
 // Row pitch of the K-major A operand of the inverse last-digit stage (re | im halves of a row).

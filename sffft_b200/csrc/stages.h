@@ -6,7 +6,8 @@
 //   ops.sincospi(x, &s, &c)                                  sin/cos of pi*x
 //   ops.pack2(lo, hi)                                        two floats -> f16x2 (round to nearest)
 //   ops.acc_val(raw)                                         TMEM word -> float (fp32 or fp16 accumulator)
-//   ops.ldK(p)                                               four floats (two complex) of the spectrum
+//   ops.ldK(p) / ops.ldsK(p)                                 four floats (two complex) of the spectrum from
+//                                                            global / staged shared memory
 //   ops.lds8(p, v)                                           eight staged input values (TIO) -> float
 //   ops.store1(p, v) / ops.store4(p, v[4])                   output values (TIO) to global memory
 //   ops.tw(e, &re, &im)                                      w_N^e from the CTA's twiddle table
@@ -156,7 +157,17 @@ struct EpiArgs {
   const float* Kf;      // [H][N] complex fp32, digit order
   void* y;              // output base (TIO*)
   int B, H, cta;        // cta: the group index (pairs cta*G .. cta*G + G - 1)
+  const uint8_t* kst;   // spectrum rows of channels khf, khf+1, ... staged by the loader warp, or null
+  int khf;
 };
+
+// Byte offset of the 16-byte piece j (two complex values) of 16-value chunk c of row rr in a staged
+// spectrum row of a plan whose last radix is R (rows = N / R): [c][rr][piece ^ rr%8], so the 32 rows a
+// warp reads hit 32 different bank groups.
+template <int N, int R>
+SF_HD uint32_t kstage_off(int rr, int c, int j) {
+  return (uint32_t)((((c * (N / R) + rr) << 3) + (j ^ (rr & 7))) << 4);
+}
 
 // Number of 16-column chunks an epilogue thread reads per row in stage SID (the last inverse stage only
 // needs time rows n0 < R0/2).
@@ -214,11 +225,23 @@ SF_HD void epilogue_unit(Ops& ops, const EpiArgs& ea, const GroupPairs& gp, int 
   float kk[32];
   if constexpr (SPEC) {
     const PairInfo pi = gp.get(g, P::L);
-    const float* Kp = ea.Kf + 2 * ((long long)(pi.h < 0 ? 0 : pi.h) * N + (long long)rr * R + c0);
-    for (int j = 0; j < 16; j += 2) {
-      float k4[4];
-      ops.ldK(Kp + 2 * j, k4);
-      kk[2 * j] = k4[0]; kk[2 * j + 1] = k4[1]; kk[2 * j + 2] = k4[2]; kk[2 * j + 3] = k4[3];
+    // an empty pair slot (past the last pair) reads any valid row; its outputs are never stored
+    if (ea.kst) {
+      const int h = pi.h < 0 ? ea.khf : pi.h;
+      const uint8_t* kb = ea.kst + (size_t)(h - ea.khf) * (N * 8);
+      for (int j = 0; j < 8; j++) {
+        float k4[4];
+        ops.ldsK(kb + kstage_off<N, R>(rr, c, j), k4);
+        kk[4 * j] = k4[0]; kk[4 * j + 1] = k4[1]; kk[4 * j + 2] = k4[2]; kk[4 * j + 3] = k4[3];
+      }
+    } else {
+      const int h = pi.h < 0 ? 0 : pi.h;
+      const float* Kp = ea.Kf + 2 * ((long long)h * N + (long long)rr * R + c0);
+      for (int j = 0; j < 16; j += 2) {
+        float k4[4];
+        ops.ldK(Kp + 2 * j, k4);
+        kk[2 * j] = k4[0]; kk[2 * j + 1] = k4[1]; kk[2 * j + 2] = k4[2]; kk[2 * j + 3] = k4[3];
+      }
     }
   }
   uint32_t raw_re[16], raw_im[16];

@@ -67,3 +67,16 @@ def test_zero_and_impulse_inputs():
     u = rng.standard_normal((2, 1, L)).astype(np.float32)
     Kf[..., 0] = 1.0
     assert rel_l2(sf.emu_conv("16x16/w4", u, Kf), u) < 5e-4
+
+
+@pytest.mark.parametrize("name", ["16x16/w4", "32x32/w4", "64x32/w4", "32x64/w8", "64x64/w4", "16x16x16/w4"])
+def test_staged_spectrum_path(oracle, name):
+    # B = 8 puts one channel in each group, so the spectrum epilogue reads staged spectrum rows
+    assert run_case(oracle, name, 8, 2) <= TOL[("fp32", "fp32")]
+
+
+def test_staged_spectrum_partial_groups(oracle):
+    # B = 2: one channel per pair; H = 33 leaves the last group with a single pair (empty slots must not
+    # read outside the staged spectrum rows)
+    for name in ["16x16/w4", "32x32/w4"]:
+        assert run_case(oracle, name, 2, 33) <= TOL[("fp32", "fp32")]
