@@ -60,18 +60,19 @@ static const std::vector<const ConvEntry*>& catalog() {
   return all;
 }
 
-// Built-in B200 default per length (the static choice of the plan selector; the CLI's empirical
-// selector can override it from measurements).
+// Built-in B200 default per length: the fastest catalog entry of the plan BASELINE-style workloads name for
+// that length (B = 8, H = 768, fp32 and bf16 I/O, timed on one B200); the CLI's empirical selector can
+// override it from its own measurements.
 static const char* default_for(int L) {
   switch (L) {
-    case 128: return "16x16/w4";
-    case 256: return "32x16/w4";
-    case 512: return "32x32/w4";
-    case 1024: return "64x32/w4";
-    case 2048: return "64x64/w4";
-    case 4096: return "32x16x16/w4";
+    case 128: return "16x16/w8";
+    case 256: return "32x16/w8";
+    case 512: return "32x32/w8";
+    case 1024: return "64x32/w8";
+    case 2048: return "64x64/w8";
+    case 4096: return "32x16x16/w8";
     case 8192: return "32x32x16/w4";
-    case 16384: return "32x32x32/w4";
+    case 16384: return "32x32x32/w8";
     default: return nullptr;
   }
 }

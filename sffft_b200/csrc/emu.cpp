@@ -140,9 +140,12 @@ struct HostOps {
     *re = (float)std::cos(a);
     *im = (float)std::sin(a);
   }
-  void twiddle16(const float* a, const float* b, float t0r, float t0i, float wr, float wi, uint32_t* pr, uint32_t* pim) {
+  // elements j < 8 step from t0, elements j >= 8 from t8 (two recurrences, as on the device)
+  void twiddle16(const float* a, const float* b, float t0r, float t0i, float t8r, float t8i, float wr, float wi,
+                 uint32_t* pr, uint32_t* pim) {
     float tr = t0r, ti = t0i;
     for (int q = 0; q < 8; q++) {
+      if (q == 4) { tr = t8r; ti = t8i; }
       float x[2], z[2];
       for (int e = 0; e < 2; e++) {
         const int j = 2 * q + e;
@@ -161,14 +164,14 @@ struct HostOps {
 template <int SID, class P, class TIO, bool ACC16>
 void run_stage_emu(HostOps& ops, const EpiArgs& ea, const GroupPairs& gp, uint32_t data_s, uint32_t bmat_s) {
   issue_stage<P, ACC16, SID>(ops, ea.tmem, data_s, bmat_s);
-  constexpr int C = epi_chunks<P, SID>();
-  for (int t = 0; t < P::tiles(SID); t++)
-    for (int c = 0; c < C; c++)
-      for (int q = 0; q < 4; q++)
-        for (int lane = 0; lane < 32; lane++) {
-          ops.cur_lane = lane;
-          epilogue_unit<P, TIO, ACC16, SID>(ops, ea, gp, t, c, q, lane);
-        }
+  // every compute warp's share of the stage, in the kernel's unit order (lane quarter q, warp wi of NWQ)
+  constexpr int NWQ = Shape<P, (int)sizeof(TIO)>::NWQ;
+  for (int wi = 0; wi < NWQ; wi++)
+    for (int q = 0; q < 4; q++)
+      for (int lane = 0; lane < 32; lane++) {
+        ops.cur_lane = lane;
+        epi_warp<P, TIO, ACC16, SID>(ops, ea, gp, wi, q, lane);
+      }
   if constexpr (SID == 2 * P::S - 1 && P::S == 3)
     for (int tid = 0; tid < 64; tid++) copy_out_staged<P, TIO>(ops, ea, gp, tid, 64);
   if constexpr (SID + 1 < 2 * P::S) run_stage_emu<SID + 1, P, TIO, ACC16>(ops, ea, gp, data_s, bmat_s);

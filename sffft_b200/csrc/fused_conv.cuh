@@ -111,27 +111,33 @@ struct DevOps {
     *re = h.x * l.x - h.y * l.y;
     *im = h.x * l.y + h.y * l.x;
   }
-  // 16 complex values (a + ib) times t0 * w^j, j = 0..15, rounded to fp16 pairs; two elements per f32x2 op.
-  __device__ __forceinline__ void twiddle16(const float* a, const float* b, float t0r, float t0i, float wr, float wi,
-                                            uint32_t* pr, uint32_t* pim) const {
+  // 16 complex values (a + ib) times t0 * w^j (j < 8) and t8 * w^(j-8) (j >= 8), rounded to fp16 pairs:
+  // two independent recurrences of four steps, each carrying two elements per f32x2 op.
+  __device__ __forceinline__ void twiddle16(const float* a, const float* b, float t0r, float t0i, float t8r, float t8i,
+                                            float wr, float wi, uint32_t* pr, uint32_t* pim) const {
     const float t1r = t0r * wr - t0i * wi, t1i = t0r * wi + t0i * wr;
+    const float t9r = t8r * wr - t8i * wi, t9i = t8r * wi + t8i * wr;
     const float w2r = wr * wr - wi * wi, w2i = 2.f * wr * wi;
-    u64 TR = pk2(t0r, t1r), TI = pk2(t0i, t1i);
+    u64 TR[2] = {pk2(t0r, t1r), pk2(t8r, t9r)}, TI[2] = {pk2(t0i, t1i), pk2(t8i, t9i)};
     const u64 W2R = pk2(w2r, w2r), W2I = pk2(w2i, w2i), NW2I = pk2(-w2i, -w2i), NEG = pk2(-1.f, -1.f);
 #pragma unroll
-    for (int q = 0; q < 8; q++) {
-      const u64 A = pk2(a[2 * q], a[2 * q + 1]), B = pk2(b[2 * q], b[2 * q + 1]);
-      const u64 NTI = mul2(TI, NEG);
-      const u64 ORE = fma2(B, NTI, mul2(A, TR));
-      const u64 OIM = fma2(A, TI, mul2(B, TR));
-      float x0, x1, z0, z1;
-      up2(ORE, x0, x1);
-      up2(OIM, z0, z1);
-      pr[q] = pack2(x0, x1);
-      pim[q] = pack2(z0, z1);
-      const u64 TRn = fma2(TI, NW2I, mul2(TR, W2R));
-      TI = fma2(TI, W2R, mul2(TR, W2I));
-      TR = TRn;
+    for (int q = 0; q < 4; q++) {
+#pragma unroll
+      for (int h = 0; h < 2; h++) {
+        const int p = q + 4 * h;   // elements 2p, 2p + 1
+        const u64 A = pk2(a[2 * p], a[2 * p + 1]), B = pk2(b[2 * p], b[2 * p + 1]);
+        const u64 NTI = mul2(TI[h], NEG);
+        const u64 ORE = fma2(B, NTI, mul2(A, TR[h]));
+        const u64 OIM = fma2(A, TI[h], mul2(B, TR[h]));
+        float x0, x1, z0, z1;
+        up2(ORE, x0, x1);
+        up2(OIM, z0, z1);
+        pr[p] = pack2(x0, x1);
+        pim[p] = pack2(z0, z1);
+        const u64 TRn = fma2(TI[h], NW2I, mul2(TR[h], W2R));
+        TI[h] = fma2(TI[h], W2R, mul2(TR[h], W2I));
+        TR[h] = TRn;
+      }
     }
   }
 };
@@ -202,6 +208,39 @@ __device__ __forceinline__ bool wait_phase(uint64_t* bar, uint32_t parity, volat
   }
 }
 
+// Every lane of the warp waits on the barrier itself (each lane then sees the data the phase publishes);
+// the vote makes the outcome uniform across the warp, so warp-wide steps that follow cannot diverge.
+__device__ __forceinline__ bool wait_phase_all(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  const bool ok = wait_phase(bar, parity, abort_flag);
+  return __all_sync(0xffffffffu, ok) != 0;
+}
+
+// Shared FIFO slots (input chunks, staged spectrum rows) are consumed by several teams out of order, so a
+// consumer can reach a slot two or more uses ahead of its barrier, where a parity test cannot tell the
+// phases apart.  The filler stamps each slot with the index of what it is filling before it arms the
+// barrier; a consumer first waits (bounded) until the stamp reaches its own index, after which the
+// barrier's pending phase is its own and the parity wait is exact.
+__device__ __forceinline__ bool wait_stamp(const volatile int* stamp, int want, volatile int* abort_flag) {
+  if (*stamp >= want) return true;
+  const uint64_t t0 = global_ns();
+  while (*stamp < want) {
+    if (*abort_flag) return false;
+    if (global_ns() - t0 > kWaitLimitNs) { *abort_flag = 1; return false; }
+  }
+  return true;
+}
+__device__ __forceinline__ bool wait_stamp_all(const volatile int* stamp, int want, volatile int* abort_flag) {
+  const bool ok = wait_stamp(stamp, want, abort_flag);
+  return __all_sync(0xffffffffu, ok) != 0;
+}
+
+// One arrival per warp on a consumer barrier (initialised with the number of arriving warps): the warp's
+// lanes finish their own accesses and fences first, the warp synchronises, then lane 0 arrives.
+__device__ __forceinline__ void warp_arrive(uint64_t* bar, int lane) {
+  __syncwarp();
+  if (lane == 0) mbar_arrive(bar);
+}
+
 template <class P, bool ACC16, int SID>
 __device__ __forceinline__ void issue_sid(DevOps& ops, uint32_t tmem, uint32_t data_s, uint32_t bmat_s) {
   issue_stage<P, ACC16, SID>(ops, tmem, data_s, bmat_s);
@@ -223,36 +262,38 @@ __device__ void issue_any(int sid, DevOps& ops, uint32_t tmem, uint32_t data_s, 
 }
 
 template <class P, class TIO, bool ACC16, int SID>
-__device__ __forceinline__ void epi_sid(DevOps& ops, const EpiArgs& ea, const GroupPairs& gp, int q, int wi, int nwq,
-                                        int lane) {
-  constexpr int C = epi_chunks<P, SID>(), U = P::tiles(SID) * C;
-  for (int u = wi; u < U; u += nwq) epilogue_unit<P, TIO, ACC16, SID>(ops, ea, gp, u / C, u - (u / C) * C, q, lane);
+__device__ __forceinline__ void epi_sid(DevOps& ops, const EpiArgs& ea, const GroupPairs& gp, int q, int wi, int lane) {
+  epi_warp<P, TIO, ACC16, SID>(ops, ea, gp, wi, q, lane);
 }
 
 template <class P, class TIO, bool ACC16>
-__device__ void epi_any(int sid, DevOps& ops, const EpiArgs& ea, const GroupPairs& gp, int q, int wi, int nwq, int lane) {
+__device__ void epi_any(int sid, DevOps& ops, const EpiArgs& ea, const GroupPairs& gp, int q, int wi, int lane) {
   switch (sid) {
-    case 0: epi_sid<P, TIO, ACC16, 0>(ops, ea, gp, q, wi, nwq, lane); break;
-    case 1: epi_sid<P, TIO, ACC16, 1>(ops, ea, gp, q, wi, nwq, lane); break;
-    case 2: epi_sid<P, TIO, ACC16, 2>(ops, ea, gp, q, wi, nwq, lane); break;
-    case 3: epi_sid<P, TIO, ACC16, 3>(ops, ea, gp, q, wi, nwq, lane); break;
+    case 0: epi_sid<P, TIO, ACC16, 0>(ops, ea, gp, q, wi, lane); break;
+    case 1: epi_sid<P, TIO, ACC16, 1>(ops, ea, gp, q, wi, lane); break;
+    case 2: epi_sid<P, TIO, ACC16, 2>(ops, ea, gp, q, wi, lane); break;
+    case 3: epi_sid<P, TIO, ACC16, 3>(ops, ea, gp, q, wi, lane); break;
     default:
       if constexpr (P::S == 3) {
-        if (sid == 4) epi_sid<P, TIO, ACC16, 4>(ops, ea, gp, q, wi, nwq, lane);
-        else epi_sid<P, TIO, ACC16, 5>(ops, ea, gp, q, wi, nwq, lane);
+        if (sid == 4) epi_sid<P, TIO, ACC16, 4>(ops, ea, gp, q, wi, lane);
+        else epi_sid<P, TIO, ACC16, 5>(ops, ea, gp, q, wi, lane);
       }
   }
 }
 
-// Named barrier over the compute warps only (id 1; id 0 is __syncthreads).
-__device__ __forceinline__ void compute_bar(int nthreads) {
-  asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
+// Barrier over one team of compute warps, on the team's mbarrier (one arrival per warp) with the same
+// bounded wait as every other wait in the kernel; `phase` is the caller's count of earlier uses.
+__device__ __forceinline__ bool team_sync(uint64_t* bar, uint32_t& phase, int lane, volatile int* abort_flag) {
+  warp_arrive(bar, lane);
+  const bool ok = wait_phase_all(bar, phase & 1u, abort_flag);
+  phase++;
+  return ok;
 }
 
 template <class P, class TIO, bool ACC16>
 __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kernel(ConvParams prm) {
   using SH = Shape<P, sizeof(TIO)>;
-  constexpr int S2 = 2 * P::S, TPG = SH::TPG, NSLOT = SH::NSLOT, NCH = SH::NCH;
+  constexpr int S2 = 2 * P::S, TPG = SH::TPG, NS = SH::NS, NCH = SH::NCH;
   constexpr int CE = SH::CHUNK / (int)sizeof(TIO);               // elements per chunk
   constexpr int SEQB = P::L * (int)sizeof(TIO);                   // bytes per sequence
   extern __shared__ uint8_t smem_raw[];
@@ -260,15 +301,18 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
   uint8_t* bmat = sm;
   uint8_t* stage = sm + SH::STAGE_OFF;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + SH::BAR_OFF);
-  uint64_t* full = bars;                  // [NCH]  staged chunk landed
-  uint64_t* empty = bars + NCH;           // [NCH]  staged chunk consumed
-  uint64_t* a_ready = bars + 2 * NCH;     // [2]    compute warps wrote a stage operand
-  uint64_t* mma_done = bars + 2 * NCH + 2;// [2]    a stage's MMAs completed
-  uint64_t* k_full = bars + 2 * NCH + 4;  // [2]    spectrum rows staged
-  uint64_t* k_empty = bars + 2 * NCH + 6; // [2]    staged spectrum consumed
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * NCH + 8);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 2 * NCH + 9);
-  int* kinfo = reinterpret_cast<int*>(bars + 2 * NCH + 10);   // [2] first staged channel, or -1
+  uint64_t* full = bars;                       // [NCH] staged chunk landed
+  uint64_t* empty = bars + NCH;                // [NCH] staged chunk consumed
+  uint64_t* a_ready = bars + 2 * NCH;          // [NS]  a team wrote a stage operand of this slot
+  uint64_t* mma_done = a_ready + NS;           // [NS]  a stage's MMAs of this slot completed
+  uint64_t* k_full = mma_done + NS;            // [2]   spectrum rows staged
+  uint64_t* k_empty = k_full + 2;              // [2]   staged spectrum consumed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(k_empty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(k_empty + 3);
+  int* kinfo = reinterpret_cast<int*>(k_empty + 4);   // [2] first staged channel, or -1
+  uint64_t* team_done = k_empty + 5;           // [NTEAM] a team's warps staged their outputs / copied them out
+  volatile int* cstamp = reinterpret_cast<volatile int*>(team_done + SH::NTEAM);   // [NCH] chunk being filled
+  volatile int* kstamp = cstamp + NCH;         // [2] group whose spectrum rows are being staged
   uint8_t* kstage = sm + SH::K_OFF;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -276,11 +320,13 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
 
   if (warp == 1) { tmem_alloc(tmem_slot, SH::TMEM_ALLOC); tmem_relinquish(); }
   if (tid == 0) {
-    for (int i = 0; i < NCH; i++) { mbar_init(full + i, 1); mbar_init(empty + i, SH::WC * 32); }
-    for (int l = 0; l < 2; l++) {
-      mbar_init(a_ready + l, SH::WC * 32); mbar_init(mma_done + l, 1);
-      mbar_init(k_full + l, 32); mbar_init(k_empty + l, SH::WC * 32);
-    }
+    // consumer barriers count one arrival per warp of the consuming team
+    for (int i = 0; i < NCH; i++) { mbar_init(full + i, 1); mbar_init(empty + i, SH::TWARPS); }
+    for (int s = 0; s < NS; s++) { mbar_init(a_ready + s, SH::TWARPS); mbar_init(mma_done + s, 1); }
+    for (int l = 0; l < 2; l++) { mbar_init(k_full + l, 32); mbar_init(k_empty + l, SH::TWARPS); }
+    for (int t = 0; t < SH::NTEAM; t++) mbar_init(team_done + t, SH::TWARPS);
+    for (int i = 0; i < NCH; i++) cstamp[i] = -1;
+    kstamp[0] = kstamp[1] = -1;
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -330,10 +376,9 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
         const long long use = cc / NCH;
         if (lane == 0) SFFFT_STAMP(0, (int)(3 * cc));
         if (use > 0) {
-          bool ok = lane == 0 ? wait_phase(empty + slot, (uint32_t)((use - 1) & 1), abort_flag) : true;
-          ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-          if (!ok) { run = false; break; }
+          if (!wait_phase_all(empty + slot, (uint32_t)((use - 1) & 1), abort_flag)) { run = false; break; }
         }
+        if (lane == 0) cstamp[slot] = (int)cc;
         if (lane == 0) SFFFT_STAMP(0, (int)(3 * cc + 1));
         // stream bytes [c*CHUNK, (c+1)*CHUNK) of the group's 2G sequences
         const long long b0 = (long long)c * SH::CHUNK;
@@ -374,37 +419,54 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
+    // Slot s holds this CTA's groups s, s + NS, ...; each group needs its 2S stages in order.  The issuer
+    // scans the slots and issues the next stage of any slot whose operand is ready.
     if (lane == 0) {
       DevOps ops{sm, ACC16, nullptr, nullptr, P::N};
-      uint32_t ar_phase[2] = {0, 0};
-      int issued[2] = {0, 0};
+      int done[NS], total[NS];
+      uint32_t ar_bits = 0;
+      int left = 0;
+#pragma unroll
+      for (int s = 0; s < NS; s++) {
+        done[s] = 0;
+        total[s] = (s < ni ? (ni - s + NS - 1) / NS : 0) * S2;
+        left += total[s];
+      }
       int nmma = 0;
       (void)nmma;
-      const int rounds = (ni + NSLOT - 1) / NSLOT;
-      for (int k = 0; k < rounds * TPG && !*abort_flag; k++) {
-        const int j = k % TPG;
-        if (j == TPG - 1) continue;   // after the last epilogue there is no MMA
-        for (int l = 0; l < NSLOT; l++) {
-          const int gi = NSLOT * (k / TPG) + l;
-          if (gi >= ni) continue;
-          SFFFT_STAMP(1, 3 * nmma);
-          if (!wait_phase(a_ready + l, ar_phase[l], abort_flag)) break;
-          SFFFT_STAMP(1, 3 * nmma + 1);
-          ar_phase[l] ^= 1;
-          tc_fence_after();
-          issue_any<P, ACC16>(j, ops, tmem + (uint32_t)(l * P::TMEM_COLS),
-                              smem_u32(sm + SH::DATA_OFF + l * P::DATA_BYTES), smem_u32(bmat));
-          mma_commit(mma_done + l);
-          SFFFT_STAMP(1, 3 * nmma + 2);
-          nmma++;
-          issued[l]++;
+      uint64_t t_idle = global_ns();
+      while (left > 0) {
+        bool progressed = false;
+#pragma unroll
+        for (int s = 0; s < NS; s++) {
+          if (done[s] < total[s] && mbar_test_wait(a_ready + s, (ar_bits >> s) & 1u)) {
+            SFFFT_STAMP(1, 3 * nmma);
+            ar_bits ^= 1u << s;
+            tc_fence_after();
+            SFFFT_STAMP(1, 3 * nmma + 1);
+            issue_any<P, ACC16>(done[s] % S2, ops, tmem + (uint32_t)(s * P::TMEM_COLS),
+                                smem_u32(sm + SH::DATA_OFF + s * P::DATA_BYTES), smem_u32(bmat));
+            mma_commit(mma_done + s);
+            SFFFT_STAMP(1, 3 * nmma + 2);
+            nmma++;
+            done[s]++;
+            left--;
+            progressed = true;
+          }
+        }
+        if (progressed) {
+          t_idle = global_ns();
+        } else {
+          if (*abort_flag) break;
+          if (global_ns() - t_idle > kWaitLimitNs) { *abort_flag = 1; break; }
         }
       }
       // make sure no MMA is still writing TMEM when the CTA frees it
-      for (int l = 0; l < NSLOT; l++) {
-        if (!issued[l]) continue;
+#pragma unroll
+      for (int s = 0; s < NS; s++) {
+        if (!done[s]) continue;
         const uint64_t t0 = global_ns();
-        while (!mbar_try_wait(mma_done + l, (uint32_t)((issued[l] - 1) & 1)) && global_ns() - t0 < kWaitLimitNs) {
+        while (!mbar_try_wait(mma_done + s, (uint32_t)((done[s] - 1) & 1)) && global_ns() - t0 < kWaitLimitNs) {
         }
       }
     }
@@ -418,10 +480,9 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
       for (int gi = 0; gi < ni; gi++) {
         const int ks = gi % SH::KSLOT, use = gi / SH::KSLOT;
         if (use > 0) {
-          bool okw = lane == 0 ? wait_phase(k_empty + ks, (uint32_t)((use - 1) & 1), abort_flag) : true;
-          okw = __shfl_sync(0xffffffffu, okw ? 1 : 0, 0) != 0;
-          if (!okw) break;
+          if (!wait_phase_all(k_empty + ks, (uint32_t)((use - 1) & 1), abort_flag)) break;
         }
+        if (lane == 0) kstamp[ks] = gi;
         const int group = (int)blockIdx.x + gi * (int)gridDim.x;
         const GroupPairs gp = group_pairs(group, P::G, prm.B, prm.H);
         const int hf = gp.get(0, P::L).h;
@@ -461,80 +522,103 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
     }
   } else {
     // ---------------- compute warps ----------------
-    const int wc = warp - SH::CW0, q = warp & 3, wi = wc >> 2, nwq = SH::WC / 4, ctid = tid - 32 * SH::CW0;
-    uint32_t md_phase[2] = {0, 0};
-    const int rounds = (ni + NSLOT - 1) / NSLOT;
+    // Team `team` (warps team*TWARPS .. of the compute warps) owns slots team*NST .. team*NST + NST - 1
+    // and, round after round, runs the TPG tasks of its groups, alternating between its slots.
+    constexpr int NST = SH::NST, TWT = SH::TWARPS * 32;
+    const int wc = warp - SH::CW0, team = wc / SH::TWARPS, wt = wc - team * SH::TWARPS;
+    const int q = warp & 3, wi = wt >> 2, ttid = wt * 32 + lane;
+    uint32_t md_bits = 0;                 // bit l: parity of local slot l's next mma_done phase
+    uint32_t ts_phase = 0;                // uses of this team's team_done barrier
+    GroupPairs gps[NST];
+    const int rounds = (ni + NS - 1) / NS;
     bool ok = true;
     int ntask = 0;
     (void)ntask;
     for (int k = 0; k < rounds * TPG && ok; k++) {
       const int j = k % TPG;
-      for (int l = 0; l < NSLOT && ok; l++) {
-        const int gi = NSLOT * (k / TPG) + l;
+#pragma unroll
+      for (int l = 0; l < NST; l++) {
+        if (!ok) break;
+        const int s = team * NST + l;
+        const int gi = NS * (k / TPG) + s;
         if (gi >= ni) continue;
         const int group = (int)blockIdx.x + gi * (int)gridDim.x;
-        const GroupPairs gp = group_pairs(group, P::G, prm.B, prm.H);
-        DevOps ops{sm + SH::DATA_OFF + l * P::DATA_BYTES, ACC16, tw_lo, tw_hi, P::N};
+        if (j == 0) gps[l] = group_pairs(group, P::G, prm.B, prm.H);
+        const GroupPairs gp = gps[l];
+        DevOps ops{sm + SH::DATA_OFF + s * P::DATA_BYTES, ACC16, tw_lo, tw_hi, P::N};
         if (lane == 0 && wc == 0) SFFFT_STAMP(2, 3 * ntask);
         if (j == 0) {
           if constexpr (SH::CPG <= NCH) {
             // the whole group fits the ring: wait for all of it, then convert in one pass
             for (int c = 0; c < SH::CPG && ok; c++) {
               const long long cc = (long long)gi * SH::CPG + c;
-              if (!wait_phase(full + (int)(cc % NCH), (uint32_t)((cc / NCH) & 1), abort_flag)) ok = false;
+              const int slot = (int)(cc % NCH);
+              if (!wait_stamp_all(cstamp + slot, (int)cc, abort_flag) ||
+                  !wait_phase_all(full + slot, (uint32_t)((cc / NCH) & 1), abort_flag))
+                ok = false;
             }
             if (!ok) break;
             if (lane == 0 && wc == 0) SFFFT_STAMP(2, 3 * ntask + 1);
 #pragma unroll
             for (int c = 0; c < SH::CPG; c++) {
               const int slot = (int)(((long long)gi * SH::CPG + c) % NCH);
-              convert_chunk<P, TIO>(ops, reinterpret_cast<const TIO*>(stage + slot * SH::CHUNK), c * CE, CE, gp, ctid,
-                                    SH::WC * 32);
+              convert_chunk<P, TIO>(ops, reinterpret_cast<const TIO*>(stage + slot * SH::CHUNK), c * CE, CE, gp, ttid,
+                                    TWT);
             }
-            for (int c = 0; c < SH::CPG; c++) mbar_arrive(empty + (int)(((long long)gi * SH::CPG + c) % NCH));
+            __syncwarp();
+            if (lane == 0)
+              for (int c = 0; c < SH::CPG; c++) mbar_arrive(empty + (int)(((long long)gi * SH::CPG + c) % NCH));
           } else {
             for (int c = 0; c < SH::CPG; c++) {
               const long long cc = (long long)gi * SH::CPG + c;
               const int slot = (int)(cc % NCH);
-              if (!wait_phase(full + slot, (uint32_t)((cc / NCH) & 1), abort_flag)) { ok = false; break; }
+              if (!wait_stamp_all(cstamp + slot, (int)cc, abort_flag) ||
+                  !wait_phase_all(full + slot, (uint32_t)((cc / NCH) & 1), abort_flag)) {
+                ok = false;
+                break;
+              }
               if (c == SH::CPG - 1 && lane == 0 && wc == 0) SFFFT_STAMP(2, 3 * ntask + 1);
-              convert_chunk<P, TIO>(ops, reinterpret_cast<const TIO*>(stage + slot * SH::CHUNK), c * CE, CE, gp, ctid,
-                                    SH::WC * 32);
-              mbar_arrive(empty + slot);
+              convert_chunk<P, TIO>(ops, reinterpret_cast<const TIO*>(stage + slot * SH::CHUNK), c * CE, CE, gp, ttid,
+                                    TWT);
+              warp_arrive(empty + slot, lane);
             }
           }
           if (!ok) break;
           fence_async_smem();
           tc_fence_before();
-          mbar_arrive(a_ready + l);
+          warp_arrive(a_ready + s, lane);
           if (lane == 0 && wc == 0) SFFFT_STAMP(2, 3 * ntask + 2);
         } else {
           const int sid = j - 1;
-          if (!wait_phase(mma_done + l, md_phase[l], abort_flag)) { ok = false; break; }
-          md_phase[l] ^= 1;
+          if (!wait_phase_all(mma_done + s, (md_bits >> l) & 1u, abort_flag)) { ok = false; break; }
+          md_bits ^= 1u << l;
           if (lane == 0 && wc == 0) SFFFT_STAMP(2, 3 * ntask + 1);
           tc_fence_after();
-          EpiArgs ea{tmem + (uint32_t)(l * P::TMEM_COLS), prm.Kf, prm.y, prm.B, prm.H, group, nullptr, 0};
+          EpiArgs ea{tmem + (uint32_t)(s * P::TMEM_COLS), prm.Kf, prm.y, prm.B, prm.H, group, nullptr, 0};
           const bool kst = SH::KSLOT > 0 && sid == P::S - 1;
           constexpr int KS = SH::KSLOT > 0 ? SH::KSLOT : 1;
           const int ks = gi % KS;
           if (kst) {
-            if (!wait_phase(k_full + ks, (uint32_t)((gi / KS) & 1), abort_flag)) { ok = false; break; }
+            if (!wait_stamp_all(kstamp + ks, gi, abort_flag) ||
+                !wait_phase_all(k_full + ks, (uint32_t)((gi / KS) & 1), abort_flag)) {
+              ok = false;
+              break;
+            }
             const int hf = kinfo[ks];
             if (hf >= 0) { ea.kst = kstage + ks * SH::KC * SH::KROW; ea.khf = hf; }
           }
-          epi_any<P, TIO, ACC16>(sid, ops, ea, gp, q, wi, nwq, lane);
-          if (kst) mbar_arrive(k_empty + ks);
+          epi_any<P, TIO, ACC16>(sid, ops, ea, gp, q, wi, lane);
+          if (kst) warp_arrive(k_empty + ks, lane);
           tc_fence_before();
           if (P::S == 3 && sid == S2 - 1) {
-            // 3-stage plans stage the outputs in shared memory; all compute warps then copy them out coalesced
-            compute_bar(SH::WC * 32);
-            copy_out_staged<P, TIO>(ops, ea, gp, ctid, SH::WC * 32);
-            compute_bar(SH::WC * 32);
+            // 3-stage plans stage the outputs in shared memory; the team then copies them out coalesced
+            if (!team_sync(team_done + team, ts_phase, lane, abort_flag)) { ok = false; break; }
+            copy_out_staged<P, TIO>(ops, ea, gp, ttid, TWT);
+            if (!team_sync(team_done + team, ts_phase, lane, abort_flag)) { ok = false; break; }
           }
           if (sid < S2 - 1) {
             fence_async_smem();
-            mbar_arrive(a_ready + l);
+            warp_arrive(a_ready + s, lane);
           }
           if (lane == 0 && wc == 0) SFFFT_STAMP(2, 3 * ntask + 2);
         }

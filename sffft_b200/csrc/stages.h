@@ -11,7 +11,8 @@
 //   ops.lds8(p, v)                                           eight staged input values (TIO) -> float
 //   ops.store1(p, v) / ops.store4(p, v[4])                   output values (TIO) to global memory
 //   ops.tw(e, &re, &im)                                      w_N^e from the CTA's twiddle table
-//   ops.twiddle16(a, b, t0r, t0i, wr, wi, pr, pim)           16 complex values x t0*w^j -> fp16 pairs
+//   ops.twiddle16(a, b, t0, t8, w, pr, pim)                  16 complex values x t0*w^j (j < 8) and
+//                                                            t8*w^(j-8) (j >= 8) -> fp16 pairs
 //   ops.st4(off, v) / ops.ld4_staged(off, rot, v)            staged fp32 outputs (3-stage plans)
 //
 // Algorithm per pair (reference: sfFFT src/sffft.cu:137-280, restated for tcgen05 and pairing):
@@ -31,17 +32,21 @@ struct PairInfo {
 };
 
 // Pair bookkeeping of one group with 32-bit arithmetic: one division per group, then pair g is found
-// by stepping from the group's first pair (pairs never exceed B*H <= INT_MAX).
+// from the group's first pair (j0 < PB and g < G <= 8, so one subtraction suffices when PB >= 8);
+// 2j*H + h < B*H <= INT_MAX.
 struct GroupPairs {
   int h0, j0, PB, B, H;
   SF_HD PairInfo get(int g, int L) const {
     int j = j0 + g, h = h0;
-    while (j >= PB) { j -= PB; h++; }
+    if (j >= PB) {
+      if (PB >= 8) { j -= PB; h++; }
+      else { const int d = j / PB; j -= d * PB; h += d; }
+    }
     PairInfo pi;
     if (h >= H) { pi.off0 = pi.off1 = -1; pi.h = -1; return pi; }
     pi.h = h;
-    pi.off0 = ((long long)(2 * j) * H + h) * L;
-    pi.off1 = (2 * j + 1 < B) ? ((long long)(2 * j + 1) * H + h) * L : -1;
+    pi.off0 = (long long)(2 * j * H + h) * L;
+    pi.off1 = (2 * j + 1 < B) ? pi.off0 + (long long)H * L : -1;
     return pi;
   }
 };
@@ -176,8 +181,6 @@ SF_HD constexpr int epi_chunks() {
   return SID == 2 * P::S - 1 ? (P::R0 / 2 < 16 ? 1 : P::R0 / 32) : P::rad(SID) / 16;
 }
 
-// One epilogue unit: TMEM lane row r = t*128 + q*32 + lane of tile t, columns [16c, 16c + 16) of both
-// the real and the imaginary half.  ea.tmem is the TMEM base of the group's accumulator slot.
 // Byte offsets of the 16-byte runs (m, k) and (m + 8, k) in an MN-major 128-B-swizzled operand (m % 8 == 0).
 SF_HD void mn_off2(int m, int k, int MB, uint32_t* o0, uint32_t* o1) {
   const uint32_t kb = (uint32_t)((k >> 3) * MB) << 10;
@@ -192,62 +195,60 @@ SF_HD void mn_off2(int m, int k, int MB, uint32_t* o0, uint32_t* o1) {
 // of a warp hit 32 different banks.
 SF_HD uint32_t out_stage_word(int e) { return (uint32_t)(e ^ ((e >> 5) & 31)); }
 
-// One epilogue unit: TMEM lane row r = t*128 + q*32 + lane of tile t, columns [16c, 16c + 16) of both
-// the real and the imaginary half.  ea.tmem is the TMEM base of the group's accumulator slot.
-template <class P, class TIO, bool ACC16, int SID, class Ops>
-SF_HD void epilogue_unit(Ops& ops, const EpiArgs& ea, const GroupPairs& gp, int t, int c, int q, int lane) {
-  constexpr int S = P::S, R = P::rad(SID), N = P::N, RPP = N / R;   // rows per pair
-  constexpr bool OUT = (SID == 2 * S - 1), SPEC = (SID == S - 1);
-  constexpr float SC = (R == 16) ? 0.25f : (R == 64 ? 0.125f : 0.17677669529663687f);
-  const int r = t * 128 + q * 32 + lane, g = r / RPP, rr = r - g * RPP, c0 = 16 * c;
-  const uint32_t taddr = ea.tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(t * 2 * R + c0);
+// Per-thread indices of one epilogue unit: TMEM lane row r = t*128 + q*32 + lane of tile t, columns
+// [16c, 16c + 16) of both the real and the imaginary half of the accumulator slot at `tmem`.
+//   ta, tb   twiddle exponent e(col) = ta*col + tb of the four-step twiddle after this stage
+//   m0, kre  first M row and real-plane K row of the next stage's operand written by this thread
+//   vv       output position inside a sequence (last inverse stage)
+struct EpiIdx {
+  uint32_t taddr;
+  int g, rr, c0, ta, tb, m0, kre, vv, r;
+};
 
-  // thread-specific twiddle exponent e(col) = ta*col + tb and next-stage write target (m0, kre)
-  int ta = 0, tb = 0, m0 = 0, kre = 0, vv = 0;
+template <class P, int SID>
+SF_HD EpiIdx epi_idx(uint32_t tmem, int t, int c, int q, int lane) {
+  constexpr int S = P::S, R = P::rad(SID), N = P::N, RPP = N / R;   // rows per pair
+  EpiIdx x;
+  x.r = t * 128 + q * 32 + lane;
+  x.g = x.r / RPP;
+  x.rr = x.r - x.g * RPP;
+  x.c0 = 16 * c;
+  x.taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(t * 2 * R + x.c0);
+  x.ta = x.tb = x.m0 = x.kre = x.vv = 0;
+  const int g = x.g, rr = x.rr;
   if constexpr (SID == 0) {
-    if constexpr (S == 2) { ta = rr; m0 = g * P::R0; kre = rr; }
-    else { const int n1 = rr / P::R2, n2 = rr - n1 * P::R2; ta = rr; m0 = g * P::R0 * P::R2 + n2 * P::R0; kre = n1; }
+    if constexpr (S == 2) { x.ta = rr; x.m0 = g * P::R0; x.kre = rr; }
+    else {
+      const int n1 = rr / P::R2, n2 = rr - n1 * P::R2;
+      x.ta = rr; x.m0 = g * P::R0 * P::R2 + n2 * P::R0; x.kre = n1;
+    }
   } else if constexpr (S == 3 && SID == 1) {
     const int n2 = rr / P::R0, k0 = rr - n2 * P::R0;
-    ta = P::R0 * n2; m0 = g * P::R0 * P::R1 + k0 * P::R1; kre = n2;
+    x.ta = P::R0 * n2; x.m0 = g * P::R0 * P::R1 + k0 * P::R1; x.kre = n2;
   } else if constexpr (SID == S && S == 2) {
-    ta = -rr; m0 = g * P::R1; kre = rr;
+    x.ta = -rr; x.m0 = g * P::R1; x.kre = rr;
   } else if constexpr (SID == S && S == 3) {
-    const int k0 = rr / P::R1, k1 = rr - k0 * P::R1; ta = -P::R0 * k1; m0 = g * P::R0 * P::R2 + k0 * P::R2; kre = k1;
+    const int k0 = rr / P::R1, k1 = rr - k0 * P::R1;
+    x.ta = -P::R0 * k1; x.m0 = g * P::R0 * P::R2 + k0 * P::R2; x.kre = k1;
   } else if constexpr (S == 3 && SID == S + 1) {
     const int k0 = rr / P::R2, n2 = rr - k0 * P::R2;
-    ta = -k0 * P::R2; tb = -k0 * n2; m0 = g * P::R1 * P::R2 + n2 * P::R1; kre = k0;
-  } else if constexpr (OUT) {
-    if constexpr (S == 2) vv = rr;
-    else { const int n2 = rr / P::R1, n1 = rr - n2 * P::R1; vv = n1 * P::R2 + n2; }
+    x.ta = -k0 * P::R2; x.tb = -k0 * n2; x.m0 = g * P::R1 * P::R2 + n2 * P::R1; x.kre = k0;
+  } else if constexpr (SID == 2 * S - 1) {
+    if constexpr (S == 2) x.vv = rr;
+    else { const int n2 = rr / P::R1, n1 = rr - n2 * P::R1; x.vv = n1 * P::R2 + n2; }
   }
+  return x;
+}
 
-  float kk[32];
-  if constexpr (SPEC) {
-    const PairInfo pi = gp.get(g, P::L);
-    // an empty pair slot (past the last pair) reads any valid row; its outputs are never stored
-    if (ea.kst) {
-      const int h = pi.h < 0 ? ea.khf : pi.h;
-      const uint8_t* kb = ea.kst + (size_t)(h - ea.khf) * (N * 8);
-      for (int j = 0; j < 8; j++) {
-        float k4[4];
-        ops.ldsK(kb + kstage_off<N, R>(rr, c, j), k4);
-        kk[4 * j] = k4[0]; kk[4 * j + 1] = k4[1]; kk[4 * j + 2] = k4[2]; kk[4 * j + 3] = k4[3];
-      }
-    } else {
-      const int h = pi.h < 0 ? 0 : pi.h;
-      const float* Kp = ea.Kf + 2 * ((long long)h * N + (long long)rr * R + c0);
-      for (int j = 0; j < 16; j += 2) {
-        float k4[4];
-        ops.ldK(Kp + 2 * j, k4);
-        kk[2 * j] = k4[0]; kk[2 * j + 1] = k4[1]; kk[2 * j + 2] = k4[2]; kk[2 * j + 3] = k4[3];
-      }
-    }
-  }
-  uint32_t raw_re[16], raw_im[16];
-  ops.tmem_ld16(taddr, raw_re);
-  ops.tmem_ld16(taddr + (uint32_t)R, raw_im);
-  ops.tmem_wait();
+// Second half of an epilogue unit, after its TMEM words have arrived: scale, twiddle (or spectrum
+// multiply), round to fp16 and write the next stage's operand -- or, after the last stage, the outputs.
+template <class P, class TIO, bool ACC16, int SID, class Ops>
+SF_HD void epi_finish(Ops& ops, const EpiArgs& ea, const GroupPairs& gp, const EpiIdx& x, const uint32_t* raw_re,
+                      const uint32_t* raw_im) {
+  constexpr int S = P::S, R = P::rad(SID), N = P::N;
+  constexpr bool OUT = (SID == 2 * S - 1), SPEC = (SID == S - 1);
+  constexpr float SC = (R == 16) ? 0.25f : (R == 64 ? 0.125f : 0.17677669529663687f);
+  const int g = x.g, rr = x.rr, c0 = x.c0, r = x.r;
   float a[16], b[16];
   for (int j = 0; j < 16; j++) { a[j] = ops.acc_val(raw_re[j]); b[j] = ops.acc_val(raw_im[j]); }
 
@@ -259,8 +260,8 @@ SF_HD void epilogue_unit(Ops& ops, const EpiArgs& ea, const GroupPairs& gp, int 
       for (int j = 0; j < 16; j++) {
         const int n0 = c0 + j;
         if (n0 < P::R0 / 2) {
-          if (pi.off0 >= 0) ops.store1(y + pi.off0 + (long long)n0 * V0 + vv, a[j] * SC);
-          if (pi.off1 >= 0) ops.store1(y + pi.off1 + (long long)n0 * V0 + vv, b[j] * SC);
+          if (pi.off0 >= 0) ops.store1(y + pi.off0 + (long long)n0 * V0 + x.vv, a[j] * SC);
+          if (pi.off1 >= 0) ops.store1(y + pi.off1 + (long long)n0 * V0 + x.vv, b[j] * SC);
         }
       }
     } else {
@@ -269,7 +270,7 @@ SF_HD void epilogue_unit(Ops& ops, const EpiArgs& ea, const GroupPairs& gp, int 
       for (int j = 0; j < 16; j++) {
         const int n0 = c0 + j;
         if (n0 < P::R0 / 2) {
-          const int n = n0 * V0 + vv;
+          const int n = n0 * V0 + x.vv;
           ops.st4(out_stage_word(g * 2 * P::L + n) * 4, a[j] * SC);
           ops.st4(out_stage_word(g * 2 * P::L + P::L + n) * 4, b[j] * SC);
         }
@@ -280,12 +281,32 @@ SF_HD void epilogue_unit(Ops& ops, const EpiArgs& ea, const GroupPairs& gp, int 
 
   uint32_t pr[8], pim[8];
   if constexpr (SPEC) {
+    float kk[32];
+    const PairInfo pi = gp.get(g, P::L);
+    // an empty pair slot (past the last pair) reads any valid row; its outputs are never stored
+    if (ea.kst) {
+      const int h = pi.h < 0 ? ea.khf : pi.h;
+      const uint8_t* kb = ea.kst + (size_t)(h - ea.khf) * (N * 8);
+      for (int j = 0; j < 8; j++) {
+        float k4[4];
+        ops.ldsK(kb + kstage_off<N, R>(rr, c0 >> 4, j), k4);
+        kk[4 * j] = k4[0]; kk[4 * j + 1] = k4[1]; kk[4 * j + 2] = k4[2]; kk[4 * j + 3] = k4[3];
+      }
+    } else {
+      const int h = pi.h < 0 ? 0 : pi.h;
+      const float* Kp = ea.Kf + 2 * ((long long)h * N + (long long)rr * R + c0);
+      for (int j = 0; j < 16; j += 2) {
+        float k4[4];
+        ops.ldK(Kp + 2 * j, k4);
+        kk[2 * j] = k4[0]; kk[2 * j + 1] = k4[1]; kk[2 * j + 2] = k4[2]; kk[2 * j + 3] = k4[3];
+      }
+    }
     for (int j = 0; j < 16; j += 2) {
       float o_re[2], o_im[2];
       for (int e = 0; e < 2; e++) {
-        const float x = a[j + e] * SC, z = b[j + e] * SC;
-        o_re[e] = x * kk[2 * (j + e)] - z * kk[2 * (j + e) + 1];
-        o_im[e] = x * kk[2 * (j + e) + 1] + z * kk[2 * (j + e)];
+        const float xx = a[j + e] * SC, z = b[j + e] * SC;
+        o_re[e] = xx * kk[2 * (j + e)] - z * kk[2 * (j + e) + 1];
+        o_im[e] = xx * kk[2 * (j + e) + 1] + z * kk[2 * (j + e)];
       }
       pr[j / 2] = ops.pack2(o_re[0], o_re[1]);
       pim[j / 2] = ops.pack2(o_im[0], o_im[1]);
@@ -296,18 +317,53 @@ SF_HD void epilogue_unit(Ops& ops, const EpiArgs& ea, const GroupPairs& gp, int 
     ops.st16(kmaj_data_off(r, R + c0, R, RWS), pim[0], pim[1], pim[2], pim[3]);
     ops.st16(kmaj_data_off(r, R + c0 + 8, R, RWS), pim[4], pim[5], pim[6], pim[7]);
   } else {
-    float t0r, t0i, wr, wi;
-    ops.tw(ta * c0 + tb, &t0r, &t0i);
-    ops.tw(ta, &wr, &wi);
-    ops.twiddle16(a, b, t0r * SC, t0i * SC, wr, wi, pr, pim);
+    float t0r, t0i, t8r, t8i, wr, wi;
+    ops.tw(x.ta * c0 + x.tb, &t0r, &t0i);
+    ops.tw(x.ta * (c0 + 8) + x.tb, &t8r, &t8i);
+    ops.tw(x.ta, &wr, &wi);
+    ops.twiddle16(a, b, t0r * SC, t0i * SC, t8r * SC, t8i * SC, wr, wi, pr, pim);
     constexpr int MBn = P::MB(SID + 1), Rn = P::rad(SID + 1);
     uint32_t o0, o1;
-    mn_off2(m0 + c0, kre, MBn, &o0, &o1);
+    mn_off2(x.m0 + c0, x.kre, MBn, &o0, &o1);
     constexpr uint32_t IMOFF = (uint32_t)(Rn / 8) * MBn * 1024;   // K-row Rn + kre is Rn/8 groups further
     ops.st16(o0, pr[0], pr[1], pr[2], pr[3]);
     ops.st16(o1, pr[4], pr[5], pr[6], pr[7]);
     ops.st16(o0 + IMOFF, pim[0], pim[1], pim[2], pim[3]);
     ops.st16(o1 + IMOFF, pim[4], pim[5], pim[6], pim[7]);
+  }
+}
+
+// NU epilogue units of one thread (units u0, u0 + ustride, ...; unit u = tile u / C, chunk u % C): all
+// their TMEM loads are issued before one wait, so their latencies overlap.
+template <class P, class TIO, bool ACC16, int SID, int NU, class Ops>
+SF_HD void epilogue_units(Ops& ops, const EpiArgs& ea, const GroupPairs& gp, int u0, int ustride, int q, int lane) {
+  constexpr int C = epi_chunks<P, SID>(), R = P::rad(SID);
+  EpiIdx x[NU];
+  uint32_t rre[NU][16], rim[NU][16];
+  for (int i = 0; i < NU; i++) {
+    const int u = u0 + i * ustride, t = u / C, c = u - t * C;
+    x[i] = epi_idx<P, SID>(ea.tmem, t, c, q, lane);
+    ops.tmem_ld16(x[i].taddr, rre[i]);
+    ops.tmem_ld16(x[i].taddr + (uint32_t)R, rim[i]);
+  }
+  ops.tmem_wait();
+  for (int i = 0; i < NU; i++) epi_finish<P, TIO, ACC16, SID>(ops, ea, gp, x[i], rre[i], rim[i]);
+}
+
+// The units of stage SID that one thread handles: its warp covers TMEM lane quarter q (warp % 4) and,
+// being warp wi of the team's NWQ warps on that quarter, units wi, wi + NWQ, ...  With two warps per
+// quarter, units are taken in pairs so that two units' TMEM loads are in flight together.
+template <class P, class TIO, bool ACC16, int SID, class Ops>
+SF_HD void epi_warp(Ops& ops, const EpiArgs& ea, const GroupPairs& gp, int wi, int q, int lane) {
+  constexpr int NWQ = Shape<P, (int)sizeof(TIO)>::NWQ;
+  constexpr int C = epi_chunks<P, SID>(), U = P::tiles(SID) * C;
+  constexpr int NU = (NWQ == 2 && U % (2 * NWQ) == 0) ? 2 : 1;
+  if constexpr (U % (NU * NWQ) == 0) {
+#pragma unroll 1
+    for (int i = 0; i < U / NWQ; i += NU) epilogue_units<P, TIO, ACC16, SID, NU>(ops, ea, gp, wi + i * NWQ, NWQ, q, lane);
+  } else {
+#pragma unroll 1
+    for (int u = wi; u < U; u += NWQ) epilogue_units<P, TIO, ACC16, SID, 1>(ops, ea, gp, u, NWQ, q, lane);
   }
 }
 
