@@ -71,7 +71,7 @@ static const char* default_for(int L) {
     case 1024: return "64x32/w8";
     case 2048: return "64x64/w8";
     case 4096: return "32x16x16/w8";
-    case 8192: return "32x32x16/w4";
+    case 8192: return "32x32x16/w8";
     case 16384: return "32x32x32/w8";
     default: return nullptr;
   }

@@ -240,15 +240,38 @@ SF_HD EpiIdx epi_idx(uint32_t tmem, int t, int c, int q, int lane) {
   return x;
 }
 
+// Spectrum values of the 16 columns [c0, c0 + 16) of row rr for channel h (complex, re/im interleaved),
+// from the loader's staged rows when the group's channels are staged, else from Kf in global memory.
+// An empty pair slot (h < 0, past the last pair) reads any valid row; its outputs are never stored.
+template <class P, int SID, class Ops>
+SF_HD void load_spec(Ops& ops, const EpiArgs& ea, int h, int rr, int c0, float* kk) {
+  constexpr int R = P::rad(SID), N = P::N;
+  if (ea.kst) {
+    const uint8_t* kb = ea.kst + (size_t)((h < 0 ? ea.khf : h) - ea.khf) * (N * 8);
+    for (int j = 0; j < 8; j++) {
+      float k4[4];
+      ops.ldsK(kb + kstage_off<N, R>(rr, c0 >> 4, j), k4);
+      kk[4 * j] = k4[0]; kk[4 * j + 1] = k4[1]; kk[4 * j + 2] = k4[2]; kk[4 * j + 3] = k4[3];
+    }
+  } else {
+    const float* Kp = ea.Kf + 2 * ((long long)(h < 0 ? 0 : h) * N + (long long)rr * R + c0);
+    for (int j = 0; j < 16; j += 2) {
+      float k4[4];
+      ops.ldK(Kp + 2 * j, k4);
+      kk[2 * j] = k4[0]; kk[2 * j + 1] = k4[1]; kk[2 * j + 2] = k4[2]; kk[2 * j + 3] = k4[3];
+    }
+  }
+}
+
 // Second half of an epilogue unit, after its TMEM words have arrived: scale, twiddle (or spectrum
 // multiply), round to fp16 and write the next stage's operand -- or, after the last stage, the outputs.
 template <class P, class TIO, bool ACC16, int SID, class Ops>
 SF_HD void epi_finish(Ops& ops, const EpiArgs& ea, const GroupPairs& gp, const EpiIdx& x, const uint32_t* raw_re,
-                      const uint32_t* raw_im) {
+                      const uint32_t* raw_im, const float* kk) {
   constexpr int S = P::S, R = P::rad(SID), N = P::N;
   constexpr bool OUT = (SID == 2 * S - 1), SPEC = (SID == S - 1);
   constexpr float SC = (R == 16) ? 0.25f : (R == 64 ? 0.125f : 0.17677669529663687f);
-  const int g = x.g, rr = x.rr, c0 = x.c0, r = x.r;
+  const int g = x.g, c0 = x.c0, r = x.r;
   float a[16], b[16];
   for (int j = 0; j < 16; j++) { a[j] = ops.acc_val(raw_re[j]); b[j] = ops.acc_val(raw_im[j]); }
 
@@ -281,26 +304,6 @@ SF_HD void epi_finish(Ops& ops, const EpiArgs& ea, const GroupPairs& gp, const E
 
   uint32_t pr[8], pim[8];
   if constexpr (SPEC) {
-    float kk[32];
-    const PairInfo pi = gp.get(g, P::L);
-    // an empty pair slot (past the last pair) reads any valid row; its outputs are never stored
-    if (ea.kst) {
-      const int h = pi.h < 0 ? ea.khf : pi.h;
-      const uint8_t* kb = ea.kst + (size_t)(h - ea.khf) * (N * 8);
-      for (int j = 0; j < 8; j++) {
-        float k4[4];
-        ops.ldsK(kb + kstage_off<N, R>(rr, c0 >> 4, j), k4);
-        kk[4 * j] = k4[0]; kk[4 * j + 1] = k4[1]; kk[4 * j + 2] = k4[2]; kk[4 * j + 3] = k4[3];
-      }
-    } else {
-      const int h = pi.h < 0 ? 0 : pi.h;
-      const float* Kp = ea.Kf + 2 * ((long long)h * N + (long long)rr * R + c0);
-      for (int j = 0; j < 16; j += 2) {
-        float k4[4];
-        ops.ldK(Kp + 2 * j, k4);
-        kk[2 * j] = k4[0]; kk[2 * j + 1] = k4[1]; kk[2 * j + 2] = k4[2]; kk[2 * j + 3] = k4[3];
-      }
-    }
     for (int j = 0; j < 16; j += 2) {
       float o_re[2], o_im[2];
       for (int e = 0; e < 2; e++) {
@@ -334,31 +337,74 @@ SF_HD void epi_finish(Ops& ops, const EpiArgs& ea, const GroupPairs& gp, const E
 }
 
 // NU epilogue units of one thread (units u0, u0 + ustride, ...; unit u = tile u / C, chunk u % C): all
-// their TMEM loads are issued before one wait, so their latencies overlap.
+// their TMEM loads (and, in the spectrum stage, their spectrum loads) are issued before one wait, so
+// their latencies overlap.
 template <class P, class TIO, bool ACC16, int SID, int NU, class Ops>
 SF_HD void epilogue_units(Ops& ops, const EpiArgs& ea, const GroupPairs& gp, int u0, int ustride, int q, int lane) {
   constexpr int C = epi_chunks<P, SID>(), R = P::rad(SID);
+  constexpr bool SPEC = SID == P::S - 1;
+  // spectrum loads ahead of the wait only where registers allow (4-warp plans: 184 per thread; the
+  // 8-warp plans' ~95 would spill)
+  constexpr bool EARLY = SPEC && P::W == 4;
   EpiIdx x[NU];
   uint32_t rre[NU][16], rim[NU][16];
+  float kk[SPEC ? NU : 1][SPEC ? 32 : 1];
   for (int i = 0; i < NU; i++) {
     const int u = u0 + i * ustride, t = u / C, c = u - t * C;
     x[i] = epi_idx<P, SID>(ea.tmem, t, c, q, lane);
     ops.tmem_ld16(x[i].taddr, rre[i]);
     ops.tmem_ld16(x[i].taddr + (uint32_t)R, rim[i]);
+    if constexpr (EARLY) load_spec<P, SID>(ops, ea, gp.get(x[i].g, P::L).h, x[i].rr, x[i].c0, kk[i]);
   }
   ops.tmem_wait();
-  for (int i = 0; i < NU; i++) epi_finish<P, TIO, ACC16, SID>(ops, ea, gp, x[i], rre[i], rim[i]);
+  for (int i = 0; i < NU; i++) {
+    if constexpr (SPEC && !EARLY) load_spec<P, SID>(ops, ea, gp.get(x[i].g, P::L).h, x[i].rr, x[i].c0, kk[i]);
+    epi_finish<P, TIO, ACC16, SID>(ops, ea, gp, x[i], rre[i], rim[i], kk[SPEC ? i : 0]);
+  }
+}
+
+// Spectrum stage of a 2-stage plan on a team with one warp per lane quarter: a pair has N / R1 <= 128 rows
+// (a divisor of 128), so the warp's rows in tiles t and t + 1 have the same row index rr and read the same
+// spectrum values whenever their pairs share a channel -- loaded once per chunk and channel (used by the
+// 4-warp plans, whose register budget holds the values across tiles).
+template <class P, class TIO, bool ACC16, int SID, class Ops>
+SF_HD void epi_spec_shared(Ops& ops, const EpiArgs& ea, const GroupPairs& gp, int q, int lane) {
+  constexpr int C = epi_chunks<P, SID>(), R = P::rad(SID), T = P::tiles(SID);
+  static_assert(128 % (P::N / R) == 0, "a pair's rows divide a tile");
+#pragma unroll 1
+  for (int c = 0; c < C; c++) {
+    float kk[32];
+    int kh = -2;
+#pragma unroll 1
+    for (int t = 0; t < T; t++) {
+      const EpiIdx x = epi_idx<P, SID>(ea.tmem, t, c, q, lane);
+      uint32_t rre[16], rim[16];
+      ops.tmem_ld16(x.taddr, rre);
+      ops.tmem_ld16(x.taddr + (uint32_t)R, rim);
+      const int h = gp.get(x.g, P::L).h;
+      if (h != kh) {
+        load_spec<P, SID>(ops, ea, h, x.rr, x.c0, kk);
+        kh = h;
+      }
+      ops.tmem_wait();
+      epi_finish<P, TIO, ACC16, SID>(ops, ea, gp, x, rre, rim, kk);
+    }
+  }
 }
 
 // The units of stage SID that one thread handles: its warp covers TMEM lane quarter q (warp % 4) and,
 // being warp wi of the team's NWQ warps on that quarter, units wi, wi + NWQ, ...  With two warps per
-// quarter, units are taken in pairs so that two units' TMEM loads are in flight together.
+// quarter on a 4-warp plan (registers to spare), units are taken in pairs so that two units' TMEM loads
+// are in flight together.
 template <class P, class TIO, bool ACC16, int SID, class Ops>
 SF_HD void epi_warp(Ops& ops, const EpiArgs& ea, const GroupPairs& gp, int wi, int q, int lane) {
   constexpr int NWQ = Shape<P, (int)sizeof(TIO)>::NWQ;
   constexpr int C = epi_chunks<P, SID>(), U = P::tiles(SID) * C;
-  constexpr int NU = (NWQ == 2 && U % (2 * NWQ) == 0) ? 2 : 1;
-  if constexpr (U % (NU * NWQ) == 0) {
+  constexpr bool SPEC = SID == P::S - 1;
+  constexpr int NU = (NWQ == 2 && P::W == 4 && !SPEC && U % (2 * NWQ) == 0) ? 2 : 1;
+  if constexpr (SPEC && P::S == 2 && NWQ == 1 && P::W == 4) {
+    epi_spec_shared<P, TIO, ACC16, SID>(ops, ea, gp, q, lane);
+  } else if constexpr (U % (NU * NWQ) == 0) {
 #pragma unroll 1
     for (int i = 0; i < U / NWQ; i += NU) epilogue_units<P, TIO, ACC16, SID, NU>(ops, ea, gp, wi + i * NWQ, NWQ, q, lane);
   } else {
