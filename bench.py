@@ -149,7 +149,9 @@ def cpu_baseline_run(args, budget_s=15.0):
     total = B * H
     # size the sample to roughly budget_s of work from a short calibration
     t0 = time.perf_counter()
-    oracle.direct_conv_seqs(u, k, np.arange(min(64, total)))
+    # every host core this process may use (launchers such as torchrun set OMP_NUM_THREADS=1 per rank)
+    cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+    oracle.direct_conv_seqs(u, k, np.arange(min(64, total)), threads=cores)
     per_seq = (time.perf_counter() - t0) / min(64, total)
     n = int(max(64, min(total, budget_s / max(per_seq, 1e-9))))
     seqs = np.linspace(0, total - 1, n).astype(np.int64)
@@ -157,14 +159,14 @@ def cpu_baseline_run(args, budget_s=15.0):
     reps = 0
     t0 = time.perf_counter()
     while True:
-        oracle.direct_conv_seqs(u, k, seqs)
+        oracle.direct_conv_seqs(u, k, seqs, threads=cores)
         reps += 1
         dt = time.perf_counter() - t0
         if n < total or dt >= budget_s or reps >= 10000:
             break
     ms_batch = dt * 1e3 * total / (n * reps)
     what = f"{n} of {total} sequences" if n < total else f"the full batch of {total} sequences x {reps}"
-    return ms_batch, {"cores": oracle.max_threads(), "sample": f"{what} (B={B} H={H} L={L}), fp64 direct causal "
+    return ms_batch, {"cores": cores, "sample": f"{what} (B={B} H={H} L={L}), fp64 direct causal "
                       f"convolution, {dt:.1f} s, scaled to ms per batch", "seconds": round(dt, 2)}
 
 
