@@ -115,8 +115,15 @@ struct HostOps {
     if (b < kst_lo || b + 16 > kst_hi) throw std::out_of_range("staged spectrum read outside the staged rows");
     std::memcpy(k, p, 16);
   }
-  void lds8(const float* p, float* v) { for (int e = 0; e < 8; e++) v[e] = p[e]; }
-  void lds8(const uint16_t* p, float* v) {
+  const uint8_t* in_lo = nullptr;   // the launch's input u (direct global reads must stay inside)
+  const uint8_t* in_hi = nullptr;
+  void check_in(const void* p, size_t n) const {
+    const uint8_t* b = (const uint8_t*)p;
+    if (in_lo && (b < in_lo || b + n > in_hi)) throw std::out_of_range("input read outside u");
+  }
+  void ldg8(const float* p, float* v) { check_in(p, 32); for (int e = 0; e < 8; e++) v[e] = p[e]; }
+  void ldg8(const uint16_t* p, float* v) {
+    check_in(p, 16);
     for (int e = 0; e < 8; e++) { uint32_t b = (uint32_t)p[e] << 16; std::memcpy(&v[e], &b, 4); }
   }
   void store1(float* p, float v) { *p = v; }
@@ -177,8 +184,8 @@ void run_stage_emu(HostOps& ops, const EpiArgs& ea, const GroupPairs& gp, uint32
   if constexpr (SID + 1 < 2 * P::S) run_stage_emu<SID + 1, P, TIO, ACC16>(ops, ea, gp, data_s, bmat_s);
 }
 
-// Emulates the persistent kernel's per-group flow: the producer's staging of each chunk of the group's
-// input stream (absent sequences are not copied), conversion, then the 2S stages, alternating between
+// Emulates the persistent kernel's per-group flow: the team's conversion of the group's input (read
+// directly from u, with the kernel's thread count and load batching), then the 2S stages, cycling through
 // the kernel's data / TMEM slots.
 template <class P, class TIO, bool ACC16>
 int run_plan(const void* u, const float* Kf, void* y, int B, int H) {
@@ -186,33 +193,20 @@ int run_plan(const void* u, const float* Kf, void* y, int B, int H) {
   const int PB = (B + 1) / 2;
   const long long pairs = (long long)PB * H;
   const int ngroups = (int)((pairs + P::G - 1) / P::G);
-  std::vector<uint8_t> smem(SH::STAGE_OFF, 0);
+  std::vector<uint8_t> smem(SH::K_OFF, 0);
   std::vector<uint32_t> tmem(128 * 512, 0);
   hostmath::build_bmat_image<P>(smem.data());
-  std::vector<uint8_t> chunk(SH::CHUNK);
   std::vector<uint8_t> kst;
-  constexpr int SEQB = P::L * (int)sizeof(TIO);
   const TIO* uu = (const TIO*)u;
   for (int group = 0; group < ngroups; group++) {
     const int slot = group % SH::NSLOT;
     const uint32_t dbase = (uint32_t)(SH::DATA_OFF + slot * P::DATA_BYTES);
-    HostOps ops{&smem, dbase, &tmem, 0, ACC16, SH::TMEM_ALLOC, (size_t)P::DATA_BYTES, nullptr, nullptr, P::N};
+    HostOps ops{&smem, dbase, &tmem, 0, ACC16, SH::TMEM_ALLOC, (size_t)P::DATA_BYTES, nullptr, nullptr, nullptr, nullptr, P::N};
+    ops.in_lo = (const uint8_t*)u;
+    ops.in_hi = (const uint8_t*)u + (size_t)B * H * P::L * sizeof(TIO);
     const GroupPairs gp = group_pairs(group, P::G, B, H);
     std::memset(smem.data() + dbase, 0xFF, P::DATA_BYTES);   // poison: stale data must never be read
-    for (int c = 0; c < SH::CPG; c++) {
-      std::memset(chunk.data(), 0xEE, chunk.size());
-      const long long b0 = (long long)c * SH::CHUNK;
-      for (long long b = b0; b < b0 + SH::CHUNK; b += (SEQB < SH::CHUNK ? SEQB : SH::CHUNK)) {
-        const int j = (int)(b / SEQB);
-        const PairInfo pi = gp.get(j >> 1, P::L);
-        const long long off = (j & 1) ? pi.off1 : pi.off0;
-        const int len = SEQB < SH::CHUNK ? SEQB : SH::CHUNK;
-        if (off >= 0) std::memcpy(chunk.data() + (b - b0), uu + off + (b - (long long)j * SEQB) / (int)sizeof(TIO), len);
-      }
-      for (int tid = 0; tid < 64; tid++)
-        convert_chunk<P, TIO>(ops, (const TIO*)chunk.data(), c * (SH::CHUNK / (int)sizeof(TIO)),
-                              SH::CHUNK / (int)sizeof(TIO), gp, tid, 64);
-    }
+    for (int tid = 0; tid < SH::TWARPS * 32; tid++) convert_group<P, TIO, SH::NB>(ops, uu, gp, tid, SH::TWARPS * 32);
     EpiArgs ea{(uint32_t)(slot * P::TMEM_COLS), Kf, y, B, H, group, nullptr, 0};
     // the loader warp's staging of the group's spectrum rows (same swizzle as the device)
     if constexpr (SH::KSLOT > 0) {

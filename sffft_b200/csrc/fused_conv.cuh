@@ -2,22 +2,22 @@
 //
 // Replaces the reference kernel fftconv<Plan,W,TIO,TAcc,CACHED> (sfFFT src/sffft.cu:243-280): the same
 // four-step transform, spectrum multiply and inverse, but one CTA per SM loops over "groups" of G pairs of
-// sequences (two batch elements of one channel per pair) with three roles:
+// sequences (two batch elements of one channel per pair) with four roles:
 //
-//   warp 0 (producer)  streams each group's raw u into a shared-memory staging ring with 1-D bulk
-//                      copies (cp.async.bulk, completion through mbarrier transaction counts) and
-//                      prefetches the group's spectrum rows into L2;
-//   warp 1 (MMA)       allocates TMEM and, for every stage of every group, issues the stage's
-//                      tcgen05.mma's once the compute warps have written its A operand, then commits to
-//                      that group's "stage done" mbarrier;
-//   warps 2.. (compute) convert staged u to the first-stage operand (fp16 hi + lo) and run every stage's
-//                      epilogue: TMEM -> registers -> twiddle / spectrum / scale -> the next stage's operand
-//                      in shared memory (or y in global memory).
+//   warp 0 (prefetch)  brings each group's input sequences and spectrum rows into L2 (bulk prefetches), a
+//                      few groups ahead of the conversions;
+//   warp 1 (MMA)       allocates TMEM and issues each stage's tcgen05.mma's as soon as a team has written
+//                      that slot's A operand, then commits to the slot's "stage done" mbarrier;
+//   warp 2 (spectrum)  stages each group's spectrum rows in shared memory, swizzled for the epilogue;
+//   warps 3.. (compute) in teams of four or more (one warp per TMEM lane quarter): each team owns slots
+//                      (a data buffer and a TMEM region each, one group in flight per slot), converts its
+//                      groups' u (read straight from global memory) to the first-stage operand (fp16 hi +
+//                      lo) and runs every stage's epilogue: TMEM -> registers -> twiddle / spectrum / scale
+//                      -> the next stage's operand in shared memory (or y in global memory).
 //
-// Two groups are in flight when their data buffers and TMEM regions fit ("slots"); the compute warps
-// alternate between them, so while they finish one group's stage the tensor core runs the other's.
-// Every wait is bounded: after kWaitLimitNs a role records SFFFT_ERR_TIMEOUT in *status, raises a shared
-// abort flag that ends the other roles' loops, drains its own bulk copies and the CTA frees its TMEM.
+// Teams run independently, so one team's waits on its MMAs are covered by the others' epilogues.  Every
+// wait is bounded: after kWaitLimitNs a role records SFFFT_ERR_TIMEOUT in *status, raises a shared abort
+// flag that ends the other roles' loops, and the CTA frees its TMEM.
 #pragma once
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -82,12 +82,13 @@ struct DevOps {
     const float4 v = __ldg(reinterpret_cast<const float4*>(p));
     k[0] = v.x; k[1] = v.y; k[2] = v.z; k[3] = v.w;
   }
-  __device__ __forceinline__ void lds8(const float* p, float* v) {
-    const float4 a = reinterpret_cast<const float4*>(p)[0], b = reinterpret_cast<const float4*>(p)[1];
+  // eight input values from global memory (read-only for the whole launch)
+  __device__ __forceinline__ void ldg8(const float* p, float* v) {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(p)), b = __ldg(reinterpret_cast<const float4*>(p) + 1);
     v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
   }
-  __device__ __forceinline__ void lds8(const __nv_bfloat16* p, float* v) {
-    const uint4 q = *reinterpret_cast<const uint4*>(p);
+  __device__ __forceinline__ void ldg8(const __nv_bfloat16* p, float* v) {
+    const uint4 q = __ldg(reinterpret_cast<const uint4*>(p));
     const uint32_t w[4] = {q.x, q.y, q.z, q.w};
     for (int e = 0; e < 4; e++) { v[2 * e] = bf16_bits_to_float(w[e] & 0xFFFFu); v[2 * e + 1] = bf16_bits_to_float(w[e] >> 16); }
   }
@@ -163,16 +164,17 @@ struct ConvParams {
   int B, H;
   int ngroups;           // ceil(pairs / G), pairs = ceil(B/2) * H
 #ifdef SFFFT_TRACE
-  unsigned long long* trace;   // debug builds only: [grid][3 roles][kTraceLen] SM clock stamps
+  unsigned long long* trace;   // debug builds only: [grid][kTraceRoles][kTraceLen] SM clock stamps
 #endif
 };
 
 #ifdef SFFFT_TRACE
-constexpr int kTraceLen = 2048;
+// roles: 0 producer, 1 MMA issuer, 2 + t compute team t (its first warp's lane 0)
+constexpr int kTraceLen = 2048, kTraceRoles = 8;
 #define SFFFT_STAMP(role, idx)                                                                         \
   do {                                                                                                 \
     if (prm.trace && (idx) < kTraceLen)                                                                \
-      prm.trace[((size_t)blockIdx.x * 3 + (role)) * kTraceLen + (idx)] = clock64();                    \
+      prm.trace[((size_t)blockIdx.x * kTraceRoles + (role)) * kTraceLen + (idx)] = clock64();          \
   } while (0)
 #else
 #define SFFFT_STAMP(role, idx) \
@@ -183,15 +185,6 @@ constexpr int kTraceLen = 2048;
 // ---- extra PTX used only by the persistent kernel ----
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                   smem_u32(dst)),
-               "l"(src), "r"(bytes), "r"(smem_u32(bar))
-               : "memory");
 }
 __device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
@@ -293,17 +286,12 @@ __device__ __forceinline__ bool team_sync(uint64_t* bar, uint32_t& phase, int la
 template <class P, class TIO, bool ACC16>
 __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kernel(ConvParams prm) {
   using SH = Shape<P, sizeof(TIO)>;
-  constexpr int S2 = 2 * P::S, TPG = SH::TPG, NS = SH::NS, NCH = SH::NCH;
-  constexpr int CE = SH::CHUNK / (int)sizeof(TIO);               // elements per chunk
-  constexpr int SEQB = P::L * (int)sizeof(TIO);                   // bytes per sequence
+  constexpr int S2 = 2 * P::S, TPG = SH::TPG, NS = SH::NS;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* bmat = sm;
-  uint8_t* stage = sm + SH::STAGE_OFF;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + SH::BAR_OFF);
-  uint64_t* full = bars;                       // [NCH] staged chunk landed
-  uint64_t* empty = bars + NCH;                // [NCH] staged chunk consumed
-  uint64_t* a_ready = bars + 2 * NCH;          // [NS]  a team wrote a stage operand of this slot
+  uint64_t* a_ready = bars;                    // [NS]  a team wrote a stage operand of this slot
   uint64_t* mma_done = a_ready + NS;           // [NS]  a stage's MMAs of this slot completed
   uint64_t* k_full = mma_done + NS;            // [2]   spectrum rows staged
   uint64_t* k_empty = k_full + 2;              // [2]   staged spectrum consumed
@@ -311,8 +299,8 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
   volatile int* abort_flag = reinterpret_cast<volatile int*>(k_empty + 3);
   int* kinfo = reinterpret_cast<int*>(k_empty + 4);   // [2] first staged channel, or -1
   uint64_t* team_done = k_empty + 5;           // [NTEAM] a team's warps staged their outputs / copied them out
-  volatile int* cstamp = reinterpret_cast<volatile int*>(team_done + SH::NTEAM);   // [NCH] chunk being filled
-  volatile int* kstamp = cstamp + NCH;         // [2] group whose spectrum rows are being staged
+  volatile int* kstamp = reinterpret_cast<volatile int*>(team_done + SH::NTEAM);   // [2] group being staged
+  volatile int* conv_done = kstamp + 2;        // groups whose input has been converted
   uint8_t* kstage = sm + SH::K_OFF;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -321,12 +309,11 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
   if (warp == 1) { tmem_alloc(tmem_slot, SH::TMEM_ALLOC); tmem_relinquish(); }
   if (tid == 0) {
     // consumer barriers count one arrival per warp of the consuming team
-    for (int i = 0; i < NCH; i++) { mbar_init(full + i, 1); mbar_init(empty + i, SH::TWARPS); }
     for (int s = 0; s < NS; s++) { mbar_init(a_ready + s, SH::TWARPS); mbar_init(mma_done + s, 1); }
     for (int l = 0; l < 2; l++) { mbar_init(k_full + l, 32); mbar_init(k_empty + l, SH::TWARPS); }
     for (int t = 0; t < SH::NTEAM; t++) mbar_init(team_done + t, SH::TWARPS);
-    for (int i = 0; i < NCH; i++) cstamp[i] = -1;
     kstamp[0] = kstamp[1] = -1;
+    *conv_done = 0;
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -356,65 +343,24 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
   const TIO* u = reinterpret_cast<const TIO*>(prm.u);
 
   if (warp == 0) {
-    // ---------------- producer ----------------
-    // A chunk holds one piece of a sequence or several whole sequences; each piece is one bulk copy,
-    // issued by its own lane so the warp issues a chunk's copies together.
-    constexpr int NP = SEQB >= SH::CHUNK ? 1 : SH::CHUNK / SEQB;
-    static_assert(NP <= 32, "one copy per producer lane");
-    long long cc = 0;
-    bool run = true;
-    for (int gi = 0; gi < ni && run; gi++) {
+    // ---------------- L2 prefetcher ----------------
+    // Brings each group's 2G input sequences (one bulk prefetch per sequence, one lane each) and spectrum
+    // rows into L2, at most PD groups ahead of the conversions, so a team's direct loads hit L2.
+    for (int gi = 0; gi < ni; gi++) {
+      if (gi >= SH::PD && !wait_stamp_all(conv_done, gi - SH::PD + 1, abort_flag)) break;
+      if (lane == 0) SFFFT_STAMP(0, 3 * gi);
       const int group = (int)blockIdx.x + gi * (int)gridDim.x;
       const GroupPairs gp = group_pairs(group, P::G, prm.B, prm.H);
+      if (lane < 2 * P::G) {
+        const PairInfo pi = gp.get(lane >> 1, P::L);
+        const long long off = (lane & 1) ? pi.off1 : pi.off0;
+        if (off >= 0) prefetch_l2(u + off, (uint32_t)SH::SEQB);
+      }
       if (lane == 0) {
         const PairInfo a = gp.get(0, P::L), b = gp.get(P::G - 1, P::L);
         if (a.h >= 0) prefetch_l2(prm.Kf + 2ll * a.h * P::N, P::N * 8);
         if (b.h >= 0 && b.h != a.h) prefetch_l2(prm.Kf + 2ll * b.h * P::N, P::N * 8);
-      }
-      for (int c = 0; c < SH::CPG; c++, cc++) {
-        const int slot = (int)(cc % NCH);
-        const long long use = cc / NCH;
-        if (lane == 0) SFFFT_STAMP(0, (int)(3 * cc));
-        if (use > 0) {
-          if (!wait_phase_all(empty + slot, (uint32_t)((use - 1) & 1), abort_flag)) { run = false; break; }
-        }
-        if (lane == 0) cstamp[slot] = (int)cc;
-        if (lane == 0) SFFFT_STAMP(0, (int)(3 * cc + 1));
-        // stream bytes [c*CHUNK, (c+1)*CHUNK) of the group's 2G sequences
-        const long long b0 = (long long)c * SH::CHUNK;
-        uint32_t bytes = 0;
-        const TIO* src = nullptr;
-        uint8_t* dst = stage + slot * SH::CHUNK;
-        if (lane < NP) {
-          const int j = (int)(b0 / SEQB) + lane;
-          const PairInfo pi = gp.get(j >> 1, P::L);
-          const long long off = (j & 1) ? pi.off1 : pi.off0;
-          if (off >= 0) {
-            if (NP == 1) {
-              bytes = SH::CHUNK;
-              src = u + off + (b0 - (long long)j * SEQB) / (int)sizeof(TIO);
-            } else {
-              bytes = SEQB;
-              src = u + off;
-              dst += lane * SEQB;
-            }
-          }
-        }
-        const uint32_t total = __reduce_add_sync(0xffffffffu, bytes);
-        if (lane == 0) mbar_arrive_expect_tx(full + slot, total);
-        __syncwarp();
-        if (bytes) bulk_g2s(dst, src, bytes, full + slot);
-        if (lane == 0) SFFFT_STAMP(0, (int)(3 * cc + 2));
-      }
-    }
-    // drain: every issued copy has landed before the CTA can exit
-    if (lane == 0) {
-      const long long first = cc > NCH ? cc - NCH : 0;
-      for (long long d = first; d < cc; d++) {
-        const int slot = (int)(d % NCH);
-        const uint64_t t0 = global_ns();
-        while (!mbar_try_wait(full + slot, (uint32_t)((d / NCH) & 1)) && global_ns() - t0 < kWaitLimitNs) {
-        }
+        SFFFT_STAMP(0, 3 * gi + 1);
       }
     }
   } else if (warp == 1) {
@@ -546,53 +492,20 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
         if (j == 0) gps[l] = group_pairs(group, P::G, prm.B, prm.H);
         const GroupPairs gp = gps[l];
         DevOps ops{sm + SH::DATA_OFF + s * P::DATA_BYTES, ACC16, tw_lo, tw_hi, P::N};
-        if (lane == 0 && wc == 0) SFFFT_STAMP(2, 3 * ntask);
+        if (lane == 0 && wt == 0) SFFFT_STAMP(2 + team, 3 * ntask);
         if (j == 0) {
-          if constexpr (SH::CPG <= NCH) {
-            // the whole group fits the ring: wait for all of it, then convert in one pass
-            for (int c = 0; c < SH::CPG && ok; c++) {
-              const long long cc = (long long)gi * SH::CPG + c;
-              const int slot = (int)(cc % NCH);
-              if (!wait_stamp_all(cstamp + slot, (int)cc, abort_flag) ||
-                  !wait_phase_all(full + slot, (uint32_t)((cc / NCH) & 1), abort_flag))
-                ok = false;
-            }
-            if (!ok) break;
-            if (lane == 0 && wc == 0) SFFFT_STAMP(2, 3 * ntask + 1);
-#pragma unroll
-            for (int c = 0; c < SH::CPG; c++) {
-              const int slot = (int)(((long long)gi * SH::CPG + c) % NCH);
-              convert_chunk<P, TIO>(ops, reinterpret_cast<const TIO*>(stage + slot * SH::CHUNK), c * CE, CE, gp, ttid,
-                                    TWT);
-            }
-            __syncwarp();
-            if (lane == 0)
-              for (int c = 0; c < SH::CPG; c++) mbar_arrive(empty + (int)(((long long)gi * SH::CPG + c) % NCH));
-          } else {
-            for (int c = 0; c < SH::CPG; c++) {
-              const long long cc = (long long)gi * SH::CPG + c;
-              const int slot = (int)(cc % NCH);
-              if (!wait_stamp_all(cstamp + slot, (int)cc, abort_flag) ||
-                  !wait_phase_all(full + slot, (uint32_t)((cc / NCH) & 1), abort_flag)) {
-                ok = false;
-                break;
-              }
-              if (c == SH::CPG - 1 && lane == 0 && wc == 0) SFFFT_STAMP(2, 3 * ntask + 1);
-              convert_chunk<P, TIO>(ops, reinterpret_cast<const TIO*>(stage + slot * SH::CHUNK), c * CE, CE, gp, ttid,
-                                    TWT);
-              warp_arrive(empty + slot, lane);
-            }
-          }
-          if (!ok) break;
+          convert_group<P, TIO, SH::NB>(ops, u, gp, ttid, TWT);
+          if (lane == 0 && wt == 0) SFFFT_STAMP(2 + team, 3 * ntask + 1);
           fence_async_smem();
           tc_fence_before();
           warp_arrive(a_ready + s, lane);
-          if (lane == 0 && wc == 0) SFFFT_STAMP(2, 3 * ntask + 2);
+          if (lane == 0 && wt == 0) atomicAdd((int*)conv_done, 1);
+          if (lane == 0 && wt == 0) SFFFT_STAMP(2 + team, 3 * ntask + 2);
         } else {
           const int sid = j - 1;
           if (!wait_phase_all(mma_done + s, (md_bits >> l) & 1u, abort_flag)) { ok = false; break; }
           md_bits ^= 1u << l;
-          if (lane == 0 && wc == 0) SFFFT_STAMP(2, 3 * ntask + 1);
+          if (lane == 0 && wt == 0) SFFFT_STAMP(2 + team, 3 * ntask + 1);
           tc_fence_after();
           EpiArgs ea{tmem + (uint32_t)(s * P::TMEM_COLS), prm.Kf, prm.y, prm.B, prm.H, group, nullptr, 0};
           const bool kst = SH::KSLOT > 0 && sid == P::S - 1;
@@ -620,7 +533,7 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
             fence_async_smem();
             warp_arrive(a_ready + s, lane);
           }
-          if (lane == 0 && wc == 0) SFFFT_STAMP(2, 3 * ntask + 2);
+          if (lane == 0 && wt == 0) SFFFT_STAMP(2 + team, 3 * ntask + 2);
         }
         ntask++;
       }

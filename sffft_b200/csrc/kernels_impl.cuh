@@ -26,7 +26,7 @@ ConvEntry make_entry(const char* name) {
   e.smem_bytes[0] = S4::SMEM; e.smem_bytes[1] = S2::SMEM;
   e.tmem_cols[0] = S4::TMEM_ALLOC; e.tmem_cols[1] = S2::TMEM_ALLOC;
   e.slots[0] = S4::NSLOT; e.slots[1] = S2::NSLOT;
-  e.stage_chunks[0] = S4::NCH; e.stage_chunks[1] = S2::NCH;
+  e.kslots[0] = S4::KSLOT; e.kslots[1] = S2::KSLOT;
   e.launch[0][0] = &launch_conv<P, float, false>;
   e.launch[0][1] = &launch_conv<P, float, true>;
   e.launch[1][0] = &launch_conv<P, __nv_bfloat16, false>;

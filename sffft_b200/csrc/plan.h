@@ -125,40 +125,33 @@ struct Plan {
 };
 
 // Resources of the persistent kernel for plan P and I/O element size SIO:
-//   1 producer warp (bulk copies of u into a staging ring), 1 MMA warp, 1 spectrum-loader warp, and
+//   1 L2-prefetch warp (a few groups ahead of the conversions), 1 MMA warp, 1 spectrum-loader warp, and
 //   WC = 2W compute warps split into NTEAM teams of TWARPS warps (a multiple of 4, so a team covers all
 //   four TMEM lane quarters).
 //   NS slots: a slot holds one group in flight (a data buffer and a TMEM accumulator region).  Team t
-//   owns slots t*NST .. t*NST + NST - 1 and steps through its groups' tasks on its own; the MMA warp
-//   serves whichever slot is ready, so one team's waits are filled by another team's work.
-//   Shared memory after the DFT matrices and the NS data buffers: a spectrum staging area (KSLOT slots
-//   of KC rows), then the input staging ring (NCH chunks of CHUNK bytes, at least two).
-// Slot policy: one slot per team of four compute warps (measured best: a team that alternates between two
-// slots of its own loses more to lockstep than it gains), at most SFFFT_MAX_SLOTS, as many as TMEM holds
-// and as leave shared memory for an input ring of SFFFT_RING_GROUPS groups (at least two chunks).
+//   owns slots t*NST .. t*NST + NST - 1 and steps through its groups' tasks on its own (it reads its
+//   groups' input straight from global memory); the MMA warp serves whichever slot is ready, so one
+//   team's waits are filled by another team's work.
+//   Shared memory after the DFT matrices and the NS data buffers: the spectrum staging area (KSLOT slots
+//   of KC channel rows).
+// Slot policy: one slot per team of four compute warps (a team that alternates between two slots of its
+// own loses more to lockstep than it gains), at most SFFFT_MAX_SLOTS, as many as TMEM and shared memory hold.
 #ifndef SFFFT_MAX_SLOTS
 #define SFFFT_MAX_SLOTS 4
 #endif
 #ifndef SFFFT_MAX_TEAMS
 #define SFFFT_MAX_TEAMS 4
 #endif
-#ifndef SFFFT_RING_GROUPS
-#define SFFFT_RING_GROUPS 0
-#endif
 template <class P, int SIO>
 struct Shape {
   static constexpr int WC = 2 * P::W;
   static constexpr int CW0 = 3;                                     // first compute warp
   static constexpr int NT = 32 * (WC + CW0);
-  static constexpr int GIN = 2 * P::G * P::L * SIO;                 // input bytes per group
-  static constexpr int CHUNK = GIN < 8192 ? GIN : 8192;
-  static constexpr int CPG = GIN / CHUNK;                           // chunks per group
+  static constexpr int SEQB = P::L * SIO;                           // input bytes per sequence
   static constexpr int TW_BYTES = ((64 + P::N / 64) * 8 + 127) / 128 * 128;   // two-level twiddle table
   static constexpr int CAP = 227 * 1024 - 1024 - 512 - TW_BYTES;    // dynamic smem minus align slack, barriers
-  static constexpr int MINSTAGE = 2 * CHUNK;
-  static constexpr int RING_MIN = SFFFT_RING_GROUPS * GIN > MINSTAGE ? SFFFT_RING_GROUPS * GIN : MINSTAGE;
   static constexpr bool fits(int ns) {
-    return ns * P::TMEM_COLS <= 512 && P::BMAT_BYTES + ns * P::DATA_BYTES + (ns > 1 ? RING_MIN : MINSTAGE) <= CAP;
+    return ns * P::TMEM_COLS <= 512 && P::BMAT_BYTES + ns * P::DATA_BYTES <= CAP;
   }
   static constexpr int NSMAX = WC / 4 < SFFFT_MAX_SLOTS ? WC / 4 : SFFFT_MAX_SLOTS;
   static constexpr int NS = (NSMAX >= 4 && fits(4)) ? 4 : ((NSMAX >= 2 && fits(2)) ? 2 : 1);
@@ -168,33 +161,33 @@ struct Shape {
   static constexpr int NST = NS / NTEAM;                            // slots per team
   static constexpr int TWARPS = WC / NTEAM;                         // warps per team
   static constexpr int NWQ = TWARPS / 4;                            // a team's warps per TMEM lane quarter
+  static constexpr int NB = P::W == 4 ? 4 : 2;                      // conversion steps whose loads overlap
+  static constexpr int PD = NS + 1;                                 // L2 prefetch distance, groups
   static constexpr int DATA_OFF = P::BMAT_BYTES;
-  static constexpr int STAGE_OFF = DATA_OFF + NS * P::DATA_BYTES;
-  static constexpr int FREE = CAP - STAGE_OFF;
-  // spectrum staging: one channel row per slot, two slots when they fit beside the minimum ring; rows
-  // of further channels (groups that span several channels) only from what the ring leaves
+  static constexpr int K_OFF = DATA_OFF + NS * P::DATA_BYTES;
+  static constexpr int FREE = CAP - K_OFF;
+  // spectrum staging: KSLOT slots of KC channel rows (N complex fp32 each), filled by the loader warp in a
+  // swizzled [chunk][row][16 B ^ row%8] order; groups spanning more than KC channels read Kf from global.
+  // A single slot serialises several teams' spectrum stages (measured slower than global reads), so it
+  // is used only by a CTA with one team.
   static constexpr int KROW = P::N * 8;
-  static constexpr int KSLOT = FREE >= MINSTAGE + 2 * KROW ? 2 : (FREE >= MINSTAGE + KROW ? 1 : 0);
-  static constexpr int STAGE_MAX = ((FREE - KSLOT * KROW) / CHUNK) * CHUNK;
-  static constexpr int STAGE = 2 * GIN < STAGE_MAX ? 2 * GIN : STAGE_MAX;
-  static constexpr int NCH = STAGE / CHUNK;
-  static constexpr int KX = KSLOT > 0 ? (FREE - STAGE) / (KSLOT * KROW) : 0;
+  static constexpr int KSLOT = FREE >= 2 * KROW ? 2 : ((FREE >= KROW && NTEAM == 1) ? 1 : 0);
+  static constexpr int KX = KSLOT > 0 ? FREE / (KSLOT * KROW) : 0;
   static constexpr int KC = KSLOT == 0 ? 0 : (KX < P::G ? KX : P::G);
   static constexpr int KBYTES = KSLOT * KC * KROW;
-  static constexpr int K_OFF = STAGE_OFF + STAGE;
   static constexpr int TW_OFF = K_OFF + KBYTES;
   static constexpr int BAR_OFF = TW_OFF + TW_BYTES;
   static constexpr int SMEM = BAR_OFF + 512 + 1024;
   static constexpr int TMEM_ALLOC = pow2ceil(cmax(32, NS * P::TMEM_COLS));
   static constexpr int TPG = 2 * P::S + 1;                          // tasks per group: convert + 2S epilogues
-  // 8-byte words from BAR_OFF: full[NCH], empty[NCH], a_ready[NS], mma_done[NS], k_full[2], k_empty[2],
-  // TMEM base, abort flag, first staged channel per spectrum slot[2], team_done[NTEAM], then the int
-  // stamps of the input chunk slots [NCH] and spectrum slots [2]
-  static constexpr int NBARW = 2 * NCH + 2 * NS + 4 + 3 + NTEAM + (NCH + 3) / 2;
-  static_assert(NCH >= 2, "staging ring needs two chunks");
+  // 8-byte words from BAR_OFF: a_ready[NS], mma_done[NS], k_full[2], k_empty[2], TMEM base, abort flag,
+  // first staged channel per spectrum slot[2], team_done[NTEAM], then ints: spectrum slot stamps[2] and the
+  // count of converted groups
+  static constexpr int NBARW = 2 * NS + 4 + 3 + NTEAM + 2;
   static_assert(NBARW <= 64, "barrier area");
   static_assert(NS % NTEAM == 0 && WC % (4 * NTEAM) == 0, "teams");
   static_assert(SMEM <= 227 * 1024, "shared memory");
+  static_assert(SEQB % 16 == 0, "sequences are whole 16-byte runs");
 };
 
 // Row pitch of the K-major A operand of the inverse last-digit stage (re | im halves of a row).

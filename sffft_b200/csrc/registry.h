@@ -11,7 +11,7 @@ typedef cudaError_t (*ConvLaunchFn)(const ConvParams& prm, int grid, int smem_by
 struct ConvEntry {
   const char* name;            // "64x32/w4"
   int R0, R1, R2, G, W, N, L, threads, bmat_bytes;
-  int smem_bytes[2], tmem_cols[2], slots[2], stage_chunks[2];   // per I/O type (fp32, bf16)
+  int smem_bytes[2], tmem_cols[2], slots[2], kslots[2];   // per I/O type (fp32, bf16)
   ConvLaunchFn launch[2][2];   // [io: 0 fp32, 1 bf16][acc: 0 fp32, 1 fp16]
   const void* func[2][2];      // kernel function pointers (attributes, occupancy)
   void (*build_bmat)(uint8_t* img);   // host builder of the cached DFT-matrix image

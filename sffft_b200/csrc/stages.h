@@ -8,7 +8,7 @@
 //   ops.acc_val(raw)                                         TMEM word -> float (fp32 or fp16 accumulator)
 //   ops.ldK(p) / ops.ldsK(p)                                 four floats (two complex) of the spectrum from
 //                                                            global / staged shared memory
-//   ops.lds8(p, v)                                           eight staged input values (TIO) -> float
+//   ops.ldg8(p, v)                                           eight input values (TIO) from global -> float
 //   ops.store1(p, v) / ops.store4(p, v[4])                   output values (TIO) to global memory
 //   ops.tw(e, &re, &im)                                      w_N^e from the CTA's twiddle table
 //   ops.twiddle16(a, b, t0, t8, w, pr, pim)                  16 complex values x t0*w^j (j < 8) and
@@ -74,29 +74,42 @@ SF_HD PairInfo pair_info(int cta, int g, int G, int B, int H, int L) {
 // ---------------------------------------------------------------------------------------------
 // Input conversion: raw u (two real sequences per pair) -> first-stage A operand, fp16 hi + lo split.
 //   element (row m = g*V0 + v, K-row plane*R0 + n0 [hi] / plane*R0 + R0/2 + n0 [lo]), n = n0*V0 + v.
-// A group's input is the stream of its 2G sequences (sequence j = 2*g + plane, element n at j*L + n);
-// convert_chunk handles the stream elements [e0, e0 + ne) staged at `chunk` (raw TIO values).
+// A group's input is its 2G sequences (sequence j = 2*g + plane, element n), read straight from global
+// memory: thread tid of nthreads takes 8 consecutive elements per step and issues NB steps' loads before it
+// converts any, so their latencies overlap.  Absent sequences (odd B, past the last pair) read as zero.
 // ---------------------------------------------------------------------------------------------
-template <class P, class TIO, class Ops>
-SF_HD void convert_chunk(Ops& ops, const TIO* chunk, int e0, int ne, const GroupPairs& gp, int tid, int nthreads) {
-  constexpr int V0 = P::N / P::R0, MB0 = P::MB(0);
-  for (int i = tid * 8; i < ne; i += nthreads * 8) {
-    const int e = e0 + i, j = e / P::L, n = e - j * P::L, g = j >> 1, plane = j & 1;
-    const PairInfo pi = gp.get(g, P::L);
-    const bool present = (plane == 0 ? pi.off0 : pi.off1) >= 0;
-    float v[8];
-    if (present) ops.lds8(chunk + i, v);
-    else {
-      for (int q = 0; q < 8; q++) v[q] = 0.f;
+template <class P, class TIO, int NB, class Ops>
+SF_HD void convert_group(Ops& ops, const TIO* u, const GroupPairs& gp, int tid, int nthreads) {
+  constexpr int V0 = P::N / P::R0, MB0 = P::MB(0), NE = 2 * P::G * P::L;
+  for (int e0 = tid * 8; e0 < NE; e0 += NB * nthreads * 8) {
+    float v[NB][8];
+    int mrow[NB], krow[NB];
+    for (int b = 0; b < NB; b++) {
+      const int e = e0 + b * nthreads * 8;
+      krow[b] = -1;
+      if (e < NE) {
+        const int j = e / P::L, n = e - j * P::L, g = j >> 1, plane = j & 1;
+        const PairInfo pi = gp.get(g, P::L);
+        const long long off = plane == 0 ? pi.off0 : pi.off1;
+        const int n0 = n / V0, vv = n - n0 * V0;
+        mrow[b] = g * V0 + vv;
+        krow[b] = plane * P::R0 + n0;
+        if (off >= 0) ops.ldg8(u + off + n, v[b]);
+        else {
+          for (int q = 0; q < 8; q++) v[b][q] = 0.f;
+        }
+      }
     }
-    uint32_t hi[4], lo[4];
-    for (int q = 0; q < 4; q++) {
-      hi[q] = ops.pack2(v[2 * q], v[2 * q + 1]);
-      lo[q] = ops.pack2(v[2 * q] - ops.lo16f(hi[q]), v[2 * q + 1] - ops.hi16f(hi[q]));
+    for (int b = 0; b < NB; b++) {
+      if (krow[b] < 0) continue;
+      uint32_t hi[4], lo[4];
+      for (int q = 0; q < 4; q++) {
+        hi[q] = ops.pack2(v[b][2 * q], v[b][2 * q + 1]);
+        lo[q] = ops.pack2(v[b][2 * q] - ops.lo16f(hi[q]), v[b][2 * q + 1] - ops.hi16f(hi[q]));
+      }
+      ops.st16(mn_off(mrow[b], krow[b], MB0), hi[0], hi[1], hi[2], hi[3]);
+      ops.st16(mn_off(mrow[b], krow[b] + P::R0 / 2, MB0), lo[0], lo[1], lo[2], lo[3]);
     }
-    const int n0 = n / V0, vv = n - n0 * V0, m = g * V0 + vv, k = plane * P::R0 + n0;
-    ops.st16(mn_off(m, k, MB0), hi[0], hi[1], hi[2], hi[3]);
-    ops.st16(mn_off(m, k + P::R0 / 2, MB0), lo[0], lo[1], lo[2], lo[3]);
   }
 }
 
