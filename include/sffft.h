@@ -124,6 +124,19 @@ int sffft_debug_umma_probe(int a_kind, int a_slice, int b_pitch, int b_slice, in
 int sffft_conv_noalloc(int L, int io, int acc, const void* u, const void* k, int k_dtype, void* y, int B, int H,
                        void* stream, int sync);
 
+/* Host-buffer pipeline (no reference counterpart: the reference keeps u and y on the device and times the
+ * kernel alone).  sffft_pipe_create sizes device staging for a B x H batch cut into about `chunks` chunks
+ * (0 = 4) of whole batch-row pairs (contiguous, one copy each way), or of pairs and channel ranges when B/2
+ * is smaller than `chunks`, and creates three streams; sffft_conv_host then computes
+ * y_host = causal_conv(u_host, k) for host buffers u_host, y_host [B][H][L] (the plan's I/O type; pinned for
+ * overlap) and the device spectrum Kf [H][N]: chunk i is uploaded, convolved and downloaded on stream i % 3,
+ * so uploads, kernels and downloads of different chunks overlap.  Ordered after earlier work on `stream`; later work on
+ * `stream` waits for it.  Calls on one pipe must not overlap. */
+typedef struct sffft_pipe* sffft_pipe_t;
+int sffft_pipe_create(sffft_pipe_t* pipe, sffft_plan_t plan, int B, int H, int chunks);
+int sffft_conv_host(sffft_pipe_t pipe, const void* u_host, const void* Kf, void* y_host, void* stream);
+int sffft_pipe_destroy(sffft_pipe_t pipe);
+
 /* Debug: a kernel waits on a barrier that nothing arrives at, using the same bounded wait as the fused
  * kernel; returns SFFFT_ERR_TIMEOUT after about limit_us microseconds (1..1e6) with the context intact.
  * No reference counterpart (the reference has no device-side timeouts). */

@@ -67,6 +67,9 @@ def _declare(lib):
         "sffft_baseline_destroy": (I, [P]),
         "sffft_debug_umma_probe": (I, [I, I, I, I, I, I, V, V, V]),
         "sffft_debug_wait_timeout": (I, [I]),
+        "sffft_pipe_create": (I, [ctypes.POINTER(P), P, I, I, I]),
+        "sffft_conv_host": (I, [P, V, V, V, V]),
+        "sffft_pipe_destroy": (I, [P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -213,6 +216,34 @@ class Plan:
     def close(self):
         if self._h:
             lib().sffft_plan_destroy(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class HostPipe:
+    """Convolution of a batch held in host memory (sffft_pipe_create / sffft_conv_host): chunks of batch-row
+    pairs are uploaded, convolved and downloaded on three streams so the copies and the kernels overlap."""
+
+    def __init__(self, plan: "Plan", B: int, H: int, chunks: int = 0):
+        self._h = ctypes.c_void_p()
+        _check(lib().sffft_pipe_create(ctypes.byref(self._h), plan._h, B, H, chunks), "pipe_create")
+        self.plan, self.B, self.H = plan, B, H
+
+    def conv(self, u_host, Kf, y_host, stream=None):
+        """y_host = causal_conv(u_host, k) for host tensors u_host, y_host [B][H][L] and the device spectrum Kf."""
+        if tuple(u_host.shape) != (self.B, self.H, self.plan.L) or tuple(y_host.shape) != tuple(u_host.shape):
+            raise ValueError("u_host / y_host must be [B][H][L] of the pipe's batch")
+        _check(lib().sffft_conv_host(self._h, _ptr(u_host), _ptr(Kf), _ptr(y_host), _stream(stream)), "conv_host")
+        return y_host
+
+    def close(self):
+        if self._h:
+            lib().sffft_pipe_destroy(self._h)
             self._h = ctypes.c_void_p()
 
     def __del__(self):

@@ -1,0 +1,130 @@
+// Host-buffer pipeline: the fused convolution of a batch that lives in host memory.
+//
+// The batch is cut into chunks of whole batch-row pairs (u[b0:b1] is contiguous in [B][H][L], so a chunk
+// moves with one 1-D copy each way); only when there are fewer pair rows than chunks are the rows also cut
+// into channel ranges (2-D copies of b1 - b0 rows, host pitch H * L, measured slower per byte).  Chunk i
+// goes through three steps on stream i % 3 -- upload to device staging, sffft_conv with the chunk's
+// spectrum rows, download into y -- so the upload of one chunk, the kernel of the previous one and the
+// download of the one before that overlap, and both copy directions run at the same time.  Pinned host
+// buffers make the copies asynchronous (pageable ones still give correct results, without the overlap).
+// The call is ordered after earlier work on the caller's stream, and later work on that stream waits for
+// all chunks.
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <new>
+
+#include "../../include/sffft.h"
+
+namespace {
+constexpr int kStreams = 3;
+}
+
+struct sffft_pipe {
+  sffft_plan_t plan;
+  int B, H, L, N, sio, nb, hc, device;   // chunk: nb batch rows (even) x hc channels
+  void* u_stage[kStreams];   // device staging [nb][hc][L] per stream
+  void* y_stage[kStreams];
+  cudaStream_t s[kStreams];
+  cudaEvent_t start, done[kStreams];
+};
+
+static void pipe_free(sffft_pipe* q) {
+  for (int i = 0; i < kStreams; i++) {
+    if (q->u_stage[i]) cudaFree(q->u_stage[i]);
+    if (q->y_stage[i]) cudaFree(q->y_stage[i]);
+    if (q->s[i]) cudaStreamDestroy(q->s[i]);
+    if (q->done[i]) cudaEventDestroy(q->done[i]);
+  }
+  if (q->start) cudaEventDestroy(q->start);
+  delete q;
+}
+
+extern "C" int sffft_pipe_create(sffft_pipe_t* pipe, sffft_plan_t plan, int B, int H, int chunks) {
+  if (!pipe || !plan || B < 1 || H < 1 || chunks < 0) return SFFFT_ERR_INVALID_ARGUMENT;
+  *pipe = nullptr;
+  sffft_plan_info_t info;
+  int rc = sffft_plan_info(plan, &info);
+  if (rc) return rc;
+  if (chunks == 0) chunks = 4;
+  const int prow = (B + 1) / 2;            // pair rows (a chunk never splits a pair)
+  int prev = 0;
+  if (cudaGetDevice(&prev) != cudaSuccess) return SFFFT_ERR_CUDA;
+  if (cudaSetDevice(info.device) != cudaSuccess) return SFFFT_ERR_CUDA;
+  sffft_pipe* q = new (std::nothrow) sffft_pipe();
+  if (!q) return SFFFT_ERR_INVALID_ARGUMENT;
+  q->plan = plan; q->B = B; q->H = H; q->L = info.L; q->N = info.N; q->device = info.device;
+  q->sio = info.io == SFFFT_IO_BF16 ? 2 : 4;
+  if (chunks <= prow) {
+    q->nb = 2 * ((prow + chunks - 1) / chunks);
+    q->hc = H;
+  } else {
+    q->nb = 2;
+    const int split = (chunks + prow - 1) / prow;
+    q->hc = (H + split - 1) / split;
+  }
+  if (q->nb > B) q->nb = B;
+  const size_t bytes = (size_t)q->nb * q->hc * q->L * q->sio;
+  bool ok = cudaEventCreateWithFlags(&q->start, cudaEventDisableTiming) == cudaSuccess;
+  for (int i = 0; i < kStreams && ok; i++) {
+    ok = cudaMalloc(&q->u_stage[i], bytes) == cudaSuccess && cudaMalloc(&q->y_stage[i], bytes) == cudaSuccess &&
+         cudaStreamCreateWithFlags(&q->s[i], cudaStreamNonBlocking) == cudaSuccess &&
+         cudaEventCreateWithFlags(&q->done[i], cudaEventDisableTiming) == cudaSuccess;
+  }
+  cudaSetDevice(prev);
+  if (!ok) {
+    pipe_free(q);
+    return SFFFT_ERR_CUDA;
+  }
+  *pipe = q;
+  return SFFFT_OK;
+}
+
+extern "C" int sffft_conv_host(sffft_pipe_t q, const void* u_host, const void* Kf, void* y_host, void* stream) {
+  if (!q || !u_host || !Kf || !y_host) return SFFFT_ERR_INVALID_ARGUMENT;
+  int prev = 0;
+  if (cudaGetDevice(&prev) != cudaSuccess) return SFFFT_ERR_CUDA;
+  if (prev != q->device && cudaSetDevice(q->device) != cudaSuccess) return SFFFT_ERR_CUDA;
+  const cudaStream_t user = (cudaStream_t)stream;
+  int rc = SFFFT_OK;
+  cudaError_t ce = cudaEventRecord(q->start, user);
+  for (int i = 0; i < kStreams && ce == cudaSuccess; i++) ce = cudaStreamWaitEvent(q->s[i], q->start, 0);
+  const size_t row = (size_t)q->H * q->L * q->sio;   // host pitch between batch rows
+  int c = 0;
+  for (int b0 = 0; b0 < q->B && ce == cudaSuccess && rc == SFFFT_OK; b0 += q->nb) {
+    const int b1 = b0 + q->nb < q->B ? b0 + q->nb : q->B, bn = b1 - b0;
+    for (int h0 = 0; h0 < q->H && ce == cudaSuccess && rc == SFFFT_OK; h0 += q->hc, c++) {
+      const int h1 = h0 + q->hc < q->H ? h0 + q->hc : q->H, hn = h1 - h0, k = c % kStreams;
+      const size_t width = (size_t)hn * q->L * q->sio;
+      const char* src = (const char*)u_host + (size_t)b0 * row + (size_t)h0 * q->L * q->sio;
+      char* dst = (char*)y_host + (size_t)b0 * row + (size_t)h0 * q->L * q->sio;
+      ce = hn == q->H ? cudaMemcpyAsync(q->u_stage[k], src, width * bn, cudaMemcpyHostToDevice, q->s[k])
+                      : cudaMemcpy2DAsync(q->u_stage[k], width, src, row, width, bn, cudaMemcpyHostToDevice, q->s[k]);
+      if (ce != cudaSuccess) break;
+      rc = sffft_conv(q->plan, q->u_stage[k], (const char*)Kf + (size_t)h0 * q->N * 8, q->y_stage[k], bn, hn, q->s[k]);
+      if (rc) break;
+      ce = hn == q->H ? cudaMemcpyAsync(dst, q->y_stage[k], width * bn, cudaMemcpyDeviceToHost, q->s[k])
+                      : cudaMemcpy2DAsync(dst, row, q->y_stage[k], width, width, bn, cudaMemcpyDeviceToHost, q->s[k]);
+    }
+  }
+  for (int i = 0; i < kStreams; i++) {
+    cudaError_t e = cudaEventRecord(q->done[i], q->s[i]);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(user, q->done[i], 0);
+    if (ce == cudaSuccess) ce = e;
+  }
+  if (prev != q->device) cudaSetDevice(prev);
+  if (rc) return rc;
+  return ce == cudaSuccess ? SFFFT_OK : SFFFT_ERR_CUDA;
+}
+
+extern "C" int sffft_pipe_destroy(sffft_pipe_t q) {
+  if (!q) return SFFFT_ERR_INVALID_ARGUMENT;
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaSetDevice(q->device);
+  for (int i = 0; i < kStreams; i++)
+    if (q->s[i]) cudaStreamSynchronize(q->s[i]);
+  pipe_free(q);
+  cudaSetDevice(prev);
+  return SFFFT_OK;
+}

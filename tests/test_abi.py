@@ -82,3 +82,6 @@ def test_null_handles_are_rejected():
     assert lib.sffft_plan_destroy(None) == sf.ERR_INVALID_ARGUMENT
     assert lib.sffft_plan_check(None) == sf.ERR_INVALID_ARGUMENT
     assert lib.sffft_baseline_destroy(None) == sf.ERR_INVALID_ARGUMENT
+    assert lib.sffft_pipe_create(None, None, 1, 1, 0) == sf.ERR_INVALID_ARGUMENT
+    assert lib.sffft_conv_host(None, 16, 16, 16, None) == sf.ERR_INVALID_ARGUMENT
+    assert lib.sffft_pipe_destroy(None) == sf.ERR_INVALID_ARGUMENT
