@@ -219,6 +219,7 @@ __device__ __forceinline__ bool wait_stamp(const volatile int* stamp, int want, 
   while (*stamp < want) {
     if (*abort_flag) return false;
     if (global_ns() - t0 > kWaitLimitNs) { *abort_flag = 1; return false; }
+    __nanosleep(64);   // polling warps would otherwise take issue slots from the compute warps
   }
   return true;
 }
@@ -405,6 +406,7 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
         } else {
           if (*abort_flag) break;
           if (global_ns() - t_idle > kWaitLimitNs) { *abort_flag = 1; break; }
+          __nanosleep(32);   // nothing ready: back off instead of spinning on the compute warps' scheduler
         }
       }
       // make sure no MMA is still writing TMEM when the CTA frees it
