@@ -1,0 +1,83 @@
+"""PyTorch operators over the C ABI (the packaging the reference names as its next step, README.md:177).
+
+    import sffft_b200.torch_ops  # registers the operators
+    Kf = torch.ops.sffft.filter_spectrum(k)            # k [H][L] fp32 or bf16 -> Kf [H][2L][2] fp32
+    y = torch.ops.sffft.conv(u, Kf)                    # u [B][H][L] fp32 or bf16 -> y, same shape and type
+    y = sffft_b200.torch_ops.causal_conv(u, k)         # both steps
+
+Both run on the current CUDA stream of the tensors' device through sffft_filter_spectrum / sffft_conv, so
+they order with surrounding PyTorch work and can be captured in CUDA graphs once a first call has created
+the plan (plan creation allocates).  Fake implementations give output shapes and types without running
+anything, so the operators trace under torch.compile.  Forward only: the path has no backward kernel.
+
+`acc` is "fp32" or "fp16" (accumulation mode); `config` names a catalog plan ("" = the default for L).
+filter_spectrum and conv must use the same config: the spectrum is in that plan's digit order.
+"""
+import threading
+
+import torch
+from torch import Tensor
+
+import sffft_b200 as sf
+
+_plans: dict = {}
+_lock = threading.Lock()
+
+
+def _plan(L: int, io: str, acc: str, config: str, device: int) -> "sf.Plan":
+    key = (L, io, acc, config, device)
+    with _lock:
+        p = _plans.get(key)
+        if p is None:
+            p = sf.Plan(L, io=io, acc=acc, config=config or None, device=device)
+            _plans[key] = p
+    return p
+
+
+def _check_cuda(t: Tensor, what: str):
+    if t.device.type != "cuda":
+        raise ValueError(f"sffft::{what} needs CUDA tensors (there is no CPU path)")
+
+
+@torch.library.custom_op("sffft::filter_spectrum", mutates_args=())
+def filter_spectrum(k: Tensor, config: str = "") -> Tensor:
+    _check_cuda(k, "filter_spectrum")
+    if k.dim() != 2 or k.dtype not in (torch.float32, torch.bfloat16):
+        raise ValueError("k must be [H][L], float32 or bfloat16")
+    H, L = k.shape
+    dev = k.device.index if k.device.index is not None else torch.cuda.current_device()
+    plan = _plan(L, "fp32", "fp32", config, dev)
+    Kf = torch.empty((H, 2 * L, 2), dtype=torch.float32, device=k.device)
+    return plan.filter_spectrum(k.contiguous(), Kf, stream=torch.cuda.current_stream(k.device))
+
+
+@filter_spectrum.register_fake
+def _(k: Tensor, config: str = "") -> Tensor:
+    H, L = k.shape
+    return k.new_empty((H, 2 * L, 2), dtype=torch.float32)
+
+
+@torch.library.custom_op("sffft::conv", mutates_args=())
+def conv(u: Tensor, Kf: Tensor, acc: str = "fp32", config: str = "") -> Tensor:
+    _check_cuda(u, "conv")
+    if u.dim() != 3 or u.dtype not in (torch.float32, torch.bfloat16):
+        raise ValueError("u must be [B][H][L], float32 or bfloat16")
+    B, H, L = u.shape
+    if tuple(Kf.shape) != (H, 2 * L, 2) or Kf.dtype != torch.float32 or Kf.device != u.device:
+        raise ValueError("Kf must be the [H][2L][2] float32 spectrum on u's device")
+    io = "bf16" if u.dtype == torch.bfloat16 else "fp32"
+    dev = u.device.index if u.device.index is not None else torch.cuda.current_device()
+    plan = _plan(L, io, acc, config, dev)
+    y = torch.empty_like(u, memory_format=torch.contiguous_format)
+    plan.conv(u.contiguous(), Kf.contiguous(), y, stream=torch.cuda.current_stream(u.device))
+    return y
+
+
+@conv.register_fake
+def _(u: Tensor, Kf: Tensor, acc: str = "fp32", config: str = "") -> Tensor:
+    return torch.empty_like(u, memory_format=torch.contiguous_format)
+
+
+def causal_conv(u: Tensor, k: Tensor, acc: str = "fp32", config: str = "") -> Tensor:
+    """y[b,h,n] = sum_{m<=n} u[b,h,m] k[h,n-m]: the spectrum of k, then the fused convolution."""
+    return conv(u, filter_spectrum(k, config), acc, config)
