@@ -32,15 +32,16 @@ struct PairInfo {
 };
 
 // Pair bookkeeping of one group with 32-bit arithmetic: one division per group, then pair g is found
-// from the group's first pair (j0 < PB and g < G <= 8, so one subtraction suffices when PB >= 8);
-// 2j*H + h < B*H <= INT_MAX.
+// from the group's first pair: j0 < PB and g < G, so one subtraction suffices whenever PB >= G (batches
+// of at least 2G); a division is left only for smaller batches.  2j*H + h < B*H <= INT_MAX.
 struct GroupPairs {
   int h0, j0, PB, B, H;
   SF_HD PairInfo get(int g, int L) const {
     int j = j0 + g, h = h0;
     if (j >= PB) {
-      if (PB >= 8) { j -= PB; h++; }
-      else { const int d = j / PB; j -= d * PB; h += d; }
+      j -= PB;
+      h++;
+      if (j >= PB) { const int d = j / PB; j -= d * PB; h += d; }
     }
     PairInfo pi;
     if (h >= H) { pi.off0 = pi.off1 = -1; pi.h = -1; return pi; }
@@ -107,8 +108,10 @@ SF_HD void convert_group(Ops& ops, const TIO* u, const GroupPairs& gp, int tid, 
         hi[q] = ops.pack2(v[b][2 * q], v[b][2 * q + 1]);
         lo[q] = ops.pack2(v[b][2 * q] - ops.lo16f(hi[q]), v[b][2 * q + 1] - ops.hi16f(hi[q]));
       }
-      ops.st16(mn_off(mrow[b], krow[b], MB0), hi[0], hi[1], hi[2], hi[3]);
-      ops.st16(mn_off(mrow[b], krow[b] + P::R0 / 2, MB0), lo[0], lo[1], lo[2], lo[3]);
+      // K-row k + R0/2 (the lo plane) is R0/16 K-groups further: same swizzle phase, since R0/2 % 8 == 0
+      const uint32_t off = mn_off(mrow[b], krow[b], MB0);
+      ops.st16(off, hi[0], hi[1], hi[2], hi[3]);
+      ops.st16(off + (uint32_t)(P::R0 / 16) * MB0 * 1024u, lo[0], lo[1], lo[2], lo[3]);
     }
   }
 }
