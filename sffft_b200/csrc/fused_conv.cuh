@@ -169,7 +169,7 @@ struct ConvParams {
 };
 
 #ifdef SFFFT_TRACE
-// roles: 0 producer, 1 MMA issuer, 2 + t compute team t (its first warp's lane 0)
+// roles: 0 L2 prefetcher, 1 MMA issuer, 2 + t compute team t (its first warp's lane 0)
 constexpr int kTraceLen = 2048, kTraceRoles = 8;
 #define SFFFT_STAMP(role, idx)                                                                         \
   do {                                                                                                 \
@@ -208,11 +208,12 @@ __device__ __forceinline__ bool wait_phase_all(uint64_t* bar, uint32_t parity, v
   return __all_sync(0xffffffffu, ok) != 0;
 }
 
-// Shared FIFO slots (input chunks, staged spectrum rows) are consumed by several teams out of order, so a
-// consumer can reach a slot two or more uses ahead of its barrier, where a parity test cannot tell the
-// phases apart.  The filler stamps each slot with the index of what it is filling before it arms the
-// barrier; a consumer first waits (bounded) until the stamp reaches its own index, after which the
-// barrier's pending phase is its own and the parity wait is exact.
+// A shared FIFO slot (the staged spectrum rows) is consumed by several teams out of order, so a consumer
+// can reach a slot two or more uses ahead of its barrier, where a parity test cannot tell the phases
+// apart.  The filler stamps each slot with the index of what it is filling before it arms the barrier; a
+// consumer first waits (bounded) until the stamp reaches its own index, after which the barrier's pending
+// phase is its own and the parity wait is exact.  The same bounded wait serves the prefetcher's count of
+// converted groups.
 __device__ __forceinline__ bool wait_stamp(const volatile int* stamp, int want, volatile int* abort_flag) {
   if (*stamp >= want) return true;
   const uint64_t t0 = global_ns();
