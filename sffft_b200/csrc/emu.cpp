@@ -170,7 +170,7 @@ struct HostOps {
 
 template <int SID, class P, class TIO, bool ACC16>
 void run_stage_emu(HostOps& ops, const EpiArgs& ea, const GroupPairs& gp, uint32_t data_s, uint32_t bmat_s) {
-  issue_stage<P, ACC16, SID>(ops, ea.tmem, data_s, bmat_s);
+  issue_stage<P, ACC16, SID, sizeof(TIO) == 4>(ops, ea.tmem, data_s, bmat_s);
   // every compute warp's share of the stage, in the kernel's unit order (lane quarter q, warp wi of NWQ)
   constexpr int NWQ = Shape<P, (int)sizeof(TIO)>::NWQ;
   for (int wi = 0; wi < NWQ; wi++)

@@ -236,22 +236,22 @@ __device__ __forceinline__ void warp_arrive(uint64_t* bar, int lane) {
   if (lane == 0) mbar_arrive(bar);
 }
 
-template <class P, bool ACC16, int SID>
+template <class P, bool ACC16, bool LO, int SID>
 __device__ __forceinline__ void issue_sid(DevOps& ops, uint32_t tmem, uint32_t data_s, uint32_t bmat_s) {
-  issue_stage<P, ACC16, SID>(ops, tmem, data_s, bmat_s);
+  issue_stage<P, ACC16, SID, LO>(ops, tmem, data_s, bmat_s);
 }
 
-template <class P, bool ACC16>
+template <class P, bool ACC16, bool LO>
 __device__ void issue_any(int sid, DevOps& ops, uint32_t tmem, uint32_t data_s, uint32_t bmat_s) {
   switch (sid) {
-    case 0: issue_sid<P, ACC16, 0>(ops, tmem, data_s, bmat_s); break;
-    case 1: issue_sid<P, ACC16, 1>(ops, tmem, data_s, bmat_s); break;
-    case 2: issue_sid<P, ACC16, 2>(ops, tmem, data_s, bmat_s); break;
-    case 3: issue_sid<P, ACC16, 3>(ops, tmem, data_s, bmat_s); break;
+    case 0: issue_sid<P, ACC16, LO, 0>(ops, tmem, data_s, bmat_s); break;
+    case 1: issue_sid<P, ACC16, LO, 1>(ops, tmem, data_s, bmat_s); break;
+    case 2: issue_sid<P, ACC16, LO, 2>(ops, tmem, data_s, bmat_s); break;
+    case 3: issue_sid<P, ACC16, LO, 3>(ops, tmem, data_s, bmat_s); break;
     default:
       if constexpr (P::S == 3) {
-        if (sid == 4) issue_sid<P, ACC16, 4>(ops, tmem, data_s, bmat_s);
-        else issue_sid<P, ACC16, 5>(ops, tmem, data_s, bmat_s);
+        if (sid == 4) issue_sid<P, ACC16, LO, 4>(ops, tmem, data_s, bmat_s);
+        else issue_sid<P, ACC16, LO, 5>(ops, tmem, data_s, bmat_s);
       }
   }
 }
@@ -392,7 +392,7 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
             ar_bits ^= 1u << s;
             tc_fence_after();
             SFFFT_STAMP(1, 3 * nmma + 1);
-            issue_any<P, ACC16>(done[s] % S2, ops, tmem + (uint32_t)(s * P::TMEM_COLS),
+            issue_any<P, ACC16, sizeof(TIO) == 4>(done[s] % S2, ops, tmem + (uint32_t)(s * P::TMEM_COLS),
                                 smem_u32(sm + SH::DATA_OFF + s * P::DATA_BYTES), smem_u32(bmat));
             mma_commit(mma_done + s);
             SFFFT_STAMP(1, 3 * nmma + 2);

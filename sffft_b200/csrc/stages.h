@@ -78,6 +78,8 @@ SF_HD PairInfo pair_info(int cta, int g, int G, int B, int H, int L) {
 // A group's input is its 2G sequences (sequence j = 2*g + plane, element n), read straight from global
 // memory: thread tid of nthreads takes 8 consecutive elements per step and issues NB steps' loads before it
 // converts any, so their latencies overlap.  Absent sequences (odd B, past the last pair) read as zero.
+// bf16 input is exact in fp16 (up to fp16-subnormal values below 6e-5, whose residue under 3e-8 is
+// dropped), so it has no lo plane to compute.
 // ---------------------------------------------------------------------------------------------
 template <class P, class TIO, int NB, class Ops>
 SF_HD void convert_group(Ops& ops, const TIO* u, const GroupPairs& gp, int tid, int nthreads) {
@@ -104,14 +106,17 @@ SF_HD void convert_group(Ops& ops, const TIO* u, const GroupPairs& gp, int tid, 
     for (int b = 0; b < NB; b++) {
       if (krow[b] < 0) continue;
       uint32_t hi[4], lo[4];
-      for (int q = 0; q < 4; q++) {
-        hi[q] = ops.pack2(v[b][2 * q], v[b][2 * q + 1]);
-        lo[q] = ops.pack2(v[b][2 * q] - ops.lo16f(hi[q]), v[b][2 * q + 1] - ops.hi16f(hi[q]));
-      }
+      for (int q = 0; q < 4; q++) hi[q] = ops.pack2(v[b][2 * q], v[b][2 * q + 1]);
       // K-row k + R0/2 (the lo plane) is R0/16 K-groups further: same swizzle phase, since R0/2 % 8 == 0
-      const uint32_t off = mn_off(mrow[b], krow[b], MB0);
+      const uint32_t off = mn_off(mrow[b], krow[b], MB0), off_lo = off + (uint32_t)(P::R0 / 16) * MB0 * 1024u;
       ops.st16(off, hi[0], hi[1], hi[2], hi[3]);
-      ops.st16(off + (uint32_t)(P::R0 / 16) * MB0 * 1024u, lo[0], lo[1], lo[2], lo[3]);
+      if constexpr (sizeof(TIO) == 4) {
+        for (int q = 0; q < 4; q++)
+          lo[q] = ops.pack2(v[b][2 * q] - ops.lo16f(hi[q]), v[b][2 * q + 1] - ops.hi16f(hi[q]));
+        ops.st16(off_lo, lo[0], lo[1], lo[2], lo[3]);
+      } else if constexpr (P::R0 == 16) {
+        ops.st16(off_lo, 0u, 0u, 0u, 0u);   // bf16 converts exactly: its lo plane is zero
+      }
     }
   }
 }
@@ -123,19 +128,23 @@ SF_HD void convert_group(Ops& ops, const TIO* u, const GroupPairs& gp, int tid, 
 // so the 14-bit field never carries into the next one).
 SF_HD uint64_t sdesc_add(uint64_t desc, uint32_t bytes) { return desc + (uint64_t)(bytes >> 4); }
 
-template <class P, bool ACC16, int SID, class Ops>
+// LO: the first stage's K axis carries the input's fp16 lo plane (fp32 input).  bf16 input converts to fp16
+// exactly, its lo plane is zero, and with R0 >= 32 its K-slices (rows n0 >= R0/2 of each plane) are skipped;
+// with R0 == 16 one slice holds both halves and the conversion writes zeros there.
+template <class P, bool ACC16, int SID, bool LO, class Ops>
 SF_HD void issue_stage(Ops& ops, uint32_t tmem, uint32_t data_s, uint32_t bmat_s) {
   constexpr int R = P::rad(SID), T = P::tiles(SID), NSL = R / 16;
   constexpr bool KM = P::kmajor(SID), INV = P::inv(SID);
   constexpr bool B0 = (SID == 0 && P::R0 == 16);
   constexpr int HS = P::R0 >= 32 ? P::R0 / 32 : 1;           // B K-slices per first-stage half
+  constexpr int NJ = (SID == 0 && !B0 && !LO) ? HS : NSL;     // K-slices issued per plane
   constexpr uint32_t idesc = make_idesc(128, 2 * R, !ACC16, !KM, false);
   constexpr int RB = kmaj_data_pitch(R), MBs = P::MB(SID);
   const uint64_t a_base = KM ? make_sdesc(data_s, 16, 8 * RB, lt_for_pitch(RB)) : make_sdesc(data_s, 1024, MBs * 1024, LT_SW128);
   const uint64_t b_base = B0 ? make_sdesc(bmat_s, 16, 8 * 32, LT_SW32) : make_sdesc(bmat_s, 16, 16 * R, lt_for_pitch(2 * R));
   for (int t = 0; t < T; t++) {
     for (int p = 0; p < 2; p++) {
-      for (int j = 0; j < NSL; j++) {
+      for (int j = 0; j < NJ; j++) {
         const int ks = p * NSL + j;
         uint32_t aoff;
         if constexpr (KM) {
