@@ -147,6 +147,18 @@ struct HostOps {
     *re = (float)std::cos(a);
     *im = (float)std::sin(a);
   }
+  void cmul16(const float* a, const float* b, const float* kk, uint32_t* pr, uint32_t* pim) {
+    for (int p = 0; p < 8; p++) {
+      float x[2], z[2];
+      for (int e = 0; e < 2; e++) {
+        const float kr = kk[4 * p + e], ki = kk[4 * p + 2 + e], av = a[2 * p + e], bv = b[2 * p + e];
+        x[e] = av * kr - bv * ki;
+        z[e] = av * ki + bv * kr;
+      }
+      pr[p] = pack2(x[0], x[1]);
+      pim[p] = pack2(z[0], z[1]);
+    }
+  }
   // elements j < 8 step from t0, elements j >= 8 from t8 (two recurrences, as on the device)
   void twiddle16(const float* a, const float* b, float t0r, float t0i, float t8r, float t8i, float wr, float wi,
                  uint32_t* pr, uint32_t* pim) {
@@ -222,8 +234,9 @@ int run_plan(const void* u, const float* Kf, void* y, int B, int H) {
         for (int ci = 0; ci <= hl - hf; ci++)
           for (int o = 0; o < SH::KROW / 16; o++) {
             const int rr = o / PPR, rem = o - rr * PPR;
-            std::memcpy(kst.data() + (size_t)ci * SH::KROW + kstage_off<P::N, P::RL>(rr, rem >> 3, rem & 7),
-                        (const uint8_t*)(Kf + 2ll * (hf + ci) * P::N) + 16 * o, 16);
+            float pc[4];
+            spec_piece(Kf + 2ll * (hf + ci) * P::N + 4 * o, stage_scale(P::RL), pc);
+            std::memcpy(kst.data() + (size_t)ci * SH::KROW + kstage_off<P::N, P::RL>(rr, rem >> 3, rem & 7), pc, 16);
           }
         ea.kst = kst.data();
         ea.khf = hf;

@@ -141,6 +141,24 @@ struct DevOps {
       }
     }
   }
+  // 16 complex values (a + ib) times the spectrum pieces kk (spec_piece format: scaled, re/im split),
+  // rounded to fp16 pairs; two elements per f32x2 op.
+  __device__ __forceinline__ void cmul16(const float* a, const float* b, const float* kk, uint32_t* pr,
+                                         uint32_t* pim) const {
+    const u64 NEG = pk2(-1.f, -1.f);
+#pragma unroll
+    for (int p = 0; p < 8; p++) {
+      const u64 A = pk2(a[2 * p], a[2 * p + 1]), B = pk2(b[2 * p], b[2 * p + 1]);
+      const u64 KR = pk2(kk[4 * p], kk[4 * p + 1]), KI = pk2(kk[4 * p + 2], kk[4 * p + 3]);
+      const u64 ORE = fma2(B, mul2(KI, NEG), mul2(A, KR));
+      const u64 OIM = fma2(A, KI, mul2(B, KR));
+      float x0, x1, z0, z1;
+      up2(ORE, x0, x1);
+      up2(OIM, z0, z1);
+      pr[p] = pack2(x0, x1);
+      pim[p] = pack2(z0, z1);
+    }
+  }
 };
 
 struct BmatEmitDev {
@@ -458,7 +476,12 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
                 const int o = o0 + q2 * 32 + lane;
                 if (o < NPIECE) {
                   const int rr = o / PPR, rem = o - rr * PPR;
-                  *reinterpret_cast<uint4*>(dst + kstage_off<P::N, P::RL>(rr, rem >> 3, rem & 7)) = v[q2];
+                  float raw[4] = {__uint_as_float(v[q2].x), __uint_as_float(v[q2].y), __uint_as_float(v[q2].z),
+                                  __uint_as_float(v[q2].w)};
+                  float pc[4];
+                  spec_piece(raw, stage_scale(P::RL), pc);
+                  *reinterpret_cast<float4*>(dst + kstage_off<P::N, P::RL>(rr, rem >> 3, rem & 7)) =
+                      make_float4(pc[0], pc[1], pc[2], pc[3]);
                 }
               }
             }

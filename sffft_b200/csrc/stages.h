@@ -8,6 +8,7 @@
 //   ops.acc_val(raw)                                         TMEM word -> float (fp32 or fp16 accumulator)
 //   ops.ldK(p) / ops.ldsK(p)                                 four floats (two complex) of the spectrum from
 //                                                            global / staged shared memory
+//   ops.cmul16(a, b, kk, pr, pim)                            16 complex values x spectrum pieces -> fp16 pairs
 //   ops.ldg8(p, v)                                           eight input values (TIO) from global -> float
 //   ops.store1(p, v) / ops.store4(p, v[4])                   output values (TIO) to global memory
 //   ops.tw(e, &re, &im)                                      w_N^e from the CTA's twiddle table
@@ -191,9 +192,22 @@ struct EpiArgs {
   int khf;
 };
 
-// Byte offset of the 16-byte piece j (two complex values) of 16-value chunk c of row rr in a staged
-// spectrum row of a plan whose last radix is R (rows = N / R): [c][rr][piece ^ rr%8], so the 32 rows a
-// warp reads hit 32 different bank groups.
+// 1/sqrt(R): the per-stage scale of a radix-R digit (the reference's 1/sqrt(R) per stage, total 1/N).
+SF_HD constexpr float stage_scale(int R) { return R == 16 ? 0.25f : (R == 64 ? 0.125f : 0.17677669529663687f); }
+
+// Spectrum values as the spectrum stage consumes them: per 16-byte piece (two complex values k0, k1 of
+// Kf), {s*re(k0), s*re(k1), s*im(k0), s*im(k1)} with s = stage_scale of the spectrum stage's radix, so
+// that the complex multiply runs on two elements per f32x2 operation and needs no separate scaling.
+SF_HD void spec_piece(const float* raw4, float s, float* out4) {
+  out4[0] = s * raw4[0];
+  out4[1] = s * raw4[2];
+  out4[2] = s * raw4[1];
+  out4[3] = s * raw4[3];
+}
+
+// Byte offset of the 16-byte piece j (two complex values, in the spec_piece format) of 16-value chunk c of
+// row rr in a staged spectrum row of a plan whose last radix is R (rows = N / R): [c][rr][piece ^ rr%8],
+// so the 32 rows a warp reads hit 32 different bank groups.
 template <int N, int R>
 SF_HD uint32_t kstage_off(int rr, int c, int j) {
   return (uint32_t)((((c * (N / R) + rr) << 3) + (j ^ (rr & 7))) << 4);
@@ -265,9 +279,10 @@ SF_HD EpiIdx epi_idx(uint32_t tmem, int t, int c, int q, int lane) {
   return x;
 }
 
-// Spectrum values of the 16 columns [c0, c0 + 16) of row rr for channel h (complex, re/im interleaved),
-// from the loader's staged rows when the group's channels are staged, else from Kf in global memory.
-// An empty pair slot (h < 0, past the last pair) reads any valid row; its outputs are never stored.
+// Spectrum values of the 16 columns [c0, c0 + 16) of row rr for channel h, in the spec_piece format (eight
+// pieces of four floats), from the loader's staged rows (stored in that format) when the group's channels
+// are staged, else from Kf in global memory (converted here).  An empty pair slot (h < 0, past the last
+// pair) reads any valid row; its outputs are never stored.
 template <class P, int SID, class Ops>
 SF_HD void load_spec(Ops& ops, const EpiArgs& ea, int h, int rr, int c0, float* kk) {
   constexpr int R = P::rad(SID), N = P::N;
@@ -280,10 +295,10 @@ SF_HD void load_spec(Ops& ops, const EpiArgs& ea, int h, int rr, int c0, float* 
     }
   } else {
     const float* Kp = ea.Kf + 2 * ((long long)(h < 0 ? 0 : h) * N + (long long)rr * R + c0);
-    for (int j = 0; j < 16; j += 2) {
+    for (int j = 0; j < 8; j++) {
       float k4[4];
-      ops.ldK(Kp + 2 * j, k4);
-      kk[2 * j] = k4[0]; kk[2 * j + 1] = k4[1]; kk[2 * j + 2] = k4[2]; kk[2 * j + 3] = k4[3];
+      ops.ldK(Kp + 4 * j, k4);
+      spec_piece(k4, stage_scale(R), kk + 4 * j);
     }
   }
 }
@@ -329,16 +344,7 @@ SF_HD void epi_finish(Ops& ops, const EpiArgs& ea, const GroupPairs& gp, const E
 
   uint32_t pr[8], pim[8];
   if constexpr (SPEC) {
-    for (int j = 0; j < 16; j += 2) {
-      float o_re[2], o_im[2];
-      for (int e = 0; e < 2; e++) {
-        const float xx = a[j + e] * SC, z = b[j + e] * SC;
-        o_re[e] = xx * kk[2 * (j + e)] - z * kk[2 * (j + e) + 1];
-        o_im[e] = xx * kk[2 * (j + e) + 1] + z * kk[2 * (j + e)];
-      }
-      pr[j / 2] = ops.pack2(o_re[0], o_re[1]);
-      pim[j / 2] = ops.pack2(o_im[0], o_im[1]);
-    }
+    ops.cmul16(a, b, kk, pr, pim);   // (a + ib) x the scaled spectrum, rounded to fp16 pairs
     constexpr int RWS = P::rows(SID + 1);
     ops.st16(kmaj_data_off(r, c0, R, RWS), pr[0], pr[1], pr[2], pr[3]);
     ops.st16(kmaj_data_off(r, c0 + 8, R, RWS), pr[4], pr[5], pr[6], pr[7]);
