@@ -61,6 +61,17 @@ int sffft_plan_info(sffft_plan_t plan, sffft_plan_info_t* info);
  * 283-288, 384). */
 int sffft_filter_spectrum(sffft_plan_t plan, const void* k, int k_dtype, int H, void* Kf, void* stream);
 
+/* Filter layouts: which convolution sffft_conv computes, for n in [0, L), with the spectrum of k. */
+#define SFFFT_FILTER_CAUSAL 0    /* k [H][L]:    y[n] = sum_{m<=n} u[m] k[n-m]           (the reference's) */
+#define SFFFT_FILTER_TWO_SIDED 1 /* k [H][2L-1]: y[n] = sum_{m<L} u[m] k[L-1+n-m]        (non-causal) */
+#define SFFFT_FILTER_CIRCULAR 2  /* k [H][L]:    y[n] = sum_{m<L} u[m] k[(n-m) mod L]    (period L) */
+
+/* sffft_filter_spectrum for a filter in the given layout (SFFFT_FILTER_*); the fused convolution is the
+ * same kernel for all three.  The reference exposes only the causal form; non-causal and circular
+ * convolution are listed as not yet exposed (README.md:174). */
+int sffft_filter_spectrum_ex(sffft_plan_t plan, const void* k, int k_dtype, int layout, int H, void* Kf,
+                             void* stream);
+
 /* The fused convolution: one kernel launch per call.  Replaces the launch
  * fftconv<P,W,TIO,TAcc,CACHED><<<B*H, 32*W, smem>>>(u, Kf, tw, dft, y, B, H) (src/sffft.cu:243-280,
  * 389-390); the unused twiddle table and the DFT table are owned by the plan. */

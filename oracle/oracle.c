@@ -10,7 +10,12 @@
  *     sqrt(-2 log U1) * cos(2 pi U2) with U1 drawn before U2;
  *   - the reference's input recipe (src/sffft.cu:339-341): u = nrand()*input_scale over B*H*L in
  *     order, then per channel h: a = 1/(4 + L*h/H), k[h,n] = nrand()*exp(-a*n)*sqrt(2a);
- *   - the BASELINE.json profiles: u ~ N(0,1); k[h,n] = N(0,1)*exp(-decay*n/L) [/sqrt(L)], same stream.
+ *   - the BASELINE.json profiles: u ~ N(0,1); k[h,n] = N(0,1)*exp(-decay*n/L) [/sqrt(L)], same stream;
+ *   - the same fp64 direct sum for the two filter layouts the reference lists as not yet exposed
+ *     (README.md:174): two-sided y[n] = sum_{m<L} u[m] k2[L-1+n-m] (k2 has 2L-1 taps, k2[L-1] is lag 0)
+ *     and period-L circular y[n] = sum_{m<L} u[m] kc[(n-m) mod L].  No reference output pins these; the
+ *     tests pin them against numpy's fp64 FFT and against the causal sum (a two-sided filter whose
+ *     negative lags are zero is the causal filter).
  * The generator stream is pinned by tests/golden/ref_rng.json, produced by compiling the reference's
  * own nrand() (oracle/ref_harness.cu).
  */
@@ -97,6 +102,36 @@ void oracle_direct_conv(const float* u, const float* k, double* y, int B, int H,
 #pragma omp parallel for schedule(dynamic, 4) num_threads(threads)
 #endif
   for (long long s = 0; s < n; s++) conv_one(u + (size_t)s * L, k + (size_t)(s % H) * L, y + (size_t)s * L, L);
+}
+
+/* Direct sums for one sequence: layout 1 = two-sided (k has 2L-1 taps), 2 = period-L circular. */
+static void conv_one_layout(const float* u, const float* k, double* y, int L, int layout) {
+  for (int n = 0; n < L; n++) {
+    double acc = 0;
+    if (layout == 1) {
+      for (int m = 0; m < L; m++) acc += (double)u[m] * (double)k[L - 1 + n - m];
+    } else {
+      for (int m = 0; m < L; m++) acc += (double)u[m] * (double)k[((n - m) % L + L) % L];
+    }
+    y[n] = acc;
+  }
+}
+
+/* fp64 direct two-sided (layout 1, k [H][2L-1]) or circular (layout 2, k [H][L]) convolution of the
+ * listed sequences (s = b*H + h); y is [nseq][L]. */
+void oracle_direct_conv_layout_seqs(const float* u, const float* k, int layout, double* y, int B, int H, int L,
+                                    const long long* seqs, int nseq, int threads) {
+  (void)B;
+  const size_t width = layout == 1 ? (size_t)(2 * L - 1) : (size_t)L;
+#ifdef _OPENMP
+  if (threads <= 0) threads = omp_get_max_threads();
+#pragma omp parallel for schedule(dynamic, 1) num_threads(threads)
+#endif
+  for (int i = 0; i < nseq; i++) {
+    const long long s = seqs[i];
+    const int h = (int)(s % H);
+    conv_one_layout(u + (size_t)s * L, k + (size_t)h * width, y + (size_t)i * L, L, layout);
+  }
 }
 
 int oracle_max_threads(void) {

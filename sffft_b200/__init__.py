@@ -23,6 +23,7 @@ OK, ERR_INVALID_ARGUMENT, ERR_UNSUPPORTED, ERR_CUDA, ERR_DEVICE, ERR_TIMEOUT, ER
 IO = {"fp32": 0, "bf16": 1}
 ACC = {"fp32": 0, "fp16": 1}
 KERNEL = {"legacy": 0, "cached": 1}
+FILTER = {"causal": 0, "two_sided": 1, "circular": 2}
 
 _lib = None
 _emu = None
@@ -52,6 +53,7 @@ def _declare(lib):
         "sffft_plan_destroy": (I, [P]),
         "sffft_plan_info": (I, [P, ctypes.POINTER(PlanInfo)]),
         "sffft_filter_spectrum": (I, [P, V, I, I, V, V]),
+        "sffft_filter_spectrum_ex": (I, [P, V, I, I, I, V, V]),
         "sffft_conv": (I, [P, V, V, V, I, I, V]),
         "sffft_plan_check": (I, [P]),
         "sffft_catalog_count": (I, []),
@@ -184,14 +186,24 @@ class Plan:
         self.N = inf.N
         self.radices = [r for r in (inf.R0, inf.R1, inf.R2) if r > 1]
 
-    def filter_spectrum(self, k, Kf=None, stream=None):
-        """Kf [H][N] complex fp32 (as float32 [H, N, 2]) in digit order from the filter k [H][L]."""
+    def filter_spectrum(self, k, Kf=None, stream=None, layout="causal"):
+        """Kf [H][N] complex fp32 (as float32 [H, N, 2]) in digit order from the filter k.
+
+        layout "causal": k [H][L], conv gives y[n] = sum_{m<=n} u[m] k[n-m] (the reference's form);
+        "two_sided": k [H][2L-1], y[n] = sum_{m<L} u[m] k[L-1+n-m] (k[:, L-1] is lag 0);
+        "circular": k [H][L], y[n] = sum_{m<L} u[m] k[(n-m) mod L]."""
         import torch
+        if layout not in FILTER:
+            raise ValueError(f"layout must be one of {sorted(FILTER)}")
+        width = 2 * self.L - 1 if layout == "two_sided" else self.L
+        if k.dim() != 2 or k.shape[1] != width or k.dtype not in (torch.float32, torch.bfloat16) or not k.is_contiguous():
+            raise ValueError(f"k must be a contiguous [H][{width}] float32 or bfloat16 tensor for layout {layout!r}")
         H = k.shape[0]
         if Kf is None:
             Kf = torch.empty((H, self.N, 2), dtype=torch.float32, device=k.device)
         kd = IO["bf16"] if k.dtype == torch.bfloat16 else IO["fp32"]
-        _check(lib().sffft_filter_spectrum(self._h, _ptr(k), kd, H, _ptr(Kf), _stream(stream)), "filter_spectrum")
+        _check(lib().sffft_filter_spectrum_ex(self._h, _ptr(k), kd, FILTER[layout], H, _ptr(Kf), _stream(stream)),
+               "filter_spectrum")
         return Kf
 
     def conv(self, u, Kf, y=None, stream=None):

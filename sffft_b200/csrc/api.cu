@@ -13,7 +13,8 @@
 #include "registry.h"
 
 namespace sffft {
-cudaError_t launch_spectrum(float2* Kf, const void* k, bool k_bf16, int H, const int* R, int S, cudaStream_t stream);
+cudaError_t launch_spectrum(float2* Kf, const void* k, bool k_bf16, int layout, int H, const int* R, int S,
+                            cudaStream_t stream);
 struct Baseline;
 int baseline_create(Baseline** out, int L, int B, int H, const float* k_dev, int device);
 int baseline_run(Baseline* b, const float* u, float* y, int full, cudaStream_t st);
@@ -209,12 +210,18 @@ static int use_device(int device) {
 }
 
 int sffft_filter_spectrum(sffft_plan_t p, const void* k, int k_dtype, int H, void* Kf, void* stream) {
+  return sffft_filter_spectrum_ex(p, k, k_dtype, SFFFT_FILTER_CAUSAL, H, Kf, stream);
+}
+
+int sffft_filter_spectrum_ex(sffft_plan_t p, const void* k, int k_dtype, int layout, int H, void* Kf, void* stream) {
   if (!p || !k || !Kf || H < 1 || (k_dtype != SFFFT_IO_FP32 && k_dtype != SFFFT_IO_BF16)) return SFFFT_ERR_INVALID_ARGUMENT;
+  if (layout != SFFFT_FILTER_CAUSAL && layout != SFFFT_FILTER_TWO_SIDED && layout != SFFFT_FILTER_CIRCULAR)
+    return SFFFT_ERR_INVALID_ARGUMENT;
   if (((uintptr_t)Kf & 15) != 0) return SFFFT_ERR_INVALID_ARGUMENT;
   int rc = use_device(p->device);
   if (rc) return rc;
   const int R[3] = {p->e->R0, p->e->R1, p->e->R2};
-  const cudaError_t ce = launch_spectrum((float2*)Kf, k, k_dtype == SFFFT_IO_BF16, H, R, p->e->R2 > 1 ? 3 : 2,
+  const cudaError_t ce = launch_spectrum((float2*)Kf, k, k_dtype == SFFFT_IO_BF16, layout, H, R, p->e->R2 > 1 ? 3 : 2,
                                          (cudaStream_t)stream);
   return ce == cudaSuccess ? SFFFT_OK : cuda_fail(ce);
 }

@@ -6,16 +6,26 @@
 // stage j loads whole length-R_j vectors of a channel into shared memory, does a direct DFT with an
 // exact twiddle table (sincospif of a reduced rational argument), applies the four-step twiddle
 // w_N^(R0..R_{j-1} * inner * k_j) (the exponent of src/sffft.cu:106-113, unscaled), and writes the
-// vectors back.  Stage 0 reads the real filter (fp32 or bf16), zero-padded to N, directly.
+// vectors back.  Stage 0 reads the real filter (fp32 or bf16) directly and lays it out over the N = 2L
+// taps of the circular filter kw that the fused kernel applies to the zero-padded input:
+//   causal     k [H][L]:     kw[n] = k[n] for n < L, 0 above (the reference's zero padding);
+//   two-sided  k [H][2L-1]:  kw[n] = k[L-1+n] for n < L, kw[L] = 0, kw[N-j] = k[L-1-j] for 0 < j < L,
+//                            so y[n] = sum_{m<L} u[m] k[L-1+n-m] (k[L-1] is lag 0);
+//   circular   k [H][L]:     kw[n] = k[n mod L], so y[n] = sum_{m<L} u[m] k[(n-m) mod L] (period L).
+// The input is zero-padded to N in every case, so lags n - m in (-L, L) never alias; the reference
+// exposes only the causal form (README.md:174 lists non-causal and circular convolution as missing).
 // Like the reference's prep it runs once per channel and plan, outside the timed convolution.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "../../include/sffft.h"
+
 namespace sffft {
 
 struct SpecStage {
   int N, L, R, stride, pre;   // digit radix, stride of the digit, product of the radices before it
+  int layout;                 // filter layout of stage 0 (SFFFT_FILTER_*)
   int vec_per_cta;            // vectors handled by one CTA
   int twiddle;                // apply the inter-stage twiddle after this digit (not the last digit)
 };
@@ -43,8 +53,22 @@ __global__ void __launch_bounds__(256) spectrum_stage_kernel(float2* __restrict_
     const int outer = v / st.stride, inner = v - outer * st.stride;
     const int p = outer * R * st.stride + d * st.stride + inner;
     float2 val;
-    if constexpr (FIRST) val = make_float2(p < st.L ? k_to_float(k[(size_t)h * st.L + p]) : 0.f, 0.f);
-    else val = Kh[p];
+    if constexpr (FIRST) {
+      const int L = st.L;
+      int col = -1;   // column of the filter row that lands on tap p, or -1 for a zero tap
+      size_t row = (size_t)h * L;
+      if (st.layout == SFFFT_FILTER_TWO_SIDED) {
+        row = (size_t)h * (2 * L - 1);
+        col = p < L ? L - 1 + p : (p > L ? p - L - 1 : -1);   // tap N - j (0 < j < L) holds lag -j
+      } else if (st.layout == SFFFT_FILTER_CIRCULAR) {
+        col = p & (L - 1);
+      } else {
+        col = p < L ? p : -1;
+      }
+      val = make_float2(col >= 0 ? k_to_float(k[row + col]) : 0.f, 0.f);
+    } else {
+      val = Kh[p];
+    }
     x[i] = val;
   }
   __syncthreads();
@@ -71,16 +95,17 @@ __global__ void __launch_bounds__(256) spectrum_stage_kernel(float2* __restrict_
   }
 }
 
-// Runs the digit stages for radices R[0..S-1] over H channels of a filter of length L = N/2.
-// k_bf16: the filter holds bf16 values instead of fp32.
-cudaError_t launch_spectrum(float2* Kf, const void* k, bool k_bf16, int H, const int* R, int S, cudaStream_t stream) {
+// Runs the digit stages for radices R[0..S-1] over H channels of a filter for length L = N/2 in the
+// given layout.  k_bf16: the filter holds bf16 values instead of fp32.
+cudaError_t launch_spectrum(float2* Kf, const void* k, bool k_bf16, int layout, int H, const int* R, int S,
+                            cudaStream_t stream) {
   int N = 1;
   for (int j = 0; j < S; j++) N *= R[j];
   int stride = N, pre = 1;
   for (int j = 0; j < S; j++) {
     stride /= R[j];
     SpecStage st;
-    st.N = N; st.L = N / 2; st.R = R[j]; st.stride = stride; st.pre = pre; st.twiddle = (j + 1 < S);
+    st.N = N; st.L = N / 2; st.layout = layout; st.R = R[j]; st.stride = stride; st.pre = pre; st.twiddle = (j + 1 < S);
     const int vec_per_ch = N / R[j];
     st.vec_per_cta = vec_per_ch < 2048 / R[j] ? vec_per_ch : 2048 / R[j];
     const int grid = H * (vec_per_ch / st.vec_per_cta);

@@ -4,6 +4,8 @@
     Kf = torch.ops.sffft.filter_spectrum(k)            # k [H][L] fp32 or bf16 -> Kf [H][2L][2] fp32
     y = torch.ops.sffft.conv(u, Kf)                    # u [B][H][L] fp32 or bf16 -> y, same shape and type
     y = sffft_b200.torch_ops.causal_conv(u, k)         # both steps
+    y = sffft_b200.torch_ops.two_sided_conv(u, k2)     # non-causal: k2 [H][2L-1], k2[:, L-1] is lag 0
+    y = sffft_b200.torch_ops.circular_conv(u, kc)      # period-L circular: kc [H][L]
 
 Both run on the current CUDA stream of the tensors' device through sffft_filter_spectrum / sffft_conv, so
 they order with surrounding PyTorch work and can be captured in CUDA graphs once a first call has created
@@ -12,6 +14,8 @@ anything, so the operators trace under torch.compile.  Forward only: the path ha
 
 `acc` is "fp32" or "fp16" (accumulation mode); `config` names a catalog plan ("" = the default for L).
 filter_spectrum and conv must use the same config: the spectrum is in that plan's digit order.
+`layout` ("causal", "two_sided", "circular") says which convolution the spectrum makes conv compute; the
+fused kernel is the same for all three.
 """
 import threading
 
@@ -39,22 +43,35 @@ def _check_cuda(t: Tensor, what: str):
         raise ValueError(f"sffft::{what} needs CUDA tensors (there is no CPU path)")
 
 
-@torch.library.custom_op("sffft::filter_spectrum", mutates_args=())
-def filter_spectrum(k: Tensor, config: str = "") -> Tensor:
-    _check_cuda(k, "filter_spectrum")
+def _filter_length(k: Tensor, layout: str) -> int:
+    """The sequence length L a filter row of this layout belongs to."""
+    if layout not in sf.FILTER:
+        raise ValueError(f"layout must be one of {sorted(sf.FILTER)}")
     if k.dim() != 2 or k.dtype not in (torch.float32, torch.bfloat16):
-        raise ValueError("k must be [H][L], float32 or bfloat16")
-    H, L = k.shape
+        raise ValueError("k must be a 2-D float32 or bfloat16 tensor")
+    width = k.shape[1]
+    if layout == "two_sided":
+        if width % 2 == 0:
+            raise ValueError("a two-sided filter has 2L-1 taps")
+        return (width + 1) // 2
+    return width
+
+
+@torch.library.custom_op("sffft::filter_spectrum", mutates_args=())
+def filter_spectrum(k: Tensor, config: str = "", layout: str = "causal") -> Tensor:
+    _check_cuda(k, "filter_spectrum")
+    L = _filter_length(k, layout)
+    H = k.shape[0]
     dev = k.device.index if k.device.index is not None else torch.cuda.current_device()
     plan = _plan(L, "fp32", "fp32", config, dev)
     Kf = torch.empty((H, 2 * L, 2), dtype=torch.float32, device=k.device)
-    return plan.filter_spectrum(k.contiguous(), Kf, stream=torch.cuda.current_stream(k.device))
+    return plan.filter_spectrum(k.contiguous(), Kf, stream=torch.cuda.current_stream(k.device), layout=layout)
 
 
 @filter_spectrum.register_fake
-def _(k: Tensor, config: str = "") -> Tensor:
-    H, L = k.shape
-    return k.new_empty((H, 2 * L, 2), dtype=torch.float32)
+def _(k: Tensor, config: str = "", layout: str = "causal") -> Tensor:
+    L = _filter_length(k, layout)
+    return k.new_empty((k.shape[0], 2 * L, 2), dtype=torch.float32)
 
 
 @torch.library.custom_op("sffft::conv", mutates_args=())
@@ -81,3 +98,13 @@ def _(u: Tensor, Kf: Tensor, acc: str = "fp32", config: str = "") -> Tensor:
 def causal_conv(u: Tensor, k: Tensor, acc: str = "fp32", config: str = "") -> Tensor:
     """y[b,h,n] = sum_{m<=n} u[b,h,m] k[h,n-m]: the spectrum of k, then the fused convolution."""
     return conv(u, filter_spectrum(k, config), acc, config)
+
+
+def two_sided_conv(u: Tensor, k: Tensor, acc: str = "fp32", config: str = "") -> Tensor:
+    """Non-causal: y[b,h,n] = sum_{m<L} u[b,h,m] k[h,L-1+n-m] for k [H][2L-1] (k[:, L-1] is lag 0)."""
+    return conv(u, filter_spectrum(k, config, "two_sided"), acc, config)
+
+
+def circular_conv(u: Tensor, k: Tensor, acc: str = "fp32", config: str = "") -> Tensor:
+    """Period-L circular: y[b,h,n] = sum_{m<L} u[b,h,m] k[h,(n-m) mod L] for k [H][L]."""
+    return conv(u, filter_spectrum(k, config, "circular"), acc, config)

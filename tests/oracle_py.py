@@ -21,6 +21,7 @@ class Oracle:
         self.lib.oracle_gen_profile.argtypes = [ULL, I, I, I, D, I, V, V]
         self.lib.oracle_direct_conv.argtypes = [V, V, V, I, I, I, I]
         self.lib.oracle_direct_conv_seqs.argtypes = [V, V, V, I, I, I, V, I, I]
+        self.lib.oracle_direct_conv_layout_seqs.argtypes = [V, V, I, V, I, I, I, V, I, I]
         self.lib.oracle_max_threads.restype = I
 
     def nrand(self, seed, n):
@@ -56,6 +57,19 @@ class Oracle:
         y = np.zeros((len(seqs), L), np.float64)
         self.lib.oracle_direct_conv_seqs(u.ctypes.data, k.ctypes.data, y.ctypes.data, B, H, L, seqs.ctypes.data,
                                          len(seqs), threads)
+        return y
+
+    def direct_conv_layout_seqs(self, u, k, layout, seqs, threads=0):
+        """fp64 direct two-sided (k [H][2L-1]) or circular (k [H][L]) convolution of the listed sequences."""
+        code = {"two_sided": 1, "circular": 2}[layout]
+        u = np.ascontiguousarray(u, np.float32)
+        k = np.ascontiguousarray(k, np.float32)
+        B, H, L = u.shape
+        assert k.shape == (H, 2 * L - 1 if code == 1 else L)
+        seqs = np.ascontiguousarray(seqs, np.int64)
+        y = np.zeros((len(seqs), L), np.float64)
+        self.lib.oracle_direct_conv_layout_seqs(u.ctypes.data, k.ctypes.data, code, y.ctypes.data, B, H, L,
+                                                seqs.ctypes.data, len(seqs), threads)
         return y
 
     def max_threads(self):

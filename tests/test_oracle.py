@@ -99,3 +99,33 @@ def test_digit_order_spectrum_is_four_step_output():
         np.testing.assert_allclose(_four_step(x, R), spectrum_digit_order(k, R)[0], rtol=1e-9, atol=1e-9)
         # digit order is a permutation of the frequencies
         assert sorted(digit_order(R)) == list(range(N))
+
+
+def test_two_sided_and_circular_sums_match_numpy(oracle):
+    # two-sided: the full linear convolution of u with the 2L-1 taps, window starting at lag 0;
+    # circular: the period-L circular convolution through numpy's fp64 FFT
+    rng = np.random.default_rng(3)
+    B, H, L = 2, 3, 64
+    u = rng.standard_normal((B, H, L)).astype(np.float32)
+    k2 = rng.standard_normal((H, 2 * L - 1)).astype(np.float32)
+    kc = rng.standard_normal((H, L)).astype(np.float32)
+    seqs = np.arange(B * H)
+    y2 = oracle.direct_conv_layout_seqs(u, k2, "two_sided", seqs)
+    yc = oracle.direct_conv_layout_seqs(u, kc, "circular", seqs)
+    for s in seqs:
+        b, h = divmod(int(s), H)
+        full = np.convolve(u[b, h].astype(np.float64), k2[h].astype(np.float64))
+        assert rel_l2(y2[s], full[L - 1:2 * L - 1]) < 1e-14
+        circ = np.fft.ifft(np.fft.fft(u[b, h].astype(np.float64)) * np.fft.fft(kc[h].astype(np.float64))).real
+        assert rel_l2(yc[s], circ) < 1e-13
+
+
+def test_two_sided_with_zero_negative_lags_is_causal(oracle):
+    rng = np.random.default_rng(4)
+    B, H, L = 2, 2, 128
+    u = rng.standard_normal((B, H, L)).astype(np.float32)
+    k = rng.standard_normal((H, L)).astype(np.float32)
+    k2 = np.concatenate([np.zeros((H, L - 1), np.float32), k], axis=1)
+    seqs = np.arange(B * H)
+    np.testing.assert_array_equal(oracle.direct_conv_layout_seqs(u, k2, "two_sided", seqs),
+                                  oracle.direct_conv_seqs(u, k, seqs))

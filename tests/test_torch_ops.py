@@ -24,3 +24,14 @@ def test_cpu_tensors_are_refused():
         torch.ops.sffft.filter_spectrum(torch.zeros((2, 128)))
     with pytest.raises(ValueError):
         torch.ops.sffft.conv(torch.zeros((1, 2, 128)), torch.zeros((2, 256, 2)))
+
+
+def test_fake_shapes_of_filter_layouts():
+    k2 = torch.empty((6, 2 * 512 - 1), device="meta")
+    assert torch.ops.sffft.filter_spectrum(k2, "", "two_sided").shape == (6, 1024, 2)
+    kc = torch.empty((6, 512), device="meta")
+    assert torch.ops.sffft.filter_spectrum(kc, "", "circular").shape == (6, 1024, 2)
+    with pytest.raises(ValueError):
+        torch.ops.sffft.filter_spectrum(torch.empty((6, 512), device="meta"), "", "two_sided")
+    with pytest.raises(ValueError):
+        torch.ops.sffft.filter_spectrum(kc, "", "acausal")
