@@ -18,6 +18,8 @@
 #ifndef SFFFT_H_
 #define SFFFT_H_
 
+#include <stddef.h>
+
 #ifdef __cplusplus
 extern "C" {
 #endif
@@ -71,6 +73,19 @@ int sffft_filter_spectrum(sffft_plan_t plan, const void* k, int k_dtype, int H, 
  * convolution are listed as not yet exposed (README.md:174). */
 int sffft_filter_spectrum_ex(sffft_plan_t plan, const void* k, int k_dtype, int layout, int H, void* Kf,
                              void* stream);
+
+/* Standalone real FFTs of length N = 2L (the plan's N) over B rows, on the same digit decomposition as
+ * the filter-spectrum prep (fp32 CUDA cores, exact twiddles); no reference counterpart (README.md:174
+ * lists standalone forward and inverse FFTs as not yet exposed).
+ *   sffft_rfft:  x [B][N] real (x_dtype SFFFT_IO_FP32 or SFFFT_IO_BF16) -> X [B][N/2+1] complex fp32,
+ *                X[f] = sum_n x[n] exp(-2 pi i f n / N)              (numpy.fft.rfft)
+ *   sffft_irfft: X [B][N/2+1] complex fp32 -> x [B][N] fp32,
+ *                x[n] = (1/N) sum_f Xfull[f] exp(+2 pi i f n / N)    (numpy.fft.irfft; the imaginary
+ *                parts of X[0] and X[N/2] are ignored)
+ * work: caller-owned device buffer of sffft_fft_workspace_bytes(plan, B) bytes, 8-byte aligned. */
+int sffft_fft_workspace_bytes(sffft_plan_t plan, int B, size_t* bytes);
+int sffft_rfft(sffft_plan_t plan, const void* x, int x_dtype, int B, void* X, void* work, void* stream);
+int sffft_irfft(sffft_plan_t plan, const void* X, int B, float* x, void* work, void* stream);
 
 /* The fused convolution: one kernel launch per call.  Replaces the launch
  * fftconv<P,W,TIO,TAcc,CACHED><<<B*H, 32*W, smem>>>(u, Kf, tw, dft, y, B, H) (src/sffft.cu:243-280,

@@ -54,6 +54,9 @@ def _declare(lib):
         "sffft_plan_info": (I, [P, ctypes.POINTER(PlanInfo)]),
         "sffft_filter_spectrum": (I, [P, V, I, I, V, V]),
         "sffft_filter_spectrum_ex": (I, [P, V, I, I, I, V, V]),
+        "sffft_fft_workspace_bytes": (I, [P, I, ctypes.POINTER(ctypes.c_size_t)]),
+        "sffft_rfft": (I, [P, V, I, I, V, V, V]),
+        "sffft_irfft": (I, [P, V, I, V, V, V]),
         "sffft_conv": (I, [P, V, V, V, I, I, V]),
         "sffft_plan_check": (I, [P]),
         "sffft_catalog_count": (I, []),
@@ -205,6 +208,43 @@ class Plan:
         _check(lib().sffft_filter_spectrum_ex(self._h, _ptr(k), kd, FILTER[layout], H, _ptr(Kf), _stream(stream)),
                "filter_spectrum")
         return Kf
+
+    def _fft_work(self, rows, work, device):
+        import torch
+        need = ctypes.c_size_t()
+        _check(lib().sffft_fft_workspace_bytes(self._h, rows, ctypes.byref(need)), "fft_workspace_bytes")
+        if work is None:
+            return torch.empty(need.value // 4, dtype=torch.float32, device=device)
+        if work.numel() * work.element_size() < need.value:
+            raise ValueError(f"workspace of {need.value} bytes needed")
+        return work
+
+    def rfft(self, x, X=None, work=None, stream=None):
+        """X [..., N/2+1] complex64 = the length-N real DFT of x [..., N] (fp32 or bf16), numpy.fft.rfft's
+        definition; N = 2L is the plan's transform length."""
+        import torch
+        if x.shape[-1] != self.N or x.dtype not in (torch.float32, torch.bfloat16) or not x.is_contiguous():
+            raise ValueError(f"x must be a contiguous [..., {self.N}] float32 or bfloat16 tensor")
+        rows = x.numel() // self.N
+        if X is None:
+            X = torch.empty(tuple(x.shape[:-1]) + (self.N // 2 + 1,), dtype=torch.complex64, device=x.device)
+        work = self._fft_work(rows, work, x.device)
+        kd = IO["bf16"] if x.dtype == torch.bfloat16 else IO["fp32"]
+        _check(lib().sffft_rfft(self._h, _ptr(x), kd, rows, _ptr(X), _ptr(work), _stream(stream)), "rfft")
+        return X
+
+    def irfft(self, X, x=None, work=None, stream=None):
+        """x [..., N] fp32 = the inverse of rfft for the half spectrum X [..., N/2+1] complex64
+        (numpy.fft.irfft's definition, 1/N included)."""
+        import torch
+        if X.shape[-1] != self.N // 2 + 1 or X.dtype != torch.complex64 or not X.is_contiguous():
+            raise ValueError(f"X must be a contiguous [..., {self.N // 2 + 1}] complex64 tensor")
+        rows = X.numel() // (self.N // 2 + 1)
+        if x is None:
+            x = torch.empty(tuple(X.shape[:-1]) + (self.N,), dtype=torch.float32, device=X.device)
+        work = self._fft_work(rows, work, X.device)
+        _check(lib().sffft_irfft(self._h, _ptr(X), rows, _ptr(x), _ptr(work), _stream(stream)), "irfft")
+        return x
 
     def conv(self, u, Kf, y=None, stream=None):
         """y = causal_conv(u, k) for u [B][H][L] with the spectrum Kf of k."""

@@ -14,7 +14,11 @@
 
 namespace sffft {
 cudaError_t launch_spectrum(float2* Kf, const void* k, bool k_bf16, int layout, int H, const int* R, int S,
-                            cudaStream_t stream);
+                            cudaStream_t stream, bool hermitian);
+cudaError_t launch_rfft(const void* x, bool x_bf16, int rows, float2* X, float2* W, const int* R, int S, int sms,
+                        cudaStream_t stream);
+cudaError_t launch_irfft(const float2* X, int rows, float* x, float2* W, const int* R, int S, int sms,
+                         cudaStream_t stream);
 struct Baseline;
 int baseline_create(Baseline** out, int L, int B, int H, const float* k_dev, int device);
 int baseline_run(Baseline* b, const float* u, float* y, int full, cudaStream_t st);
@@ -222,7 +226,37 @@ int sffft_filter_spectrum_ex(sffft_plan_t p, const void* k, int k_dtype, int lay
   if (rc) return rc;
   const int R[3] = {p->e->R0, p->e->R1, p->e->R2};
   const cudaError_t ce = launch_spectrum((float2*)Kf, k, k_dtype == SFFFT_IO_BF16, layout, H, R, p->e->R2 > 1 ? 3 : 2,
-                                         (cudaStream_t)stream);
+                                         (cudaStream_t)stream, false);
+  return ce == cudaSuccess ? SFFFT_OK : cuda_fail(ce);
+}
+
+int sffft_fft_workspace_bytes(sffft_plan_t p, int B, size_t* bytes) {
+  if (!p || !bytes || B < 1) return SFFFT_ERR_INVALID_ARGUMENT;
+  *bytes = (size_t)B * p->e->N * sizeof(float2);
+  return SFFFT_OK;
+}
+
+int sffft_rfft(sffft_plan_t p, const void* x, int x_dtype, int B, void* X, void* work, void* stream) {
+  if (!p || !x || !X || !work || B < 1 || (x_dtype != SFFFT_IO_FP32 && x_dtype != SFFFT_IO_BF16))
+    return SFFFT_ERR_INVALID_ARGUMENT;
+  if ((((uintptr_t)X | (uintptr_t)work) & 7) != 0 || ((uintptr_t)x & (x_dtype == SFFFT_IO_BF16 ? 1 : 3)) != 0)
+    return SFFFT_ERR_INVALID_ARGUMENT;
+  int rc = use_device(p->device);
+  if (rc) return rc;
+  const int R[3] = {p->e->R0, p->e->R1, p->e->R2};
+  const cudaError_t ce = launch_rfft(x, x_dtype == SFFFT_IO_BF16, B, (float2*)X, (float2*)work, R,
+                                     p->e->R2 > 1 ? 3 : 2, p->sms, (cudaStream_t)stream);
+  return ce == cudaSuccess ? SFFFT_OK : cuda_fail(ce);
+}
+
+int sffft_irfft(sffft_plan_t p, const void* X, int B, float* x, void* work, void* stream) {
+  if (!p || !X || !x || !work || B < 1) return SFFFT_ERR_INVALID_ARGUMENT;
+  if ((((uintptr_t)X | (uintptr_t)work) & 7) != 0 || ((uintptr_t)x & 3) != 0) return SFFFT_ERR_INVALID_ARGUMENT;
+  int rc = use_device(p->device);
+  if (rc) return rc;
+  const int R[3] = {p->e->R0, p->e->R1, p->e->R2};
+  const cudaError_t ce = launch_irfft((const float2*)X, B, x, (float2*)work, R, p->e->R2 > 1 ? 3 : 2, p->sms,
+                                      (cudaStream_t)stream);
   return ce == cudaSuccess ? SFFFT_OK : cuda_fail(ce);
 }
 

@@ -33,7 +33,14 @@ struct SpecStage {
 __device__ __forceinline__ float k_to_float(float v) { return v; }
 __device__ __forceinline__ float k_to_float(__nv_bfloat16 v) { return __bfloat162float(v); }
 
-template <class TK, bool FIRST>
+// Where stage 0 takes its input from: the buffer itself (later stages), a real row per channel placed
+// by a filter layout (kLayoutFull: all N samples, the standalone forward FFT), or the conjugated
+// Hermitian extension of a half spectrum [N/2 + 1] (the standalone inverse FFT, computed as
+// conj(DFT(conj(X))) / N).
+enum { kSrcInPlace = 0, kSrcReal = 1, kSrcHermitian = 2 };
+constexpr int kLayoutFull = 3;
+
+template <class TK, int SRC>
 __global__ void __launch_bounds__(256) spectrum_stage_kernel(float2* __restrict__ Kf, const TK* __restrict__ k, SpecStage st) {
   extern __shared__ float2 sbuf[];
   float2* tab = sbuf;                 // w_R^q, q in [0, R)
@@ -53,7 +60,15 @@ __global__ void __launch_bounds__(256) spectrum_stage_kernel(float2* __restrict_
     const int outer = v / st.stride, inner = v - outer * st.stride;
     const int p = outer * R * st.stride + d * st.stride + inner;
     float2 val;
-    if constexpr (FIRST) {
+    if constexpr (SRC == kSrcHermitian) {
+      const float2* X = reinterpret_cast<const float2*>(k) + (size_t)h * (N / 2 + 1);
+      if (p <= N / 2) {
+        const float2 xv = X[p];
+        val = make_float2(xv.x, (p == 0 || p == N / 2) ? 0.f : -xv.y);
+      } else {
+        val = X[N - p];
+      }
+    } else if constexpr (SRC == kSrcReal) {
       const int L = st.L;
       int col = -1;   // column of the filter row that lands on tap p, or -1 for a zero tap
       size_t row = (size_t)h * L;
@@ -62,6 +77,9 @@ __global__ void __launch_bounds__(256) spectrum_stage_kernel(float2* __restrict_
         col = p < L ? L - 1 + p : (p > L ? p - L - 1 : -1);   // tap N - j (0 < j < L) holds lag -j
       } else if (st.layout == SFFFT_FILTER_CIRCULAR) {
         col = p & (L - 1);
+      } else if (st.layout == kLayoutFull) {
+        row = (size_t)h * N;
+        col = p;
       } else {
         col = p < L ? p : -1;
       }
@@ -95,10 +113,29 @@ __global__ void __launch_bounds__(256) spectrum_stage_kernel(float2* __restrict_
   }
 }
 
+// Natural order out of the digit-order buffer W [rows][N]: the forward FFT writes the half spectrum
+// X[f] = W[pos(f)], f <= N/2; the inverse writes x[n] = Re W[pos(n)] / N (W = DFT(conj(Xfull)), whose
+// conjugate has the same real part).  pos(f) = k0*R1*R2 + k1*R2 + k2 for f = k0 + R0*k1 + R0*R1*k2.
+template <bool INV>
+__global__ void __launch_bounds__(256) fft_gather_kernel(const float2* __restrict__ W, void* __restrict__ out, int rows,
+                                                         int R0, int R1, int R2) {
+  const int N = R0 * R1 * R2, width = INV ? N : N / 2 + 1;
+  const long long total = (long long)rows * width;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i / width;
+    const int f = (int)(i - r * width);
+    const int k0 = f % R0, k1 = (f / R0) % R1, k2 = f / (R0 * R1);
+    const float2 v = W[r * N + (k0 * R1 + k1) * R2 + k2];
+    if constexpr (INV) reinterpret_cast<float*>(out)[i] = v.x * (1.0f / (float)N);
+    else reinterpret_cast<float2*>(out)[i] = v;
+  }
+}
+
 // Runs the digit stages for radices R[0..S-1] over H channels of a filter for length L = N/2 in the
-// given layout.  k_bf16: the filter holds bf16 values instead of fp32.
+// given layout.  k_bf16: the filter holds bf16 values instead of fp32.  hermitian: k is a half spectrum
+// [H][N/2 + 1] of float2 for the inverse FFT (layout and k_bf16 unused).
 cudaError_t launch_spectrum(float2* Kf, const void* k, bool k_bf16, int layout, int H, const int* R, int S,
-                            cudaStream_t stream) {
+                            cudaStream_t stream, bool hermitian) {
   int N = 1;
   for (int j = 0; j < S; j++) N *= R[j];
   int stride = N, pre = 1;
@@ -110,17 +147,37 @@ cudaError_t launch_spectrum(float2* Kf, const void* k, bool k_bf16, int layout, 
     st.vec_per_cta = vec_per_ch < 2048 / R[j] ? vec_per_ch : 2048 / R[j];
     const int grid = H * (vec_per_ch / st.vec_per_cta);
     const size_t smem = (size_t)(st.R + st.vec_per_cta * st.R) * sizeof(float2);
-    if (j == 0) {
-      if (k_bf16) spectrum_stage_kernel<__nv_bfloat16, true><<<grid, 256, smem, stream>>>(Kf, (const __nv_bfloat16*)k, st);
-      else spectrum_stage_kernel<float, true><<<grid, 256, smem, stream>>>(Kf, (const float*)k, st);
+    if (j == 0 && hermitian) {
+      spectrum_stage_kernel<float2, kSrcHermitian><<<grid, 256, smem, stream>>>(Kf, (const float2*)k, st);
+    } else if (j == 0) {
+      if (k_bf16) spectrum_stage_kernel<__nv_bfloat16, kSrcReal><<<grid, 256, smem, stream>>>(Kf, (const __nv_bfloat16*)k, st);
+      else spectrum_stage_kernel<float, kSrcReal><<<grid, 256, smem, stream>>>(Kf, (const float*)k, st);
     } else {
-      spectrum_stage_kernel<float, false><<<grid, 256, smem, stream>>>(Kf, nullptr, st);
+      spectrum_stage_kernel<float, kSrcInPlace><<<grid, 256, smem, stream>>>(Kf, nullptr, st);
     }
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     pre *= R[j];
   }
   return cudaSuccess;
+}
+
+// Standalone real FFTs of length N = R0*R1*R2 over `rows` rows, through the digit stages in the caller's
+// workspace W [rows][N] and one gather into natural order.
+cudaError_t launch_rfft(const void* x, bool x_bf16, int rows, float2* X, float2* W, const int* R, int S, int sms,
+                        cudaStream_t stream) {
+  cudaError_t e = launch_spectrum(W, x, x_bf16, kLayoutFull, rows, R, S, stream, false);
+  if (e != cudaSuccess) return e;
+  fft_gather_kernel<false><<<sms * 8, 256, 0, stream>>>(W, X, rows, R[0], R[1], S > 2 ? R[2] : 1);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_irfft(const float2* X, int rows, float* x, float2* W, const int* R, int S, int sms,
+                         cudaStream_t stream) {
+  cudaError_t e = launch_spectrum(W, X, false, 0, rows, R, S, stream, true);
+  if (e != cudaSuccess) return e;
+  fft_gather_kernel<true><<<sms * 8, 256, 0, stream>>>(W, x, rows, R[0], R[1], S > 2 ? R[2] : 1);
+  return cudaGetLastError();
 }
 
 }  // namespace sffft

@@ -6,6 +6,8 @@
     y = sffft_b200.torch_ops.causal_conv(u, k)         # both steps
     y = sffft_b200.torch_ops.two_sided_conv(u, k2)     # non-causal: k2 [H][2L-1], k2[:, L-1] is lag 0
     y = sffft_b200.torch_ops.circular_conv(u, kc)      # period-L circular: kc [H][L]
+    X = torch.ops.sffft.rfft(x)                        # x [..., N] fp32/bf16 -> X [..., N/2+1] complex64
+    x = torch.ops.sffft.irfft(X)                       # X [..., N/2+1] complex64 -> x [..., N] fp32
 
 Both run on the current CUDA stream of the tensors' device through sffft_filter_spectrum / sffft_conv, so
 they order with surrounding PyTorch work and can be captured in CUDA graphs once a first call has created
@@ -108,3 +110,40 @@ def two_sided_conv(u: Tensor, k: Tensor, acc: str = "fp32", config: str = "") ->
 def circular_conv(u: Tensor, k: Tensor, acc: str = "fp32", config: str = "") -> Tensor:
     """Period-L circular: y[b,h,n] = sum_{m<L} u[b,h,m] k[h,(n-m) mod L] for k [H][L]."""
     return conv(u, filter_spectrum(k, config, "circular"), acc, config)
+
+
+def _fft_plan(N: int, config: str, device) -> "sf.Plan":
+    if N < 256 or N & (N - 1):
+        raise ValueError("the transform length must be a power of two from 256 to 32768")
+    dev = device.index if device.index is not None else torch.cuda.current_device()
+    return _plan(N // 2, "fp32", "fp32", config, dev)
+
+
+@torch.library.custom_op("sffft::rfft", mutates_args=())
+def rfft(x: Tensor, config: str = "") -> Tensor:
+    """Real DFT along the last axis (numpy.fft.rfft), fp32 with exact twiddles."""
+    _check_cuda(x, "rfft")
+    if x.dtype not in (torch.float32, torch.bfloat16):
+        raise ValueError("x must be float32 or bfloat16")
+    plan = _fft_plan(x.shape[-1], config, x.device)
+    return plan.rfft(x.contiguous(), stream=torch.cuda.current_stream(x.device))
+
+
+@rfft.register_fake
+def _(x: Tensor, config: str = "") -> Tensor:
+    return x.new_empty(tuple(x.shape[:-1]) + (x.shape[-1] // 2 + 1,), dtype=torch.complex64)
+
+
+@torch.library.custom_op("sffft::irfft", mutates_args=())
+def irfft(X: Tensor, config: str = "") -> Tensor:
+    """Inverse of rfft for an even length N = 2 (X.shape[-1] - 1) (numpy.fft.irfft)."""
+    _check_cuda(X, "irfft")
+    if X.dtype != torch.complex64:
+        raise ValueError("X must be complex64")
+    plan = _fft_plan(2 * (X.shape[-1] - 1), config, X.device)
+    return plan.irfft(X.contiguous(), stream=torch.cuda.current_stream(X.device))
+
+
+@irfft.register_fake
+def _(X: Tensor, config: str = "") -> Tensor:
+    return X.new_empty(tuple(X.shape[:-1]) + (2 * (X.shape[-1] - 1),), dtype=torch.float32)

@@ -30,10 +30,11 @@ def cuda_device():
 
 
 def rel_l2(a, b):
-    a = np.asarray(a, dtype=np.float64)
-    b = np.asarray(b, dtype=np.float64)
-    d = float(np.sum((a - b) ** 2))
-    r = float(np.sum(b ** 2))
+    cplx = np.iscomplexobj(a) or np.iscomplexobj(b)
+    a = np.asarray(a, dtype=np.complex128 if cplx else np.float64)
+    b = np.asarray(b, dtype=np.complex128 if cplx else np.float64)
+    d = float(np.sum(np.abs(a - b) ** 2))
+    r = float(np.sum(np.abs(b) ** 2))
     if r > 0:
         return (d / r) ** 0.5
     return 0.0 if d == 0 else float("inf")

@@ -80,6 +80,8 @@ def test_null_handles_are_rejected():
     assert lib.sffft_conv(None, 16, 16, 16, 1, 1, None) == sf.ERR_INVALID_ARGUMENT
     assert lib.sffft_filter_spectrum(None, 16, 0, 1, 16, None) == sf.ERR_INVALID_ARGUMENT
     assert lib.sffft_filter_spectrum_ex(None, 16, 0, 1, 1, 16, None) == sf.ERR_INVALID_ARGUMENT
+    assert lib.sffft_rfft(None, 16, 0, 1, 16, 16, None) == sf.ERR_INVALID_ARGUMENT
+    assert lib.sffft_irfft(None, 16, 1, 16, 16, None) == sf.ERR_INVALID_ARGUMENT
     assert lib.sffft_plan_destroy(None) == sf.ERR_INVALID_ARGUMENT
     assert lib.sffft_plan_check(None) == sf.ERR_INVALID_ARGUMENT
     assert lib.sffft_baseline_destroy(None) == sf.ERR_INVALID_ARGUMENT

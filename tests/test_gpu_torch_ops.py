@@ -30,3 +30,12 @@ def test_ops_equal_plan_api(L, io, acc):
     s.synchronize()
     assert torch.equal(y2, ref)
     plan.close()
+
+
+def test_fft_operators(cuda_device):
+    x = torch.randn((2, 3, 1024), device=cuda_device)
+    X = torch.ops.sffft.rfft(x)
+    ref = torch.fft.rfft(x.double())
+    assert (torch.linalg.norm(X.cdouble() - ref) / torch.linalg.norm(ref)).item() < 3e-6
+    xr = torch.ops.sffft.irfft(X)
+    assert (torch.linalg.norm(xr - x) / torch.linalg.norm(x)).item() < 3e-6

@@ -35,3 +35,12 @@ def test_fake_shapes_of_filter_layouts():
         torch.ops.sffft.filter_spectrum(torch.empty((6, 512), device="meta"), "", "two_sided")
     with pytest.raises(ValueError):
         torch.ops.sffft.filter_spectrum(kc, "", "acausal")
+
+
+def test_fake_shapes_of_ffts():
+    X = torch.ops.sffft.rfft(torch.empty((3, 4, 2048), device="meta"))
+    assert X.shape == (3, 4, 1025) and X.dtype == torch.complex64
+    x = torch.ops.sffft.irfft(X)
+    assert x.shape == (3, 4, 2048) and x.dtype == torch.float32
+    with pytest.raises(ValueError):
+        torch.ops.sffft.rfft(torch.zeros((2, 256)))
