@@ -48,12 +48,19 @@ typedef struct {
   int pairs_per_cta;   /* G: pairs of batch elements (same channel) per CTA */
   int warps, threads, smem_bytes, tmem_cols, occupancy;
   int io, acc, kernel_mode, device;
-  char config[96];     /* catalog name, e.g. "64x32/w4" */
+  int blocks;          /* 1, or the block count of a composite plan (L = blocks * block length) */
+  char config[96];     /* catalog name, e.g. "64x32/w4", or "2x[32x32x32/w8]" for a composite plan */
 } sffft_plan_info_t;
 
-/* Creates a plan for length L (128..16384, power of two).  config: catalog name ("64x32/w4"), or NULL /
- * "" for the built-in B200 default for L.  Replaces the compile-time choice of fftconv<Plan<R0,R1,R2>,W,
- * TIO,TAcc,CACHED> plus its cudaFuncSetAttribute / occupancy setup (src/sffft.cu:243-245, 385-388). */
+/* Creates a plan for length L (power of two).  config: catalog name ("64x32/w4") for L = 128..16384, or
+ * NULL / "" for the built-in B200 default for L.  Replaces the compile-time choice of fftconv<Plan<R0,R1,R2>,
+ * W,TIO,TAcc,CACHED> plus its cudaFuncSetAttribute / occupancy setup (src/sffft.cu:243-245, 385-388).
+ * Composite plans (no reference counterpart; the reference stops at L = 8192 and lists multi-pass plans
+ * as missing, README.md:175): config "<P>x[<catalog name>]" runs L = P * Lb (P = 2..16) as a block
+ * convolution on the catalog plan of length Lb, and the default for L = 32768 .. 262144 is
+ * "<L/16384>x[<default for 16384>]".  For a composite plan Kf holds the P block spectra [P][H][2 Lb]
+ * (the same H * 2L complex values), filter layouts other than causal are unsupported, and sffft_conv
+ * takes a stream-ordered workspace of (P + P (P + 1) / 2) * B * H * Lb elements for the call. */
 int sffft_plan_create(sffft_plan_t* plan, int L, int io, int acc, const char* config, int kernel_mode, int device);
 int sffft_plan_destroy(sffft_plan_t plan);
 int sffft_plan_info(sffft_plan_t plan, sffft_plan_info_t* info);

@@ -38,7 +38,7 @@ class SffftError(RuntimeError):
 class PlanInfo(ctypes.Structure):
     _fields_ = [(n, ctypes.c_int) for n in (
         "L", "N", "stages", "R0", "R1", "R2", "pairs_per_cta", "warps", "threads", "smem_bytes",
-        "tmem_cols", "occupancy", "io", "acc", "kernel_mode", "device")] + [("config", ctypes.c_char * 96)]
+        "tmem_cols", "occupancy", "io", "acc", "kernel_mode", "device", "blocks")] + [("config", ctypes.c_char * 96)]
 
 
 class _Candidate(ctypes.Structure):
@@ -187,7 +187,10 @@ class Plan:
         self.info["config"] = inf.config.decode()
         self.config = self.info["config"]
         self.N = inf.N
+        self.blocks = inf.blocks
+        # digits of the length-N transform; a composite plan's last digit spans its blocks
         self.radices = [r for r in (inf.R0, inf.R1, inf.R2) if r > 1]
+        self.radices[-1] *= self.blocks
 
     def filter_spectrum(self, k, Kf=None, stream=None, layout="causal"):
         """Kf [H][N] complex fp32 (as float32 [H, N, 2]) in digit order from the filter k.

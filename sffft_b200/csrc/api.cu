@@ -11,10 +11,9 @@
 #include "../../include/sffft.h"
 #include "fused_conv.cuh"
 #include "registry.h"
+#include "spectrum.h"
 
 namespace sffft {
-cudaError_t launch_spectrum(float2* Kf, const void* k, bool k_bf16, int layout, int H, const int* R, int S,
-                            cudaStream_t stream, bool hermitian);
 cudaError_t launch_rfft(const void* x, bool x_bf16, int rows, float2* X, float2* W, const int* R, int S, int sms,
                         cudaStream_t stream);
 cudaError_t launch_irfft(const float2* X, int rows, float* x, float2* W, const int* R, int S, int sms,
@@ -31,7 +30,9 @@ int wait_timeout_probe(int limit_us);
 using namespace sffft;
 
 struct sffft_plan {
-  const ConvEntry* e;
+  const ConvEntry* e;   // the fused kernel's plan (the block plan of a composite plan)
+  int blocks, L;        // composite plans: L = blocks * e->L (blocks = 1: the plan itself)
+  int kio;              // I/O type of the fused kernel launches (fp32 for composite plans)
   int io, acc, kernel_mode, device, occupancy, smem_launch, sms;
   uint4* btab;   // cached DFT-matrix image (device), null in legacy mode
   int* status;   // device status word
@@ -68,6 +69,10 @@ static const std::vector<const ConvEntry*>& catalog() {
 // Built-in B200 default per length: the fastest catalog entry of the plan BASELINE-style workloads name for
 // that length (B = 8, H = 768, fp32 and bf16 I/O, timed on one B200); the CLI's empirical selector can
 // override it from its own measurements.
+// Composite plans: lengths above the largest single-kernel plan run as block convolutions of up to
+// kMaxBlocks blocks (the work grows as blocks * (blocks + 1) / 2 block convolutions).
+constexpr int kMaxBlockL = 16384, kMaxBlocks = 16;
+
 static const char* default_for(int L) {
   switch (L) {
     case 128: return "16x16/w8";
@@ -128,12 +133,32 @@ int sffft_plan_create(sffft_plan_t* out, int L, int io, int acc, const char* con
   if ((io != SFFFT_IO_FP32 && io != SFFFT_IO_BF16) || (acc != SFFFT_ACC_FP32 && acc != SFFFT_ACC_FP16) ||
       (kernel_mode != SFFFT_KERNEL_LEGACY && kernel_mode != SFFFT_KERNEL_CACHED) || device < 0)
     return SFFFT_ERR_INVALID_ARGUMENT;
-  const char* want = (config && *config) ? config : default_for(L);
-  if (!want) return SFFFT_ERR_UNSUPPORTED;
+  // A composite plan "<P>x[<block plan>]" runs lengths L = P * Lb as block convolutions on the block plan;
+  // lengths above the largest catalog plan get one by default.
+  int blocks = 1;
+  std::string want;
+  if (config && *config) {
+    want = config;
+    const size_t lb = want.find("x["), n = want.size();
+    if (lb != std::string::npos && lb > 0 && n > lb + 3 && want[n - 1] == ']' &&
+        want.find_first_not_of("0123456789") == lb) {
+      blocks = std::atoi(want.substr(0, lb).c_str());
+      want = want.substr(lb + 2, n - lb - 3);
+      if (blocks < 2 || blocks > kMaxBlocks || (blocks & (blocks - 1))) return SFFFT_ERR_UNSUPPORTED;
+    }
+  } else if (default_for(L)) {
+    want = default_for(L);
+  } else if (L > kMaxBlockL && L % kMaxBlockL == 0) {
+    blocks = L / kMaxBlockL;
+    want = default_for(kMaxBlockL);
+    if (blocks > kMaxBlocks || (blocks & (blocks - 1))) return SFFFT_ERR_UNSUPPORTED;
+  } else {
+    return SFFFT_ERR_UNSUPPORTED;
+  }
   const ConvEntry* e = nullptr;
   for (const ConvEntry* c : catalog())
-    if (std::strcmp(c->name, want) == 0) e = c;
-  if (!e || e->L != L) return SFFFT_ERR_UNSUPPORTED;
+    if (want == c->name) e = c;
+  if (!e || (long long)e->L * blocks != L) return SFFFT_ERR_UNSUPPORTED;
 
   int ndev = 0;
   cudaError_t ce = cudaGetDeviceCount(&ndev);
@@ -142,7 +167,9 @@ int sffft_plan_create(sffft_plan_t* out, int L, int io, int acc, const char* con
   if ((ce = cudaSetDevice(device)) != cudaSuccess) return cuda_fail(ce);
   cudaDeviceProp prop;
   if ((ce = cudaGetDeviceProperties(&prop, device)) != cudaSuccess) return cuda_fail(ce);
-  const int need = e->smem_bytes[io];
+  // a composite plan runs its blocks through the block plan's fp32-I/O kernel (fp32 partial sums)
+  const int kio = blocks > 1 ? SFFFT_IO_FP32 : io;
+  const int need = e->smem_bytes[kio];
   if (prop.major != 10 || prop.minor != 0 || (int)prop.sharedMemPerBlockOptin < need) return SFFFT_ERR_DEVICE;
 
   // The kernel is persistent with one CTA per SM (the grid never exceeds the SM count).  Requesting
@@ -151,13 +178,14 @@ int sffft_plan_create(sffft_plan_t* out, int L, int io, int acc, const char* con
   const int half = (int)prop.sharedMemPerMultiprocessor / 2 + 1024;
   if (smem_launch < half) smem_launch = half;
   if (smem_launch > (int)prop.sharedMemPerBlockOptin) smem_launch = (int)prop.sharedMemPerBlockOptin;
-  const void* fn = e->func[io][acc];
+  const void* fn = e->func[kio][acc];
   if ((ce = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_launch)) != cudaSuccess)
     return cuda_fail(ce);
   const int occ = 1;
 
   sffft_plan* p = new sffft_plan();
-  p->e = e; p->io = io; p->acc = acc; p->kernel_mode = kernel_mode; p->device = device;
+  p->e = e; p->blocks = blocks; p->L = L; p->kio = kio;
+  p->io = io; p->acc = acc; p->kernel_mode = kernel_mode; p->device = device;
   p->occupancy = occ; p->smem_launch = smem_launch; p->sms = prop.multiProcessorCount;
   p->btab = nullptr; p->status = nullptr;
   if ((ce = cudaMalloc(&p->status, sizeof(int))) != cudaSuccess || (ce = cudaMemset(p->status, 0, sizeof(int))) != cudaSuccess) {
@@ -195,13 +223,14 @@ int sffft_plan_info(sffft_plan_t p, sffft_plan_info_t* info) {
   if (!p || !info) return SFFFT_ERR_INVALID_ARGUMENT;
   const ConvEntry* e = p->e;
   std::memset(info, 0, sizeof(*info));
-  info->L = e->L; info->N = e->N; info->stages = e->R2 > 1 ? 3 : 2;
+  info->L = p->L; info->N = 2 * p->L; info->blocks = p->blocks; info->stages = e->R2 > 1 ? 3 : 2;
   info->R0 = e->R0; info->R1 = e->R1; info->R2 = e->R2; info->pairs_per_cta = e->G;
-  info->warps = e->W; info->threads = e->threads; info->smem_bytes = e->smem_bytes[p->io];
-  info->tmem_cols = e->tmem_cols[p->io];
+  info->warps = e->W; info->threads = e->threads; info->smem_bytes = e->smem_bytes[p->kio];
+  info->tmem_cols = e->tmem_cols[p->kio];
   info->occupancy = p->occupancy; info->io = p->io; info->acc = p->acc; info->kernel_mode = p->kernel_mode;
   info->device = p->device;
-  std::strncpy(info->config, e->name, sizeof(info->config) - 1);
+  if (p->blocks > 1) std::snprintf(info->config, sizeof(info->config), "%dx[%s]", p->blocks, e->name);
+  else std::strncpy(info->config, e->name, sizeof(info->config) - 1);
   return SFFFT_OK;
 }
 
@@ -224,16 +253,38 @@ int sffft_filter_spectrum_ex(sffft_plan_t p, const void* k, int k_dtype, int lay
   if (((uintptr_t)Kf & 15) != 0) return SFFFT_ERR_INVALID_ARGUMENT;
   int rc = use_device(p->device);
   if (rc) return rc;
-  const int R[3] = {p->e->R0, p->e->R1, p->e->R2};
-  const cudaError_t ce = launch_spectrum((float2*)Kf, k, k_dtype == SFFFT_IO_BF16, layout, H, R, p->e->R2 > 1 ? 3 : 2,
-                                         (cudaStream_t)stream, false);
-  return ce == cudaSuccess ? SFFFT_OK : cuda_fail(ce);
+  const int R[3] = {p->e->R0, p->e->R1, p->e->R2}, S = p->e->R2 > 1 ? 3 : 2;
+  const bool bf = k_dtype == SFFFT_IO_BF16;
+  if (p->blocks == 1) {
+    const cudaError_t ce = launch_spectrum((float2*)Kf, k, bf, layout, H, R, S, (cudaStream_t)stream, false, -1, 0);
+    return ce == cudaSuccess ? SFFFT_OK : cuda_fail(ce);
+  }
+  // composite: spectrum of lag d at Kf + d * H * Nb, [blocks][H][Nb]; lag 0 is the causal first block of
+  // k, lag d >= 1 the two-sided filter k[(d-1) Lb + 1 : (d+1) Lb] (rows of k have the full length L)
+  if (layout != SFFFT_FILTER_CAUSAL) return SFFFT_ERR_UNSUPPORTED;
+  const int Lb = p->e->L;
+  for (int d = 0; d < p->blocks; d++) {
+    float2* dst = (float2*)Kf + (size_t)d * H * p->e->N;
+    const cudaError_t ce = d == 0 ? launch_spectrum(dst, k, bf, SFFFT_FILTER_CAUSAL, H, R, S, (cudaStream_t)stream, false, p->L, 0)
+                                  : launch_spectrum(dst, k, bf, SFFFT_FILTER_TWO_SIDED, H, R, S, (cudaStream_t)stream, false,
+                                                    p->L, (long long)(d - 1) * Lb + 1);
+    if (ce != cudaSuccess) return cuda_fail(ce);
+  }
+  return SFFFT_OK;
 }
 
 int sffft_fft_workspace_bytes(sffft_plan_t p, int B, size_t* bytes) {
   if (!p || !bytes || B < 1) return SFFFT_ERR_INVALID_ARGUMENT;
-  *bytes = (size_t)B * p->e->N * sizeof(float2);
+  *bytes = (size_t)B * 2 * p->L * sizeof(float2);
   return SFFFT_OK;
+}
+
+// Digits of the standalone FFT of length 2L: the plan's radices, the last one times the block count.
+static int fft_radices(sffft_plan_t p, int R[3]) {
+  const int S = p->e->R2 > 1 ? 3 : 2;
+  R[0] = p->e->R0; R[1] = p->e->R1; R[2] = p->e->R2;
+  R[S - 1] *= p->blocks;
+  return S;
 }
 
 int sffft_rfft(sffft_plan_t p, const void* x, int x_dtype, int B, void* X, void* work, void* stream) {
@@ -243,9 +294,10 @@ int sffft_rfft(sffft_plan_t p, const void* x, int x_dtype, int B, void* X, void*
     return SFFFT_ERR_INVALID_ARGUMENT;
   int rc = use_device(p->device);
   if (rc) return rc;
-  const int R[3] = {p->e->R0, p->e->R1, p->e->R2};
-  const cudaError_t ce = launch_rfft(x, x_dtype == SFFFT_IO_BF16, B, (float2*)X, (float2*)work, R,
-                                     p->e->R2 > 1 ? 3 : 2, p->sms, (cudaStream_t)stream);
+  int R[3];
+  const int S = fft_radices(p, R);
+  const cudaError_t ce = launch_rfft(x, x_dtype == SFFFT_IO_BF16, B, (float2*)X, (float2*)work, R, S, p->sms,
+                                     (cudaStream_t)stream);
   return ce == cudaSuccess ? SFFFT_OK : cuda_fail(ce);
 }
 
@@ -254,15 +306,45 @@ int sffft_irfft(sffft_plan_t p, const void* X, int B, float* x, void* work, void
   if ((((uintptr_t)X | (uintptr_t)work) & 7) != 0 || ((uintptr_t)x & 3) != 0) return SFFFT_ERR_INVALID_ARGUMENT;
   int rc = use_device(p->device);
   if (rc) return rc;
-  const int R[3] = {p->e->R0, p->e->R1, p->e->R2};
-  const cudaError_t ce = launch_irfft((const float2*)X, B, x, (float2*)work, R, p->e->R2 > 1 ? 3 : 2, p->sms,
-                                      (cudaStream_t)stream);
+  int R[3];
+  const int S = fft_radices(p, R);
+  const cudaError_t ce = launch_irfft((const float2*)X, B, x, (float2*)work, R, S, p->sms, (cudaStream_t)stream);
   return ce == cudaSuccess ? SFFFT_OK : cuda_fail(ce);
 }
+
+static int conv_launch(sffft_plan_t p, const void* u, const void* Kf, void* y, int B, int H, cudaStream_t stream);
 
 int sffft_conv(sffft_plan_t p, const void* u, const void* Kf, void* y, int B, int H, void* stream) {
   if (!p || !u || !Kf || !y || B < 1 || H < 1) return SFFFT_ERR_INVALID_ARGUMENT;
   if ((((uintptr_t)u | (uintptr_t)y | (uintptr_t)Kf) & 15) != 0) return SFFFT_ERR_INVALID_ARGUMENT;
+  if (p->blocks == 1) return conv_launch(p, u, Kf, y, B, H, (cudaStream_t)stream);
+
+  // composite plan: u in block-major order, one fused launch per block lag, then the fp32 block sum
+  const int P = p->blocks, Lb = p->e->L;
+  const bool bf = p->io == SFFFT_IO_BF16;
+  const long long blk = (long long)B * H * Lb;
+  if ((long long)P * B * H > std::numeric_limits<int>::max() / 2) return SFFFT_ERR_INVALID_ARGUMENT;
+  int rc = use_device(p->device);
+  if (rc) return rc;
+  const cudaStream_t st = (cudaStream_t)stream;
+  float* work = nullptr;
+  const size_t elems = (size_t)blk * (size_t)(P + part_offset(P, P, 1));
+  cudaError_t ce = cudaMallocAsync((void**)&work, elems * sizeof(float), st);
+  if (ce != cudaSuccess) return cuda_fail(ce);
+  float* ub = work;                              // [P][B][H][Lb]
+  float* parts = work + (size_t)P * blk;         // lag d: [P - d][B][H][Lb] at part_offset(d)
+  ce = launch_block_gather(u, ub, bf, B, H, Lb, P, p->sms, st);
+  for (int d = 0; d < P && ce == cudaSuccess && rc == SFFFT_OK; d++)
+    rc = conv_launch(p, ub, (const char*)Kf + (size_t)d * H * p->e->N * 8, parts + part_offset(d, P, blk),
+                     (P - d) * B, H, st);
+  if (ce == cudaSuccess && rc == SFFFT_OK) ce = launch_block_sum(parts, y, bf, B, H, Lb, P, p->sms, st);
+  const cudaError_t cf = cudaFreeAsync(work, st);
+  if (rc) return rc;
+  if (ce == cudaSuccess) ce = cf;
+  return ce == cudaSuccess ? SFFFT_OK : cuda_fail(ce);
+}
+
+static int conv_launch(sffft_plan_t p, const void* u, const void* Kf, void* y, int B, int H, cudaStream_t stream) {
   const ConvEntry* e = p->e;
   const long long pairs = (long long)((B + 1) / 2) * H;
   const long long groups = (pairs + e->G - 1) / e->G;
@@ -277,7 +359,7 @@ int sffft_conv(sffft_plan_t p, const void* u, const void* Kf, void* y, int B, in
 #ifdef SFFFT_TRACE
   prm.trace = g_trace;
 #endif
-  const cudaError_t ce = e->launch[p->io][p->acc](prm, grid, p->smem_launch, (cudaStream_t)stream);
+  const cudaError_t ce = e->launch[p->kio][p->acc](prm, grid, p->smem_launch, stream);
   return ce == cudaSuccess ? SFFFT_OK : cuda_fail(ce);
 }
 

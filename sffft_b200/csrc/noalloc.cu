@@ -18,11 +18,7 @@
 #include "../../include/sffft.h"
 #include "fused_conv.cuh"
 #include "registry.h"
-
-namespace sffft {
-cudaError_t launch_spectrum(float2* Kf, const void* k, bool k_bf16, int layout, int H, const int* R, int S,
-                            cudaStream_t stream, bool hermitian);
-}
+#include "spectrum.h"
 
 namespace {
 
@@ -119,7 +115,7 @@ extern "C" int sffft_conv_noalloc(int L, int io, int acc, const void* u, const v
   float2* Kf = reinterpret_cast<float2*>(ds.scratch + kStatusBytes);
   if (cudaMemsetAsync(status, 0, sizeof(int), st) != cudaSuccess) return SFFFT_ERR_CUDA;
   const int R[3] = {e->R0, e->R1, e->R2};
-  if (launch_spectrum(Kf, k, k_dtype == SFFFT_IO_BF16, SFFFT_FILTER_CAUSAL, H, R, e->R2 > 1 ? 3 : 2, st, false) != cudaSuccess) return SFFFT_ERR_CUDA;
+  if (launch_spectrum(Kf, k, k_dtype == SFFFT_IO_BF16, SFFFT_FILTER_CAUSAL, H, R, e->R2 > 1 ? 3 : 2, st, false, -1, 0) != cudaSuccess) return SFFFT_ERR_CUDA;
   ConvParams prm;
   std::memset(&prm, 0, sizeof(prm));
   prm.u = u; prm.Kf = reinterpret_cast<const float*>(Kf); prm.btab = nullptr;   // DFT matrices built in-kernel

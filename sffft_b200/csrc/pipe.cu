@@ -48,6 +48,9 @@ extern "C" int sffft_pipe_create(sffft_pipe_t* pipe, sffft_plan_t plan, int B, i
   if (rc) return rc;
   if (chunks == 0) chunks = 4;
   const int prow = (B + 1) / 2;            // pair rows (a chunk never splits a pair)
+  // a composite plan's spectrum is [blocks][H][2 Lb]: channel ranges are not contiguous in it, so its
+  // chunks are whole batch-row pairs only
+  if (info.blocks > 1 && chunks > prow) chunks = prow;
   int prev = 0;
   if (cudaGetDevice(&prev) != cudaSuccess) return SFFFT_ERR_CUDA;
   if (cudaSetDevice(info.device) != cudaSuccess) return SFFFT_ERR_CUDA;

@@ -19,6 +19,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "spectrum.h"
+
 #include "../../include/sffft.h"
 
 namespace sffft {
@@ -26,6 +28,7 @@ namespace sffft {
 struct SpecStage {
   int N, L, R, stride, pre;   // digit radix, stride of the digit, product of the radices before it
   int layout;                 // filter layout of stage 0 (SFFFT_FILTER_*)
+  long long kpitch, koff;     // stage 0: element offset of channel h's row is h * kpitch + koff
   int vec_per_cta;            // vectors handled by one CTA
   int twiddle;                // apply the inter-stage twiddle after this digit (not the last digit)
 };
@@ -71,19 +74,16 @@ __global__ void __launch_bounds__(256) spectrum_stage_kernel(float2* __restrict_
     } else if constexpr (SRC == kSrcReal) {
       const int L = st.L;
       int col = -1;   // column of the filter row that lands on tap p, or -1 for a zero tap
-      size_t row = (size_t)h * L;
       if (st.layout == SFFFT_FILTER_TWO_SIDED) {
-        row = (size_t)h * (2 * L - 1);
         col = p < L ? L - 1 + p : (p > L ? p - L - 1 : -1);   // tap N - j (0 < j < L) holds lag -j
       } else if (st.layout == SFFFT_FILTER_CIRCULAR) {
         col = p & (L - 1);
       } else if (st.layout == kLayoutFull) {
-        row = (size_t)h * N;
         col = p;
       } else {
         col = p < L ? p : -1;
       }
-      val = make_float2(col >= 0 ? k_to_float(k[row + col]) : 0.f, 0.f);
+      val = make_float2(col >= 0 ? k_to_float(k[h * st.kpitch + st.koff + col]) : 0.f, 0.f);
     } else {
       val = Kh[p];
     }
@@ -133,16 +133,21 @@ __global__ void __launch_bounds__(256) fft_gather_kernel(const float2* __restric
 
 // Runs the digit stages for radices R[0..S-1] over H channels of a filter for length L = N/2 in the
 // given layout.  k_bf16: the filter holds bf16 values instead of fp32.  hermitian: k is a half spectrum
-// [H][N/2 + 1] of float2 for the inverse FFT (layout and k_bf16 unused).
+// [H][N/2 + 1] of float2 for the inverse FFT (layout and k_bf16 unused).  kpitch / koff: the filter row of
+// channel h starts at element h * kpitch + koff (kpitch < 0: the layout's own row width, koff = 0).
 cudaError_t launch_spectrum(float2* Kf, const void* k, bool k_bf16, int layout, int H, const int* R, int S,
-                            cudaStream_t stream, bool hermitian) {
+                            cudaStream_t stream, bool hermitian, long long kpitch, long long koff) {
   int N = 1;
   for (int j = 0; j < S; j++) N *= R[j];
+  if (kpitch < 0) {
+    kpitch = layout == SFFFT_FILTER_TWO_SIDED ? N - 1 : (layout == kLayoutFull ? N : N / 2);
+    koff = 0;
+  }
   int stride = N, pre = 1;
   for (int j = 0; j < S; j++) {
     stride /= R[j];
     SpecStage st;
-    st.N = N; st.L = N / 2; st.layout = layout; st.R = R[j]; st.stride = stride; st.pre = pre; st.twiddle = (j + 1 < S);
+    st.N = N; st.L = N / 2; st.layout = layout; st.kpitch = kpitch; st.koff = koff; st.R = R[j]; st.stride = stride; st.pre = pre; st.twiddle = (j + 1 < S);
     const int vec_per_ch = N / R[j];
     st.vec_per_cta = vec_per_ch < 2048 / R[j] ? vec_per_ch : 2048 / R[j];
     const int grid = H * (vec_per_ch / st.vec_per_cta);
@@ -166,7 +171,7 @@ cudaError_t launch_spectrum(float2* Kf, const void* k, bool k_bf16, int layout, 
 // workspace W [rows][N] and one gather into natural order.
 cudaError_t launch_rfft(const void* x, bool x_bf16, int rows, float2* X, float2* W, const int* R, int S, int sms,
                         cudaStream_t stream) {
-  cudaError_t e = launch_spectrum(W, x, x_bf16, kLayoutFull, rows, R, S, stream, false);
+  cudaError_t e = launch_spectrum(W, x, x_bf16, kLayoutFull, rows, R, S, stream, false, -1, 0);
   if (e != cudaSuccess) return e;
   fft_gather_kernel<false><<<sms * 8, 256, 0, stream>>>(W, X, rows, R[0], R[1], S > 2 ? R[2] : 1);
   return cudaGetLastError();
@@ -174,7 +179,7 @@ cudaError_t launch_rfft(const void* x, bool x_bf16, int rows, float2* X, float2*
 
 cudaError_t launch_irfft(const float2* X, int rows, float* x, float2* W, const int* R, int S, int sms,
                          cudaStream_t stream) {
-  cudaError_t e = launch_spectrum(W, X, false, 0, rows, R, S, stream, true);
+  cudaError_t e = launch_spectrum(W, X, false, 0, rows, R, S, stream, true, -1, 0);
   if (e != cudaSuccess) return e;
   fft_gather_kernel<true><<<sms * 8, 256, 0, stream>>>(W, x, rows, R[0], R[1], S > 2 ? R[2] : 1);
   return cudaGetLastError();
