@@ -60,7 +60,8 @@ typedef struct {
  * convolution on the catalog plan of length Lb, and the default for L = 32768 .. 262144 is
  * "<L/16384>x[<default for 16384>]".  For a composite plan Kf holds the P block spectra [P][H][2 Lb]
  * (the same H * 2L complex values), filter layouts other than causal are unsupported, and sffft_conv
- * takes a stream-ordered workspace of (P + P (P + 1) / 2) * B * H * Lb elements for the call. */
+ * takes a stream-ordered workspace of (P + P (P + 1) / 2) * B * H * Lb fp32 elements for the call from a
+ * memory pool the plan owns (the pool keeps the largest workspace mapped until sffft_plan_destroy). */
 int sffft_plan_create(sffft_plan_t* plan, int L, int io, int acc, const char* config, int kernel_mode, int device);
 int sffft_plan_destroy(sffft_plan_t plan);
 int sffft_plan_info(sffft_plan_t plan, sffft_plan_info_t* info);

@@ -33,6 +33,7 @@ struct sffft_plan {
   const ConvEntry* e;   // the fused kernel's plan (the block plan of a composite plan)
   int blocks, L;        // composite plans: L = blocks * e->L (blocks = 1: the plan itself)
   int kio;              // I/O type of the fused kernel launches (fp32 for composite plans)
+  cudaMemPool_t pool;   // composite plans: pool of the per-call workspaces (keeps its memory until destroy)
   int io, acc, kernel_mode, device, occupancy, smem_launch, sms;
   uint4* btab;   // cached DFT-matrix image (device), null in legacy mode
   int* status;   // device status word
@@ -187,11 +188,27 @@ int sffft_plan_create(sffft_plan_t* out, int L, int io, int acc, const char* con
   p->e = e; p->blocks = blocks; p->L = L; p->kio = kio;
   p->io = io; p->acc = acc; p->kernel_mode = kernel_mode; p->device = device;
   p->occupancy = occ; p->smem_launch = smem_launch; p->sms = prop.multiProcessorCount;
-  p->btab = nullptr; p->status = nullptr;
+  p->btab = nullptr; p->status = nullptr; p->pool = nullptr;
   if ((ce = cudaMalloc(&p->status, sizeof(int))) != cudaSuccess || (ce = cudaMemset(p->status, 0, sizeof(int))) != cudaSuccess) {
     cudaFree(p->status);
     delete p;
     return cuda_fail(ce);
+  }
+  if (blocks > 1) {
+    // A pool of its own that never trims: a composite call's workspace (gigabytes at L >= 32768) is then
+    // mapped once, not again after every synchronisation as the default pool would do.
+    cudaMemPoolProps props = {};
+    props.allocType = cudaMemAllocationTypePinned;
+    props.location.type = cudaMemLocationTypeDevice;
+    props.location.id = device;
+    uint64_t keep = ~0ull;
+    if ((ce = cudaMemPoolCreate(&p->pool, &props)) != cudaSuccess ||
+        (ce = cudaMemPoolSetAttribute(p->pool, cudaMemPoolAttrReleaseThreshold, &keep)) != cudaSuccess) {
+      if (p->pool) cudaMemPoolDestroy(p->pool);
+      cudaFree(p->status);
+      delete p;
+      return cuda_fail(ce);
+    }
   }
   if (kernel_mode == SFFFT_KERNEL_CACHED) {
     std::vector<uint8_t> img(e->bmat_bytes, 0);
@@ -199,6 +216,7 @@ int sffft_plan_create(sffft_plan_t* out, int L, int io, int acc, const char* con
     if ((ce = cudaMalloc(&p->btab, e->bmat_bytes)) != cudaSuccess ||
         (ce = cudaMemcpy(p->btab, img.data(), e->bmat_bytes, cudaMemcpyHostToDevice)) != cudaSuccess) {
       cudaFree(p->btab); cudaFree(p->status);
+      if (p->pool) cudaMemPoolDestroy(p->pool);
       delete p;
       return cuda_fail(ce);
     }
@@ -214,6 +232,10 @@ int sffft_plan_destroy(sffft_plan_t p) {
   cudaSetDevice(p->device);
   cudaFree(p->btab);
   cudaFree(p->status);
+  if (p->pool) {
+    cudaDeviceSynchronize();   // workspaces of calls still in flight return to the pool first
+    cudaMemPoolDestroy(p->pool);
+  }
   cudaSetDevice(prev);
   delete p;
   return SFFFT_OK;
@@ -329,7 +351,7 @@ int sffft_conv(sffft_plan_t p, const void* u, const void* Kf, void* y, int B, in
   const cudaStream_t st = (cudaStream_t)stream;
   float* work = nullptr;
   const size_t elems = (size_t)blk * (size_t)(P + part_offset(P, P, 1));
-  cudaError_t ce = cudaMallocAsync((void**)&work, elems * sizeof(float), st);
+  cudaError_t ce = cudaMallocFromPoolAsync((void**)&work, elems * sizeof(float), p->pool, st);
   if (ce != cudaSuccess) return cuda_fail(ce);
   float* ub = work;                              // [P][B][H][Lb]
   float* parts = work + (size_t)P * blk;         // lag d: [P - d][B][H][Lb] at part_offset(d)

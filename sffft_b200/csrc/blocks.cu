@@ -8,7 +8,8 @@
 // blocks).  block_gather_kernel copies u into block-major fp32 [P][B][H][Lb], the host runs the block
 // plan's fused kernel with fp32 I/O once per lag d over the P - d input blocks that have a partner (one
 // launch of (P - d) * B batch rows), and block_sum_kernel adds the fp32 partial outputs of each output
-// block and writes y in the caller's type (bf16 I/O is rounded once, at the end).
+// block and writes y in the caller's type (bf16 I/O is rounded once, at the end).  Lb and P are powers
+// of two.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -38,57 +39,64 @@ __device__ __forceinline__ void st4(__nv_bfloat16* p, float4 v) {
   *reinterpret_cast<uint2*>(p) = o;
 }
 
-// ub[q][b][h][t] = u[b][h][q*Lb + t] in fp32; four consecutive elements per thread.
+// ub[q][row][t] = u[row][q*Lb + t] in fp32 (row = b*H + h); four consecutive elements per thread.  L and Lb
+// are powers of two (lgL, lgLb their logarithms), so the index split is shifts and masks.
 template <class T>
-__global__ void __launch_bounds__(256) block_gather_kernel(const T* __restrict__ u, float* __restrict__ ub, int B, int H,
-                                                           int Lb, int P) {
-  const long long L = (long long)P * Lb, blk = (long long)B * H * Lb;
-  const long long total4 = (long long)B * H * L / 4;
+__global__ void __launch_bounds__(256) block_gather_kernel(const T* __restrict__ u, float* __restrict__ ub, long long rows,
+                                                           int lgL, int lgLb) {
+  const long long total4 = rows << (lgL - 2), blk = rows << lgLb;
+  const long long cmask = (1ll << lgL) - 1, tmask = (1ll << lgLb) - 1;
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total4; i += (long long)gridDim.x * blockDim.x) {
-    const long long e = 4 * i, row = e / L;           // row = b * H + h
-    const long long col = e - row * L;
-    const int q = (int)(col / Lb);
-    const long long t = col - (long long)q * Lb;
-    st4(ub + q * blk + row * Lb + t, ld4(u + e));
+    const long long e = 4 * i, row = e >> lgL, col = e & cmask;
+    st4(ub + (col >> lgLb) * blk + (row << lgLb) + (col & tmask), ld4(u + e));
   }
 }
 
-// y[b][h][p*Lb + t] = sum_{d <= p} parts_d[(p - d)*B + b][h][t]; four consecutive elements per thread.
+// y[row][p*Lb + t] = sum_{d <= p} parts_d[(p - d)*rows + row][t]; four consecutive elements per thread.
 template <class T>
-__global__ void __launch_bounds__(256) block_sum_kernel(const float* __restrict__ parts, T* __restrict__ y, int B, int H,
-                                                        int Lb, int P) {
-  const long long L = (long long)P * Lb, blk = (long long)B * H * Lb;
-  const long long total4 = (long long)B * H * L / 4;
+__global__ void __launch_bounds__(256) block_sum_kernel(const float* __restrict__ parts, T* __restrict__ y, long long rows,
+                                                        int lgL, int lgLb) {
+  const int P = 1 << (lgL - lgLb);
+  const long long total4 = rows << (lgL - 2), blk = rows << lgLb;
+  const long long cmask = (1ll << lgL) - 1, tmask = (1ll << lgLb) - 1;
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total4; i += (long long)gridDim.x * blockDim.x) {
-    const long long e = 4 * i, row = e / L;           // row = b * H + h
-    const long long col = e - row * L;
-    const int p = (int)(col / Lb);
-    const long long t = col - (long long)p * Lb;
-    const long long b = row / H, h = row - b * H;
+    const long long e = 4 * i, row = e >> lgL, col = e & cmask;
+    const int p = (int)(col >> lgLb);
+    const long long off = (row << lgLb) + (col & tmask);
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int d = 0; d <= p; d++) {
-      const float4 v = ld4(parts + part_offset(d, P, blk) + (((long long)(p - d) * B + b) * H + h) * Lb + t);
+      const float4 v = ld4(parts + part_offset(d, P, blk) + (long long)(p - d) * blk + off);
       acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
     }
     st4(y + e, acc);
   }
 }
 
+static int log2i(long long v) {
+  int r = 0;
+  while ((1ll << r) < v) r++;
+  return r;
+}
+
 cudaError_t launch_block_gather(const void* u, float* ub, bool bf16, int B, int H, int Lb, int P, int sms,
                                 cudaStream_t stream) {
+  const long long rows = (long long)B * H;
+  const int lgLb = log2i(Lb), lgL = lgLb + log2i(P);
   if (bf16)
-    block_gather_kernel<__nv_bfloat16><<<sms * 8, 256, 0, stream>>>((const __nv_bfloat16*)u, ub, B, H, Lb, P);
+    block_gather_kernel<__nv_bfloat16><<<sms * 8, 256, 0, stream>>>((const __nv_bfloat16*)u, ub, rows, lgL, lgLb);
   else
-    block_gather_kernel<float><<<sms * 8, 256, 0, stream>>>((const float*)u, ub, B, H, Lb, P);
+    block_gather_kernel<float><<<sms * 8, 256, 0, stream>>>((const float*)u, ub, rows, lgL, lgLb);
   return cudaGetLastError();
 }
 
 cudaError_t launch_block_sum(const float* parts, void* y, bool bf16, int B, int H, int Lb, int P, int sms,
                              cudaStream_t stream) {
+  const long long rows = (long long)B * H;
+  const int lgLb = log2i(Lb), lgL = lgLb + log2i(P);
   if (bf16)
-    block_sum_kernel<__nv_bfloat16><<<sms * 8, 256, 0, stream>>>(parts, (__nv_bfloat16*)y, B, H, Lb, P);
+    block_sum_kernel<__nv_bfloat16><<<sms * 8, 256, 0, stream>>>(parts, (__nv_bfloat16*)y, rows, lgL, lgLb);
   else
-    block_sum_kernel<float><<<sms * 8, 256, 0, stream>>>(parts, (float*)y, B, H, Lb, P);
+    block_sum_kernel<float><<<sms * 8, 256, 0, stream>>>(parts, (float*)y, rows, lgL, lgLb);
   return cudaGetLastError();
 }
 
