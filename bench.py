@@ -324,7 +324,7 @@ def main():
             "e2e": {"value": round(e2e_step / world, 5), "unit": UNIT, "h2d_bytes_per_step": u_h.numel() * u_h.element_size(),
                     "d2h_bytes_per_step": y_h.numel() * y_h.element_size(),
                     "path": f"pinned host u -> sffft_conv_host (C ABI: ~{pipe_chunks} batch-row chunks, upload / fused "
-                            "conv / download overlapped on 3 streams) -> pinned host y, per step"},
+                            "conv / download overlapped, one stream per stage) -> pinned host y, per step"},
             "gpu_launches": args.steps * world,
             "clocks": clk,
         }

@@ -161,10 +161,10 @@ int sffft_conv_noalloc(int L, int io, int acc, const void* u, const void* k, int
 /* Host-buffer pipeline (no reference counterpart: the reference keeps u and y on the device and times the
  * kernel alone).  sffft_pipe_create sizes device staging for a B x H batch cut into about `chunks` chunks
  * (0 = 4) of whole batch-row pairs (contiguous, one copy each way), or of pairs and channel ranges when B/2
- * is smaller than `chunks`, and creates three streams; sffft_conv_host then computes
- * y_host = causal_conv(u_host, k) for host buffers u_host, y_host [B][H][L] (the plan's I/O type; pinned for
- * overlap) and the device spectrum Kf [H][N]: chunk i is uploaded, convolved and downloaded on stream i % 3,
- * so uploads, kernels and downloads of different chunks overlap.  Ordered after earlier work on `stream`; later work on
+ * is smaller than `chunks`, and creates one stream per stage (upload, convolution, download) with three
+ * staging slots; sffft_conv_host then computes y_host = causal_conv(u_host, k) for host buffers u_host,
+ * y_host [B][H][L] (the plan's I/O type; pinned for overlap) and the device spectrum Kf [H][N]: chunk i goes
+ * through slot i % 3, so uploads, kernels and downloads of different chunks overlap.  Ordered after earlier work on `stream`; later work on
  * `stream` waits for it.  Calls on one pipe must not overlap. */
 typedef struct sffft_pipe* sffft_pipe_t;
 int sffft_pipe_create(sffft_pipe_t* pipe, sffft_plan_t plan, int B, int H, int chunks);

@@ -2,13 +2,16 @@
 //
 // The batch is cut into chunks of whole batch-row pairs (u[b0:b1] is contiguous in [B][H][L], so a chunk
 // moves with one 1-D copy each way); only when there are fewer pair rows than chunks are the rows also cut
-// into channel ranges (2-D copies of b1 - b0 rows, host pitch H * L, measured slower per byte).  Chunk i
-// goes through three steps on stream i % 3 -- upload to device staging, sffft_conv with the chunk's
-// spectrum rows, download into y -- so the upload of one chunk, the kernel of the previous one and the
-// download of the one before that overlap, and both copy directions run at the same time.  Pinned host
-// buffers make the copies asynchronous (pageable ones still give correct results, without the overlap).
-// The call is ordered after earlier work on the caller's stream, and later work on that stream waits for
-// all chunks.
+// into channel ranges (one 1-D copy per batch row each way: a row's channel range is contiguous).  Each
+// stage has a stream of its own -- uploads into device staging, sffft_conv with the chunk's spectrum rows,
+// downloads into y -- and chunk c uses staging slot c % 3, handed from stage to stage by events: the
+// upload of chunk c waits until the slot's previous kernel has read its input, and the kernel waits until
+// the slot's previous download has read its output (also across calls).  So each copy direction runs its chunks in
+// order on one stream while the other direction and the kernels overlap it (chaining the three steps of
+// a chunk on one stream per chunk measured 0.79 ms against 0.51 ms of concurrent copies at B = 8, H = 768,
+// L = 1024).  Pinned host buffers make the copies asynchronous (pageable ones still give correct results,
+// without the overlap).  The call is ordered after earlier work on the caller's stream, and later work on
+// that stream waits for all chunks.
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -20,12 +23,15 @@ namespace {
 constexpr int kStreams = 3;
 }
 
+enum { kUp = 0, kConv = 1, kDown = 2 };   // stage streams
+
 struct sffft_pipe {
   sffft_plan_t plan;
   int B, H, L, N, sio, nb, hc, device;   // chunk: nb batch rows (even) x hc channels
-  void* u_stage[kStreams];   // device staging [nb][hc][L] per stream
+  void* u_stage[kStreams];   // device staging [nb][hc][L] per slot
   void* y_stage[kStreams];
-  cudaStream_t s[kStreams];
+  cudaStream_t s[kStreams];  // one per stage
+  cudaEvent_t up[kStreams], conv[kStreams], down[kStreams];   // per slot: its last upload / kernel / download
   cudaEvent_t start, done[kStreams];
 };
 
@@ -35,6 +41,9 @@ static void pipe_free(sffft_pipe* q) {
     if (q->y_stage[i]) cudaFree(q->y_stage[i]);
     if (q->s[i]) cudaStreamDestroy(q->s[i]);
     if (q->done[i]) cudaEventDestroy(q->done[i]);
+    if (q->up[i]) cudaEventDestroy(q->up[i]);
+    if (q->conv[i]) cudaEventDestroy(q->conv[i]);
+    if (q->down[i]) cudaEventDestroy(q->down[i]);
   }
   if (q->start) cudaEventDestroy(q->start);
   delete q;
@@ -72,7 +81,10 @@ extern "C" int sffft_pipe_create(sffft_pipe_t* pipe, sffft_plan_t plan, int B, i
   for (int i = 0; i < kStreams && ok; i++) {
     ok = cudaMalloc(&q->u_stage[i], bytes) == cudaSuccess && cudaMalloc(&q->y_stage[i], bytes) == cudaSuccess &&
          cudaStreamCreateWithFlags(&q->s[i], cudaStreamNonBlocking) == cudaSuccess &&
-         cudaEventCreateWithFlags(&q->done[i], cudaEventDisableTiming) == cudaSuccess;
+         cudaEventCreateWithFlags(&q->done[i], cudaEventDisableTiming) == cudaSuccess &&
+         cudaEventCreateWithFlags(&q->up[i], cudaEventDisableTiming) == cudaSuccess &&
+         cudaEventCreateWithFlags(&q->conv[i], cudaEventDisableTiming) == cudaSuccess &&
+         cudaEventCreateWithFlags(&q->down[i], cudaEventDisableTiming) == cudaSuccess;
   }
   cudaSetDevice(prev);
   if (!ok) {
@@ -93,6 +105,7 @@ extern "C" int sffft_conv_host(sffft_pipe_t q, const void* u_host, const void* K
   cudaError_t ce = cudaEventRecord(q->start, user);
   for (int i = 0; i < kStreams && ce == cudaSuccess; i++) ce = cudaStreamWaitEvent(q->s[i], q->start, 0);
   const size_t row = (size_t)q->H * q->L * q->sio;   // host pitch between batch rows
+  const cudaStream_t su = q->s[kUp], sk = q->s[kConv], sd = q->s[kDown];
   int c = 0;
   for (int b0 = 0; b0 < q->B && ce == cudaSuccess && rc == SFFFT_OK; b0 += q->nb) {
     const int b1 = b0 + q->nb < q->B ? b0 + q->nb : q->B, bn = b1 - b0;
@@ -101,13 +114,33 @@ extern "C" int sffft_conv_host(sffft_pipe_t q, const void* u_host, const void* K
       const size_t width = (size_t)hn * q->L * q->sio;
       const char* src = (const char*)u_host + (size_t)b0 * row + (size_t)h0 * q->L * q->sio;
       char* dst = (char*)y_host + (size_t)b0 * row + (size_t)h0 * q->L * q->sio;
-      ce = hn == q->H ? cudaMemcpyAsync(q->u_stage[k], src, width * bn, cudaMemcpyHostToDevice, q->s[k])
-                      : cudaMemcpy2DAsync(q->u_stage[k], width, src, row, width, bn, cudaMemcpyHostToDevice, q->s[k]);
+      // upload: the slot's input is free once the slot's previous kernel (chunk c - 3, or the previous
+      // call's) has run; an event never recorded is complete
+      ce = cudaStreamWaitEvent(su, q->conv[k], 0);
+      // a chunk of whole rows is one contiguous copy; a channel range is one contiguous copy per batch row
+      if (ce == cudaSuccess && hn == q->H) {
+        ce = cudaMemcpyAsync(q->u_stage[k], src, width * bn, cudaMemcpyHostToDevice, su);
+      } else {
+        for (int r = 0; r < bn && ce == cudaSuccess; r++)
+          ce = cudaMemcpyAsync((char*)q->u_stage[k] + r * width, src + r * row, width, cudaMemcpyHostToDevice, su);
+      }
+      if (ce == cudaSuccess) ce = cudaEventRecord(q->up[k], su);
+      // kernel: after the upload, and once the slot's previous download has emptied its output
+      if (ce == cudaSuccess) ce = cudaStreamWaitEvent(sk, q->up[k], 0);
+      if (ce == cudaSuccess) ce = cudaStreamWaitEvent(sk, q->down[k], 0);
       if (ce != cudaSuccess) break;
-      rc = sffft_conv(q->plan, q->u_stage[k], (const char*)Kf + (size_t)h0 * q->N * 8, q->y_stage[k], bn, hn, q->s[k]);
+      rc = sffft_conv(q->plan, q->u_stage[k], (const char*)Kf + (size_t)h0 * q->N * 8, q->y_stage[k], bn, hn, sk);
       if (rc) break;
-      ce = hn == q->H ? cudaMemcpyAsync(dst, q->y_stage[k], width * bn, cudaMemcpyDeviceToHost, q->s[k])
-                      : cudaMemcpy2DAsync(dst, row, q->y_stage[k], width, width, bn, cudaMemcpyDeviceToHost, q->s[k]);
+      ce = cudaEventRecord(q->conv[k], sk);
+      // download after the kernel
+      if (ce == cudaSuccess) ce = cudaStreamWaitEvent(sd, q->conv[k], 0);
+      if (ce == cudaSuccess && hn == q->H) {
+        ce = cudaMemcpyAsync(dst, q->y_stage[k], width * bn, cudaMemcpyDeviceToHost, sd);
+      } else {
+        for (int r = 0; r < bn && ce == cudaSuccess; r++)
+          ce = cudaMemcpyAsync(dst + r * row, (char*)q->y_stage[k] + r * width, width, cudaMemcpyDeviceToHost, sd);
+      }
+      if (ce == cudaSuccess) ce = cudaEventRecord(q->down[k], sd);
     }
   }
   for (int i = 0; i < kStreams; i++) {
