@@ -192,6 +192,12 @@ def run_reference(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
+# BASELINE.json's configurations by (B, H per GPU, L, I/O, accumulation); other shapes are "custom".
+BASELINE_CONFIGS = {(1, 1, 128, "fp32", "fp32"): "BASELINE configs[0]", (8, 768, 1024, "fp32", "fp32"): "BASELINE configs[1]",
+                    (8, 768, 4096, "bf16", "fp32"): "BASELINE configs[2]", (8, 768, 8192, "bf16", "fp16"): "BASELINE configs[3]",
+                    (16, 1024, 16384, "fp32", "fp32"): "BASELINE configs[4]"}
+
+
 def main():
     args = parse()
     world, rank, local = dist_setup(args)
@@ -308,8 +314,8 @@ def main():
             "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": False, "scaling": "weak",
             "vs_baseline": round(value / pub, 4) if pub else None, "dtype": "f16",
             "data": "synthetic (seeded torch.randn u; k = N(0,1) exp(-4n/L)/sqrt(L))",
-            "config": {"workload": f"BASELINE configs[1]: causal long conv B={B} H={H} per GPU, L={L}, "
-                                   f"{args.io} I/O, {args.acc} accumulation",
+            "config": {"workload": f"{BASELINE_CONFIGS.get((B, H, L, args.io, args.acc), 'custom')}: causal long conv "
+                                   f"B={B} H={H} per GPU, L={L}, {args.io} I/O, {args.acc} accumulation",
                        "plan": plan.config, "B": B, "H_per_gpu": H, "H_total": H * world, "L": L, "io": args.io,
                        "acc": args.acc, "occupancy": plan.info["occupancy"], "smem_bytes": plan.info["smem_bytes"],
                        "parallelism": f"channel-sharded x{world}, no collective on the data path",
