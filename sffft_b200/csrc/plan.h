@@ -162,7 +162,14 @@ struct Shape {
   static constexpr int TWARPS = WC / NTEAM;                         // warps per team
   static constexpr int NWQ = TWARPS / 4;                            // a team's warps per TMEM lane quarter
   static constexpr int NB = P::W == 4 ? 4 : 2;                      // conversion steps whose loads overlap
-  static constexpr int PD = NS + 1;                                 // L2 prefetch distance, groups
+  // L2 prefetch distance in groups: NS + 1, but at most kPrefetchBytes of input and spectrum rows ahead of
+  // the conversions per CTA (about 24 MB over 148 CTAs).  Prefetching further ahead at long lengths evicts
+  // the spectrum rows and outputs of the groups in flight (measured: one group ahead is 2-4 % faster than
+  // NS + 1 at L = 8192 and 16384, two ahead 5 % faster at L = 2048, no change at L <= 1024).
+  static constexpr int kPrefetchBytes = 160 * 1024;
+  static constexpr int GROUP_L2_BYTES = 2 * P::G * SEQB + P::N * 8;
+  static constexpr int PD = kPrefetchBytes / GROUP_L2_BYTES < 1 ? 1
+                            : (kPrefetchBytes / GROUP_L2_BYTES > NS + 1 ? NS + 1 : kPrefetchBytes / GROUP_L2_BYTES);
   static constexpr int DATA_OFF = P::BMAT_BYTES;
   static constexpr int K_OFF = DATA_OFF + NS * P::DATA_BYTES;
   static constexpr int FREE = CAP - K_OFF;
