@@ -77,47 +77,56 @@ SF_HD PairInfo pair_info(int cta, int g, int G, int B, int H, int L) {
 // Input conversion: raw u (two real sequences per pair) -> first-stage A operand, fp16 hi + lo split.
 //   element (row m = g*V0 + v, K-row plane*R0 + n0 [hi] / plane*R0 + R0/2 + n0 [lo]), n = n0*V0 + v.
 // A group's input is its 2G sequences (sequence j = 2*g + plane, element n), read straight from global
-// memory: thread tid of nthreads takes 8 consecutive elements per step and issues NB steps' loads before it
-// converts any, so their latencies overlap.  Absent sequences (odd B, past the last pair) read as zero.
+// memory: thread tid of nthreads takes 8 consecutive elements per step and keeps NB steps' loads in flight,
+// refilling each register slot with the load NB steps ahead as soon as it has converted the slot (issuing
+// NB loads, converting all NB and only then issuing the next NB drained the loads at every batch: 8 %
+// slower at L = 1024).  Absent sequences (odd B, past the last pair) read as zero.
 // bf16 input is exact in fp16 (up to fp16-subnormal values below 6e-5, whose residue under 3e-8 is
 // dropped), so it has no lo plane to compute.
 // ---------------------------------------------------------------------------------------------
 template <class P, class TIO, int NB, class Ops>
 SF_HD void convert_group(Ops& ops, const TIO* u, const GroupPairs& gp, int tid, int nthreads) {
   constexpr int V0 = P::N / P::R0, MB0 = P::MB(0), NE = 2 * P::G * P::L;
-  for (int e0 = tid * 8; e0 < NE; e0 += NB * nthreads * 8) {
-    float v[NB][8];
-    int mrow[NB], krow[NB];
-    for (int b = 0; b < NB; b++) {
-      const int e = e0 + b * nthreads * 8;
-      krow[b] = -1;
-      if (e < NE) {
-        const int j = e / P::L, n = e - j * P::L, g = j >> 1, plane = j & 1;
-        const PairInfo pi = gp.get(g, P::L);
-        const long long off = plane == 0 ? pi.off0 : pi.off1;
-        const int n0 = n / V0, vv = n - n0 * V0;
-        mrow[b] = g * V0 + vv;
-        krow[b] = plane * P::R0 + n0;
-        if (off >= 0) ops.ldg8(u + off + n, v[b]);
-        else {
-          for (int q = 0; q < 8; q++) v[b][q] = 0.f;
-        }
+  const int stride = nthreads * 8;
+  float v[NB][8];
+  int mrow[NB], krow[NB];
+  auto issue = [&](int b, int e) {
+    krow[b] = -1;
+    if (e < NE) {
+      const int j = e / P::L, n = e - j * P::L, g = j >> 1, plane = j & 1;
+      const PairInfo pi = gp.get(g, P::L);
+      const long long off = plane == 0 ? pi.off0 : pi.off1;
+      const int n0 = n / V0, vv = n - n0 * V0;
+      mrow[b] = g * V0 + vv;
+      krow[b] = plane * P::R0 + n0;
+      if (off >= 0) ops.ldg8(u + off + n, v[b]);
+      else {
+        for (int q = 0; q < 8; q++) v[b][q] = 0.f;
       }
     }
+  };
+  auto finish = [&](int b) {
+    if (krow[b] < 0) return;
+    uint32_t hi[4], lo[4];
+    for (int q = 0; q < 4; q++) hi[q] = ops.pack2(v[b][2 * q], v[b][2 * q + 1]);
+    // K-row k + R0/2 (the lo plane) is R0/16 K-groups further: same swizzle phase, since R0/2 % 8 == 0
+    const uint32_t off = mn_off(mrow[b], krow[b], MB0), off_lo = off + (uint32_t)(P::R0 / 16) * MB0 * 1024u;
+    ops.st16(off, hi[0], hi[1], hi[2], hi[3]);
+    if constexpr (sizeof(TIO) == 4) {
+      for (int q = 0; q < 4; q++)
+        lo[q] = ops.pack2(v[b][2 * q] - ops.lo16f(hi[q]), v[b][2 * q + 1] - ops.hi16f(hi[q]));
+      ops.st16(off_lo, lo[0], lo[1], lo[2], lo[3]);
+    } else if constexpr (P::R0 == 16) {
+      ops.st16(off_lo, 0u, 0u, 0u, 0u);   // bf16 converts exactly: its lo plane is zero
+    }
+  };
+#pragma unroll
+  for (int b = 0; b < NB; b++) issue(b, tid * 8 + b * stride);
+  for (int e0 = tid * 8; e0 < NE; e0 += NB * stride) {
+#pragma unroll
     for (int b = 0; b < NB; b++) {
-      if (krow[b] < 0) continue;
-      uint32_t hi[4], lo[4];
-      for (int q = 0; q < 4; q++) hi[q] = ops.pack2(v[b][2 * q], v[b][2 * q + 1]);
-      // K-row k + R0/2 (the lo plane) is R0/16 K-groups further: same swizzle phase, since R0/2 % 8 == 0
-      const uint32_t off = mn_off(mrow[b], krow[b], MB0), off_lo = off + (uint32_t)(P::R0 / 16) * MB0 * 1024u;
-      ops.st16(off, hi[0], hi[1], hi[2], hi[3]);
-      if constexpr (sizeof(TIO) == 4) {
-        for (int q = 0; q < 4; q++)
-          lo[q] = ops.pack2(v[b][2 * q] - ops.lo16f(hi[q]), v[b][2 * q + 1] - ops.hi16f(hi[q]));
-        ops.st16(off_lo, lo[0], lo[1], lo[2], lo[3]);
-      } else if constexpr (P::R0 == 16) {
-        ops.st16(off_lo, 0u, 0u, 0u, 0u);   // bf16 converts exactly: its lo plane is zero
-      }
+      finish(b);
+      issue(b, e0 + (b + NB) * stride);
     }
   }
 }
