@@ -121,10 +121,15 @@ struct HostOps {
     const uint8_t* b = (const uint8_t*)p;
     if (in_lo && (b < in_lo || b + n > in_hi)) throw std::out_of_range("input read outside u");
   }
-  void ldg8(const float* p, float* v) { check_in(p, 32); for (int e = 0; e < 8; e++) v[e] = p[e]; }
-  void ldg8(const uint16_t* p, float* v) {
-    check_in(p, 16);
-    for (int e = 0; e < 8; e++) { uint32_t b = (uint32_t)p[e] << 16; std::memcpy(&v[e], &b, 4); }
+  void ldraw(const float* p, uint32_t (&w)[8]) { check_in(p, 32); std::memcpy(w, p, 32); }
+  void ldraw(const uint16_t* p, uint32_t (&w)[8]) { check_in(p, 16); std::memcpy(w, p, 16); }
+  void unpack(const float*, const uint32_t (&w)[8], float* v) { std::memcpy(v, w, 32); }
+  void unpack(const uint16_t*, const uint32_t (&w)[8], float* v) {
+    for (int e = 0; e < 4; e++) {
+      const uint32_t lo = (w[e] & 0xFFFFu) << 16, hi = w[e] & 0xFFFF0000u;
+      std::memcpy(&v[2 * e], &lo, 4);
+      std::memcpy(&v[2 * e + 1], &hi, 4);
+    }
   }
   void store1(float* p, float v) { *p = v; }
   void store1(uint16_t* p, float v) { *p = (uint16_t)bf16_from_float(v); }

@@ -86,13 +86,20 @@ struct DevOps {
   // u is read once (after the L2 prefetch) and y written once: both use the streaming (evict-first) cache
   // policy so they do not displace the spectrum rows that several groups of a channel share (measured 3 %
   // faster at L = 1024 and 2048, no change at longer lengths).
-  __device__ __forceinline__ void ldg8(const float* p, float* v) {
-    const float4 a = __ldcs(reinterpret_cast<const float4*>(p)), b = __ldcs(reinterpret_cast<const float4*>(p) + 1);
-    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  // Eight input values as raw words (eight fp32 bit patterns, or four words of bf16 pairs), unpacked only
+  // when the conversion reaches them, so that nothing waits on a load right after issuing it.
+  __device__ __forceinline__ void ldraw(const float* p, uint32_t (&w)[8]) {
+    const uint4 a = __ldcs(reinterpret_cast<const uint4*>(p)), b = __ldcs(reinterpret_cast<const uint4*>(p) + 1);
+    w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w; w[4] = b.x; w[5] = b.y; w[6] = b.z; w[7] = b.w;
   }
-  __device__ __forceinline__ void ldg8(const __nv_bfloat16* p, float* v) {
+  __device__ __forceinline__ void ldraw(const __nv_bfloat16* p, uint32_t (&w)[8]) {
     const uint4 q = __ldcs(reinterpret_cast<const uint4*>(p));
-    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+    w[0] = q.x; w[1] = q.y; w[2] = q.z; w[3] = q.w;
+  }
+  __device__ __forceinline__ void unpack(const float*, const uint32_t (&w)[8], float* v) {
+    for (int e = 0; e < 8; e++) v[e] = __uint_as_float(w[e]);
+  }
+  __device__ __forceinline__ void unpack(const __nv_bfloat16*, const uint32_t (&w)[8], float* v) {
     for (int e = 0; e < 4; e++) { v[2 * e] = bf16_bits_to_float(w[e] & 0xFFFFu); v[2 * e + 1] = bf16_bits_to_float(w[e] >> 16); }
   }
   __device__ __forceinline__ void store1(float* p, float v) { __stcs(p, v); }

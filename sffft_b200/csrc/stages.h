@@ -9,7 +9,8 @@
 //   ops.ldK(p) / ops.ldsK(p)                                 four floats (two complex) of the spectrum from
 //                                                            global / staged shared memory
 //   ops.cmul16(a, b, kk, pr, pim)                            16 complex values x spectrum pieces -> fp16 pairs
-//   ops.ldg8(p, v)                                           eight input values (TIO) from global -> float
+//   ops.ldraw(p, w) / ops.unpack(p, w, v)                    eight input values (TIO) from global, as raw words
+//                                                            -> float (unpacked when converted)
 //   ops.store1(p, v) / ops.store4(p, v[4])                   output values (TIO) to global memory
 //   ops.tw(e, &re, &im)                                      w_N^e from the CTA's twiddle table
 //   ops.twiddle16(a, b, t0, t8, w, pr, pim)                  16 complex values x t0*w^j (j < 8) and
@@ -88,7 +89,7 @@ template <class P, class TIO, int NB, class Ops>
 SF_HD void convert_group(Ops& ops, const TIO* u, const GroupPairs& gp, int tid, int nthreads) {
   constexpr int V0 = P::N / P::R0, MB0 = P::MB(0), NE = 2 * P::G * P::L;
   const int stride = nthreads * 8;
-  float v[NB][8];
+  uint32_t w[NB][8];
   int mrow[NB], krow[NB];
   auto issue = [&](int b, int e) {
     krow[b] = -1;
@@ -99,22 +100,24 @@ SF_HD void convert_group(Ops& ops, const TIO* u, const GroupPairs& gp, int tid, 
       const int n0 = n / V0, vv = n - n0 * V0;
       mrow[b] = g * V0 + vv;
       krow[b] = plane * P::R0 + n0;
-      if (off >= 0) ops.ldg8(u + off + n, v[b]);
+      if (off >= 0) ops.ldraw(u + off + n, w[b]);
       else {
-        for (int q = 0; q < 8; q++) v[b][q] = 0.f;
+        for (int q = 0; q < 8; q++) w[b][q] = 0u;   // zero bits read as 0.0 in both formats
       }
     }
   };
   auto finish = [&](int b) {
     if (krow[b] < 0) return;
+    float v[8];
+    ops.unpack(u, w[b], v);
     uint32_t hi[4], lo[4];
-    for (int q = 0; q < 4; q++) hi[q] = ops.pack2(v[b][2 * q], v[b][2 * q + 1]);
+    for (int q = 0; q < 4; q++) hi[q] = ops.pack2(v[2 * q], v[2 * q + 1]);
     // K-row k + R0/2 (the lo plane) is R0/16 K-groups further: same swizzle phase, since R0/2 % 8 == 0
     const uint32_t off = mn_off(mrow[b], krow[b], MB0), off_lo = off + (uint32_t)(P::R0 / 16) * MB0 * 1024u;
     ops.st16(off, hi[0], hi[1], hi[2], hi[3]);
     if constexpr (sizeof(TIO) == 4) {
       for (int q = 0; q < 4; q++)
-        lo[q] = ops.pack2(v[b][2 * q] - ops.lo16f(hi[q]), v[b][2 * q + 1] - ops.hi16f(hi[q]));
+        lo[q] = ops.pack2(v[2 * q] - ops.lo16f(hi[q]), v[2 * q + 1] - ops.hi16f(hi[q]));
       ops.st16(off_lo, lo[0], lo[1], lo[2], lo[3]);
     } else if constexpr (P::R0 == 16) {
       ops.st16(off_lo, 0u, 0u, 0u, 0u);   // bf16 converts exactly: its lo plane is zero
