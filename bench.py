@@ -1,10 +1,10 @@
-"""Benchmark of the fused causal long convolution (BASELINE.json metric: ms per B=8 x H=768 batch and
+"""Benchmark of the fused causal long convolution (headline metric: ms per B=8 x H=768 batch and
 fraction of the HBM / tensor roofline).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--L 1024] [--io fp32]
     torchrun --nproc-per-node N bench.py --gpus N ...      (one rank per GPU)
 
-Workload (default): BASELINE.json configs[1] -- B=8, H=768 channels per GPU, L=1024, fp32 I/O, fp32
+Workload (default): the headline configuration configs[1] -- B=8, H=768 channels per GPU, L=1024, fp32 I/O, fp32
 accumulation, u ~ N(0,1), k = N(0,1) exp(-4n/L)/sqrt(L).  A step is one sffft_conv launch over the
 GPU's batch.  With N GPUs each rank owns its own 768-channel slice of an N*768-channel batch (channel
 sharding, weak scaling, no collective on the data path); `value` is the whole job's ms per 8 x 768 batch
@@ -192,7 +192,7 @@ def run_reference(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
-# BASELINE.json's configurations by (B, H per GPU, L, I/O, accumulation); other shapes are "custom".
+# The benchmark's named configurations by (B, H per GPU, L, I/O, accumulation); other shapes are "custom".
 BASELINE_CONFIGS = {(1, 1, 128, "fp32", "fp32"): "BASELINE configs[0]", (8, 768, 1024, "fp32", "fp32"): "BASELINE configs[1]",
                     (8, 768, 4096, "bf16", "fp32"): "BASELINE configs[2]", (8, 768, 8192, "bf16", "fp16"): "BASELINE configs[3]",
                     (16, 1024, 16384, "fp32", "fp32"): "BASELINE configs[4]"}

@@ -154,7 +154,9 @@ int sffft_debug_umma_probe(int a_kind, int a_slice, int b_pitch, int b_slice, in
  * in-kernel; results equal sffft_filter_spectrum + sffft_conv on a "legacy" plan.  The first call on a
  * device sets up that device (looks up the array's device address, sets kernel attributes); make it
  * before any stream capture.  All calls on a device share the array, so calls whose work overlaps on the
- * GPU race.  sync != 0 waits for the stream and returns the kernel's device-side status. */
+ * GPU race.  sync != 0 waits for the stream and returns the kernel's device-side status; with sync == 0 the
+ * call returns once the work is queued and a device-side error of that call (a barrier timeout) is not
+ * reported, since the next call on the device clears the status word before it launches. */
 int sffft_conv_noalloc(int L, int io, int acc, const void* u, const void* k, int k_dtype, void* y, int B, int H,
                        void* stream, int sync);
 
@@ -175,6 +177,15 @@ int sffft_pipe_destroy(sffft_pipe_t pipe);
  * kernel; returns SFFFT_ERR_TIMEOUT after about limit_us microseconds (1..1e6) with the context intact.
  * No reference counterpart (the reference has no device-side timeouts). */
 int sffft_debug_wait_timeout(int limit_us);
+
+/* Debug: sffft_conv with every barrier wait of the fused kernel limited to limit_us microseconds (1..1e6) and
+ * one arrival withheld (the first warp of the team that converts the first group skips its arrival on the
+ * "operand ready" barrier), so the stage-0 MMAs are never issued and the bounded waits run out: the kernel's
+ * roles see the abort flag, wait for their MMAs in flight, free TMEM and return; sffft_plan_check then reports
+ * SFFFT_ERR_TIMEOUT and the context stays usable.  Exercises the fused kernel's failure path without a fault.
+ * No reference counterpart (the reference fails fast on host errors only, src/sffft.cu:22-23). */
+int sffft_debug_conv_timeout(sffft_plan_t plan, const void* u, const void* Kf, void* y, int B, int H, int limit_us,
+                             void* stream);
 
 #ifdef __cplusplus
 }

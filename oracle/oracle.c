@@ -10,7 +10,7 @@
  *     sqrt(-2 log U1) * cos(2 pi U2) with U1 drawn before U2;
  *   - the reference's input recipe (src/sffft.cu:339-341): u = nrand()*input_scale over B*H*L in
  *     order, then per channel h: a = 1/(4 + L*h/H), k[h,n] = nrand()*exp(-a*n)*sqrt(2a);
- *   - the BASELINE.json profiles: u ~ N(0,1); k[h,n] = N(0,1)*exp(-decay*n/L) [/sqrt(L)], same stream;
+ *   - the benchmark configurations' profiles: u ~ N(0,1); k[h,n] = N(0,1)*exp(-decay*n/L) [/sqrt(L)], same stream;
  *   - the same fp64 direct sum for the two filter layouts the reference lists as not yet exposed
  *     (README.md:174): two-sided y[n] = sum_{m<L} u[m] k2[L-1+n-m] (k2 has 2L-1 taps, k2[L-1] is lag 0)
  *     and period-L circular y[n] = sum_{m<L} u[m] kc[(n-m) mod L].  No reference output pins these; the
@@ -60,7 +60,7 @@ void oracle_gen_reference(unsigned long long seed, int B, int H, int L, double i
   }
 }
 
-/* BASELINE.json profile: k[h,n] = N(0,1) * exp(-decay * n / L) * (sqrt_norm ? 1/sqrt(L) : 1). */
+/* Benchmark-configuration profile: k[h,n] = N(0,1) * exp(-decay * n / L) * (sqrt_norm ? 1/sqrt(L) : 1). */
 void oracle_gen_profile(unsigned long long seed, int B, int H, int L, double decay, int sqrt_norm, float* u, float* k) {
   oracle_rng r = {seed ? seed : 88172645463325252ULL};
   const size_t n = (size_t)B * H * L;

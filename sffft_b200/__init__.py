@@ -72,6 +72,8 @@ def _declare(lib):
         "sffft_baseline_destroy": (I, [P]),
         "sffft_debug_umma_probe": (I, [I, I, I, I, I, I, V, V, V]),
         "sffft_debug_wait_timeout": (I, [I]),
+        "sffft_debug_conv_timeout": (I, [P, V, V, V, I, I, I, V]),
+        "sffft_conv_noalloc": (I, [I, I, I, V, V, I, V, I, I, V, I]),
         "sffft_pipe_create": (I, [ctypes.POINTER(P), P, I, I, I]),
         "sffft_conv_host": (I, [P, V, V, V, V]),
         "sffft_pipe_destroy": (I, [P]),

@@ -67,7 +67,7 @@ static const std::vector<const ConvEntry*>& catalog() {
   return all;
 }
 
-// Built-in B200 default per length: the fastest catalog entry of the plan BASELINE-style workloads name for
+// Built-in B200 default per length: the fastest catalog entry of the plan the benchmark configurations name for
 // that length (B = 8, H = 768, fp32 and bf16 I/O, timed on one B200); the CLI's empirical selector can
 // override it from its own measurements.
 // Composite plans: lengths above the largest single-kernel plan run as block convolutions of up to
@@ -334,12 +334,13 @@ int sffft_irfft(sffft_plan_t p, const void* X, int B, float* x, void* work, void
   return ce == cudaSuccess ? SFFFT_OK : cuda_fail(ce);
 }
 
-static int conv_launch(sffft_plan_t p, const void* u, const void* Kf, void* y, int B, int H, cudaStream_t stream);
+static int conv_launch(sffft_plan_t p, const void* u, const void* Kf, void* y, int B, int H, cudaStream_t stream,
+                       unsigned long long wait_ns, int skip_arrive);
 
 int sffft_conv(sffft_plan_t p, const void* u, const void* Kf, void* y, int B, int H, void* stream) {
   if (!p || !u || !Kf || !y || B < 1 || H < 1) return SFFFT_ERR_INVALID_ARGUMENT;
   if ((((uintptr_t)u | (uintptr_t)y | (uintptr_t)Kf) & 15) != 0) return SFFFT_ERR_INVALID_ARGUMENT;
-  if (p->blocks == 1) return conv_launch(p, u, Kf, y, B, H, (cudaStream_t)stream);
+  if (p->blocks == 1) return conv_launch(p, u, Kf, y, B, H, (cudaStream_t)stream, 0, 0);
 
   // composite plan: u in block-major order, one fused launch per block lag, then the fp32 block sum
   const int P = p->blocks, Lb = p->e->L;
@@ -358,7 +359,7 @@ int sffft_conv(sffft_plan_t p, const void* u, const void* Kf, void* y, int B, in
   ce = launch_block_gather(u, ub, bf, B, H, Lb, P, p->sms, st);
   for (int d = 0; d < P && ce == cudaSuccess && rc == SFFFT_OK; d++)
     rc = conv_launch(p, ub, (const char*)Kf + (size_t)d * H * p->e->N * 8, parts + part_offset(d, P, blk),
-                     (P - d) * B, H, st);
+                     (P - d) * B, H, st, 0, 0);
   if (ce == cudaSuccess && rc == SFFFT_OK) ce = launch_block_sum(parts, y, bf, B, H, Lb, P, p->sms, st);
   const cudaError_t cf = cudaFreeAsync(work, st);
   if (rc) return rc;
@@ -366,7 +367,8 @@ int sffft_conv(sffft_plan_t p, const void* u, const void* Kf, void* y, int B, in
   return ce == cudaSuccess ? SFFFT_OK : cuda_fail(ce);
 }
 
-static int conv_launch(sffft_plan_t p, const void* u, const void* Kf, void* y, int B, int H, cudaStream_t stream) {
+static int conv_launch(sffft_plan_t p, const void* u, const void* Kf, void* y, int B, int H, cudaStream_t stream,
+                       unsigned long long wait_ns = 0, int skip_arrive = 0) {
   const ConvEntry* e = p->e;
   const long long pairs = (long long)((B + 1) / 2) * H;
   const long long groups = (pairs + e->G - 1) / e->G;
@@ -378,6 +380,8 @@ static int conv_launch(sffft_plan_t p, const void* u, const void* Kf, void* y, i
   ConvParams prm;
   prm.u = u; prm.Kf = (const float*)Kf; prm.btab = p->btab; prm.y = y; prm.status = p->status; prm.B = B; prm.H = H;
   prm.ngroups = (int)groups;
+  prm.wait_ns = wait_ns;
+  prm.debug_skip_arrive = skip_arrive;
 #ifdef SFFFT_TRACE
   prm.trace = g_trace;
 #endif
@@ -453,5 +457,13 @@ int sffft_debug_umma_probe(int a_kind, int a_slice, int b_pitch, int b_slice, in
 }
 
 int sffft_debug_wait_timeout(int limit_us) { return wait_timeout_probe(limit_us); }
+
+int sffft_debug_conv_timeout(sffft_plan_t p, const void* u, const void* Kf, void* y, int B, int H, int limit_us,
+                             void* stream) {
+  if (!p || !u || !Kf || !y || B < 1 || H < 1 || p->blocks != 1 || limit_us < 1 || limit_us > 1000000)
+    return SFFFT_ERR_INVALID_ARGUMENT;
+  if ((((uintptr_t)u | (uintptr_t)y | (uintptr_t)Kf) & 15) != 0) return SFFFT_ERR_INVALID_ARGUMENT;
+  return conv_launch(p, u, Kf, y, B, H, (cudaStream_t)stream, 1000ull * (unsigned long long)limit_us, 1);
+}
 
 }  // extern "C"

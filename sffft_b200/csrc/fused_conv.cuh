@@ -29,7 +29,10 @@
 
 namespace sffft {
 
-constexpr unsigned long long kWaitLimitNs = 1000000000ull;   // 1 s per barrier phase
+constexpr unsigned long long kWaitLimitNs = 1000000000ull;   // default: 1 s per barrier phase
+
+// The launch's wait limit (ConvParams::wait_ns, or the default), set by thread 0 before the first block barrier.
+static __shared__ unsigned long long s_wait_ns;
 
 __device__ __forceinline__ float bf16_bits_to_float(uint32_t bits16) { return __uint_as_float(bits16 << 16); }
 
@@ -113,6 +116,14 @@ struct DevOps {
     __nv_bfloat162 a = __floats2bfloat162_rn(v[0], v[1]), b = __floats2bfloat162_rn(v[2], v[3]);
     __stcs(reinterpret_cast<uint2*>(p), make_uint2(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&b)));
   }
+  // Energy of one conversion step: the sum of squares of the 8 values of each of the SEG lanes that share
+  // a run of one sequence, stored by the run's first lane (the steps of a warp are warp-uniform).
+  __device__ __forceinline__ void energy_store(float* part, int e, float ss, int seg) {
+#pragma unroll
+    for (int m = 16; m > 0; m >>= 1)
+      if (m < seg) ss += __shfl_xor_sync(0xffffffffu, ss, m);
+    if ((threadIdx.x & (seg - 1)) == 0) part[e / (8 * seg)] = ss;
+  }
   __device__ __forceinline__ void st4(uint32_t off, float v) { *reinterpret_cast<float*>(sm + off) = v; }
   __device__ __forceinline__ void ld4_staged(uint32_t off, uint32_t rot, float* v) {
     const float4 q = *reinterpret_cast<const float4*>(sm + off);
@@ -195,6 +206,10 @@ struct ConvParams {
   int* status;
   int B, H;
   int ngroups;           // ceil(pairs / G), pairs = ceil(B/2) * H
+  unsigned long long wait_ns;   // limit of every barrier wait, in ns (0: kWaitLimitNs)
+  int debug_skip_arrive;        // test hook of sffft_debug_conv_timeout: g + 1 makes the first warp of the
+                                // team converting group g skip its arrival, so that a barrier never completes
+                                // and the bounded waits run out (0 in every regular launch)
 #ifdef SFFFT_TRACE
   unsigned long long* trace;   // debug builds only: [grid][kTraceRoles][kTraceLen] SM clock stamps
 #endif
@@ -229,7 +244,7 @@ __device__ __forceinline__ bool wait_phase(uint64_t* bar, uint32_t parity, volat
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;
-    if (global_ns() - t0 > kWaitLimitNs) { *abort_flag = 1; return false; }
+    if (global_ns() - t0 > s_wait_ns) { *abort_flag = 1; return false; }
   }
 }
 
@@ -251,7 +266,7 @@ __device__ __forceinline__ bool wait_stamp(const volatile int* stamp, int want, 
   const uint64_t t0 = global_ns();
   while (*stamp < want) {
     if (*abort_flag) return false;
-    if (global_ns() - t0 > kWaitLimitNs) { *abort_flag = 1; return false; }
+    if (global_ns() - t0 > s_wait_ns) { *abort_flag = 1; return false; }
     __nanosleep(64);   // polling warps would otherwise take issue slots from the compute warps
   }
   return true;
@@ -317,6 +332,30 @@ __device__ __forceinline__ bool team_sync(uint64_t* bar, uint32_t& phase, int la
   return ok;
 }
 
+// The conversion task of a group (a team's first task): the energy pass, a team barrier, the pair scales
+// (computed by lane 0 of every warp, which all write the same values and are read by their own warp) and, for
+// a group with a pair to rescale, the scaled pass -- the same code run a second time, so that the rare pass
+// adds no registers to the kernel's allocation.  Returns false when the team barrier gave up.
+template <class P, class TIO, int NB>
+__device__ __forceinline__ bool convert_task(DevOps& ops, const TIO* u, const GroupPairs& gp, int tid, int nthreads,
+                                             float* en, uint64_t* team_bar, uint32_t& team_phase,
+                                             volatile int* abort_flag) {
+  constexpr int ENS = Energy<P>::SLOTS;
+  const int lane = tid & 31;
+#pragma unroll 1
+  for (int pass = 0; pass < 2; pass++) {
+    convert_group<P, TIO, NB>(ops, u, gp, tid, nthreads, pass == 0 ? en : nullptr, en + ENS);
+    if (pass == 1) break;
+    if (!team_sync(team_bar, team_phase, lane, abort_flag)) return false;
+    int redo = 0;
+    if (lane == 0) redo = pair_scales<P>(en, en + ENS, en + ENS + 2 * P::G) ? 1 : 0;
+    redo = __shfl_sync(0xffffffffu, redo, 0);
+    __syncwarp();   // orders lane 0's stores before the other lanes' reads of the scales
+    if (!redo) break;
+  }
+  return true;
+}
+
 template <class P, class TIO, bool ACC16>
 __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kernel(ConvParams prm) {
   using SH = Shape<P, sizeof(TIO)>;
@@ -349,6 +388,7 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
     kstamp[0] = kstamp[1] = -1;
     *conv_done = 0;
     *abort_flag = 0;
+    s_wait_ns = prm.wait_ns ? prm.wait_ns : kWaitLimitNs;
     fence_mbar_init();
   }
   if (prm.btab) {
@@ -438,7 +478,7 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
           t_idle = global_ns();
         } else {
           if (*abort_flag) break;
-          if (global_ns() - t_idle > kWaitLimitNs) { *abort_flag = 1; break; }
+          if (global_ns() - t_idle > s_wait_ns) { *abort_flag = 1; break; }
           // nothing ready: poll again at once (sleeping 32 or 128 ns between polls measured 0.5-1 % slower; the
           // issue slots the spin takes from the compute warps on this scheduler cost less than the delay)
         }
@@ -448,7 +488,7 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
       for (int s = 0; s < NS; s++) {
         if (!done[s]) continue;
         const uint64_t t0 = global_ns();
-        while (!mbar_try_wait(mma_done + s, (uint32_t)((done[s] - 1) & 1)) && global_ns() - t0 < kWaitLimitNs) {
+        while (!mbar_try_wait(mma_done + s, (uint32_t)((done[s] - 1) & 1)) && global_ns() - t0 < s_wait_ns) {
         }
       }
     }
@@ -511,7 +551,9 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
     // ---------------- compute warps ----------------
     // Team `team` (warps team*TWARPS .. of the compute warps) owns slots team*NST .. team*NST + NST - 1
     // and, round after round, runs the TPG tasks of its groups, alternating between its slots.
-    constexpr int NST = SH::NST, TWT = SH::TWARPS * 32;
+    constexpr int NST = SH::NST, TWT = SH::TWARPS * 32, ENS = Energy<P>::SLOTS;
+    static_assert(Energy<P>::SLOTS + 4 * P::G == SH::EN_STRIDE, "energy area");
+    float* energies = reinterpret_cast<float*>(sm + SH::EN_OFF);   // [NS][2 parities][EN_STRIDE]
     const int wc = warp - SH::CW0, team = wc / SH::TWARPS, wt = wc - team * SH::TWARPS;
     const int q = warp & 3, wi = wt >> 2, ttid = wt * 32 + lane;
     uint32_t md_bits = 0;                 // bit l: parity of local slot l's next mma_done phase
@@ -535,11 +577,18 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
         DevOps ops{sm + SH::DATA_OFF + s * P::DATA_BYTES, ACC16, tw_lo, tw_hi, P::N};
         if (lane == 0 && wt == 0) SFFFT_STAMP(2 + team, 3 * ntask);
         if (j == 0) {
-          convert_group<P, TIO, SH::NB>(ops, u, gp, ttid, TWT);
+          // first pass: convert unscaled and measure each sequence's energy; once the team's energies are
+          // in, every thread derives the same pair scales, and a group with a pair to rescale is converted
+          // again with them (pair_scales)
+          float* en = energies + (s * 2 + ((gi / NS) & 1)) * SH::EN_STRIDE;
+          if (!convert_task<P, TIO, SH::NB>(ops, u, gp, ttid, TWT, en, team_done + team, ts_phase, abort_flag)) {
+            ok = false;
+            break;
+          }
           if (lane == 0 && wt == 0) SFFFT_STAMP(2 + team, 3 * ntask + 1);
           fence_async_smem();
           tc_fence_before();
-          warp_arrive(a_ready + s, lane);
+          if (!(prm.debug_skip_arrive == group + 1 && wt == 0)) warp_arrive(a_ready + s, lane);
           if (lane == 0 && wt == 0) atomicAdd((int*)conv_done, 1);
           if (lane == 0 && wt == 0) SFFFT_STAMP(2 + team, 3 * ntask + 2);
         } else {
@@ -548,7 +597,8 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
           md_bits ^= 1u << l;
           if (lane == 0 && wt == 0) SFFFT_STAMP(2 + team, 3 * ntask + 1);
           tc_fence_after();
-          EpiArgs ea{tmem + (uint32_t)(s * P::TMEM_COLS), prm.Kf, prm.y, prm.B, prm.H, group, nullptr, 0};
+          EpiArgs ea{tmem + (uint32_t)(s * P::TMEM_COLS), prm.Kf, prm.y, prm.B, prm.H, group, nullptr, 0,
+                     energies + (s * 2 + ((gi / NS) & 1)) * SH::EN_STRIDE + ENS + 2 * P::G};
           const bool kst = SH::KSLOT > 0 && sid == P::S - 1;
           constexpr int KS = SH::KSLOT > 0 ? SH::KSLOT : 1;
           const int ks = gi % KS;

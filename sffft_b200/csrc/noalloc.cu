@@ -84,11 +84,16 @@ extern "C" int sffft_conv_noalloc(int L, int io, int acc, const void* u, const v
     // one-time set-up per device (and per kernel variant), with that device current
     std::lock_guard<std::mutex> lock(g_mutex);
     if (!ds.scratch) {
-      void* ptr = nullptr;
-      if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || !ptr) return SFFFT_ERR_CUDA;
+      // the device check comes first: on another GPU the library has no kernel image, so the symbol lookup
+      // below would fail with a CUDA error instead of SFFFT_ERR_DEVICE
       cudaDeviceProp prop;
       if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) return SFFFT_ERR_CUDA;
       if (prop.major != 10 || prop.minor != 0) return SFFFT_ERR_DEVICE;
+      void* ptr = nullptr;
+      if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || !ptr) {
+        cudaGetLastError();   // leave no pending error behind for the caller's next CUDA call
+        return SFFFT_ERR_CUDA;
+      }
       ds.sms = prop.multiProcessorCount;
       ds.smem_per_sm = (int)prop.sharedMemPerMultiprocessor;
       ds.smem_optin = (int)prop.sharedMemPerBlockOptin;

@@ -149,7 +149,13 @@ struct Shape {
   static constexpr int NT = 32 * (WC + CW0);
   static constexpr int SEQB = P::L * SIO;                           // input bytes per sequence
   static constexpr int TW_BYTES = ((64 + P::N / 64) * 8 + 127) / 128 * 128;   // two-level twiddle table
-  static constexpr int CAP = 227 * 1024 - 1024 - 512 - TW_BYTES;    // dynamic smem minus align slack, barriers
+  // per slot and round parity: the conversion's energy slots of the group's 2G sequences, then the 2G input
+  // scales and the 2G output scales of pair_scales (floats)
+  static constexpr int EN_SEG = P::L / 8 < 32 ? P::L / 8 : 32;
+  static constexpr int EN_STRIDE = 2 * P::G * (P::L / (8 * EN_SEG)) + 4 * P::G;
+  static constexpr int EN_BYTES_MAX = (4 * 2 * EN_STRIDE * 4 + 127) / 128 * 128;   // for up to 4 slots
+  static constexpr int CAP = 227 * 1024 - 1024 - 512 - TW_BYTES - EN_BYTES_MAX;   // dynamic smem minus align
+                                                                                // slack, barriers, energies
   static constexpr bool fits(int ns) {
     return ns * P::TMEM_COLS <= 512 && P::BMAT_BYTES + ns * P::DATA_BYTES <= CAP;
   }
@@ -184,7 +190,9 @@ struct Shape {
   static constexpr int KBYTES = KSLOT * KC * KROW;
   static constexpr int TW_OFF = K_OFF + KBYTES;
   static constexpr int BAR_OFF = TW_OFF + TW_BYTES;
-  static constexpr int SMEM = BAR_OFF + 512 + 1024;
+  static constexpr int EN_OFF = BAR_OFF + 512;
+  static constexpr int EN_BYTES = (NS * 2 * EN_STRIDE * 4 + 127) / 128 * 128;
+  static constexpr int SMEM = EN_OFF + EN_BYTES + 1024;
   static constexpr int TMEM_ALLOC = pow2ceil(cmax(32, NS * P::TMEM_COLS));
   static constexpr int TPG = 2 * P::S + 1;                          // tasks per group: convert + 2S epilogues
   // 8-byte words from BAR_OFF: a_ready[NS], mma_done[NS], k_full[2], k_empty[2], TMEM base, abort flag,

@@ -82,17 +82,35 @@ SF_HD PairInfo pair_info(int cta, int g, int G, int B, int H, int L) {
 // refilling each register slot with the load NB steps ahead as soon as it has converted the slot (issuing
 // NB loads, converting all NB and only then issuing the next NB drained the loads at every batch: 8 %
 // slower at L = 1024).  Absent sequences (odd B, past the last pair) read as zero.
-// bf16 input is exact in fp16 (up to fp16-subnormal values below 6e-5, whose residue under 3e-8 is
-// dropped), so it has no lo plane to compute.
+// bf16 input within the fp16 range is exact in fp16 (apart from fp16-subnormal values below 6e-5, whose
+// residue under 3e-8 is dropped), so it has no lo plane to compute.  Values beyond the fp16 range
+// (|x| > 65504, possible in fp32 and bf16 input) become infinite in the hi plane and give inf / NaN
+// outputs, as the reference's fp16 conversion does.
+//
+// A group is converted in one or two passes (see pair_scales below):
+//   part != null  first pass: unscaled conversion that also records each sequence's energy: for every run
+//                 of 8 * SEG consecutive elements of one sequence (one step of SEG lanes of a warp) the sum
+//                 of squares, in part[e / (8 * SEG)] (e = element index within the group)
+//   part == null  second pass (only for groups that have a pair to rescale): every value of sequence j is
+//                 multiplied by the power of two psc[j] before the fp16 split.
 // ---------------------------------------------------------------------------------------------
+template <class P>
+struct Energy {
+  static constexpr int SEG = P::L / 8 < 32 ? P::L / 8 : 32;   // lanes whose 8-element runs share a sequence
+  static constexpr int SPS = P::L / (8 * SEG);                 // energy slots per sequence
+  static constexpr int SLOTS = 2 * P::G * SPS;
+};
+
 template <class P, class TIO, int NB, class Ops>
-SF_HD void convert_group(Ops& ops, const TIO* u, const GroupPairs& gp, int tid, int nthreads) {
+SF_HD void convert_group(Ops& ops, const TIO* u, const GroupPairs& gp, int tid, int nthreads, float* part,
+                         const float* psc) {
   constexpr int V0 = P::N / P::R0, MB0 = P::MB(0), NE = 2 * P::G * P::L;
   const int stride = nthreads * 8;
   uint32_t w[NB][8];
-  int mrow[NB], krow[NB];
+  int mrow[NB], krow[NB], eb[NB];
   auto issue = [&](int b, int e) {
     krow[b] = -1;
+    eb[b] = e;
     if (e < NE) {
       const int j = e / P::L, n = e - j * P::L, g = j >> 1, plane = j & 1;
       const PairInfo pi = gp.get(g, P::L);
@@ -107,9 +125,17 @@ SF_HD void convert_group(Ops& ops, const TIO* u, const GroupPairs& gp, int tid, 
     }
   };
   auto finish = [&](int b) {
-    if (krow[b] < 0) return;
+    if (krow[b] < 0) return;   // uniform across a warp: its 256 elements lie all below or all above NE
     float v[8];
     ops.unpack(u, w[b], v);
+    if (part) {
+      float ss = 0.f;
+      for (int q = 0; q < 8; q++) ss += v[q] * v[q];
+      ops.energy_store(part, eb[b], ss, Energy<P>::SEG);
+    } else {
+      const float s = psc[eb[b] / P::L];
+      for (int q = 0; q < 8; q++) v[q] *= s;
+    }
     uint32_t hi[4], lo[4];
     for (int q = 0; q < 4; q++) hi[q] = ops.pack2(v[2 * q], v[2 * q + 1]);
     // K-row k + R0/2 (the lo plane) is R0/16 K-groups further: same swizzle phase, since R0/2 % 8 == 0
@@ -132,6 +158,62 @@ SF_HD void convert_group(Ops& ops, const TIO* u, const GroupPairs& gp, int tid, 
       issue(b, e0 + (b + NB) * stride);
     }
   }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Per-sequence scaling of pairs.
+//
+// A pair packs two batch rows into one complex transform, so the fp16 rounding noise of each stage is set by
+// the pair's combined magnitude and lands in both rows' outputs.  A row much smaller than its partner would
+// then carry the partner's noise: relative error ~ 3.5e-4 * sqrt((1 + E_big / E_small) / 2) for energies
+// E = sum u^2 (the reference transforms every row alone, sfFFT src/sffft.cu:249, and has no such coupling).
+// The conversion's first pass measures both energies; where they differ by 2x or more, or where the pair's
+// rows are all tiny (rms below 2^-6, where fp16 storage would lose digits), the group is converted again
+// with each row multiplied by a power of two: the smaller row is brought within a factor sqrt(2) of its
+// partner's rms (never above the larger row's level, so the fp16 range -- and the reference's overflow at
+// large input scales -- is unchanged for balanced pairs), and tiny pairs are brought up to rms ~1.  The
+// output epilogue multiplies each row by the inverse power of two (exact), or by 0 for an all-zero row,
+// whose output would otherwise be its partner's rounding noise (and whose exact result is 0).
+// Non-finite energies leave the pair unscaled (inf / NaN then propagate as in the reference).  A row whose
+// sum of squares underflows fp32 (|u| below ~1e-19) counts as all-zero; the reference's fp16 storage
+// flushes such values to zero as well.
+// ---------------------------------------------------------------------------------------------
+SF_HD int round_half_log2(float r) {   // round(log2(r) / 2), |result| <= 100
+  float f = 0.5f * log2f(r);
+  f = f > 100.f ? 100.f : (f < -100.f ? -100.f : f);
+  return (int)(f < 0.f ? f - 0.5f : f + 0.5f);
+}
+
+template <class P>
+SF_HD bool pair_scales(const float* part, float* psc, float* osc) {
+  using EN = Energy<P>;
+  bool redo = false;
+  for (int g = 0; g < P::G; g++) {
+    float E[2];
+    for (int p = 0; p < 2; p++) {
+      float s = 0.f;
+      for (int i = 0; i < EN::SPS; i++) s += part[(2 * g + p) * EN::SPS + i];
+      E[p] = s;
+    }
+    int f[2] = {0, 0};
+    const bool finite = E[0] <= 3.0e38f && E[1] <= 3.0e38f;   // false for inf and NaN
+    if (finite) {
+      const float Eb = E[0] > E[1] ? E[0] : E[1];
+      if (Eb > 0.f && Eb < (float)P::L * (1.f / 4096.f)) f[0] = f[1] = round_half_log2((float)P::L / Eb);
+      if (E[0] > 0.f && E[1] > 0.f) {
+        const float r = E[0] / E[1];
+        if (r >= 2.f) f[1] += round_half_log2(r);
+        else if (r <= 0.5f) f[0] += round_half_log2(1.f / r);
+      }
+    }
+    for (int p = 0; p < 2; p++) {
+      const int e = f[p] > 120 ? 120 : f[p];
+      psc[2 * g + p] = ldexpf(1.f, e);
+      osc[2 * g + p] = E[p] == 0.f ? 0.f : ldexpf(1.f, -e);
+      redo = redo || e != 0;
+    }
+  }
+  return redo;
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -202,6 +284,7 @@ struct EpiArgs {
   int B, H, cta;        // cta: the group index (pairs cta*G .. cta*G + G - 1)
   const uint8_t* kst;   // spectrum rows of channels khf, khf+1, ... staged by the loader warp, or null
   int khf;
+  const float* osc;     // output multiplier of each of the group's 2G sequences (pair_scales)
 };
 
 // 1/sqrt(R): the per-stage scale of a radix-R digit (the reference's 1/sqrt(R) per stage, total 1/N).
@@ -328,6 +411,8 @@ SF_HD void epi_finish(Ops& ops, const EpiArgs& ea, const GroupPairs& gp, const E
   for (int j = 0; j < 16; j++) { a[j] = ops.acc_val(raw_re[j]); b[j] = ops.acc_val(raw_im[j]); }
 
   if constexpr (OUT) {
+    // each row's scale undoes its input scaling (pair_scales): a power of two, or 0 for an all-zero row
+    const float s0 = SC * ea.osc[2 * g], s1 = SC * ea.osc[2 * g + 1];
     if constexpr (S == 2) {
       const PairInfo pi = gp.get(g, P::L);
       TIO* y = (TIO*)ea.y;
@@ -335,8 +420,8 @@ SF_HD void epi_finish(Ops& ops, const EpiArgs& ea, const GroupPairs& gp, const E
       for (int j = 0; j < 16; j++) {
         const int n0 = c0 + j;
         if (n0 < P::R0 / 2) {
-          if (pi.off0 >= 0) ops.store1(y + pi.off0 + (long long)n0 * V0 + x.vv, a[j] * SC);
-          if (pi.off1 >= 0) ops.store1(y + pi.off1 + (long long)n0 * V0 + x.vv, b[j] * SC);
+          if (pi.off0 >= 0) ops.store1(y + pi.off0 + (long long)n0 * V0 + x.vv, a[j] * s0);
+          if (pi.off1 >= 0) ops.store1(y + pi.off1 + (long long)n0 * V0 + x.vv, b[j] * s1);
         }
       }
     } else {
@@ -346,8 +431,8 @@ SF_HD void epi_finish(Ops& ops, const EpiArgs& ea, const GroupPairs& gp, const E
         const int n0 = c0 + j;
         if (n0 < P::R0 / 2) {
           const int n = n0 * V0 + x.vv;
-          ops.st4(out_stage_word(g * 2 * P::L + n) * 4, a[j] * SC);
-          ops.st4(out_stage_word(g * 2 * P::L + P::L + n) * 4, b[j] * SC);
+          ops.st4(out_stage_word(g * 2 * P::L + n) * 4, a[j] * s0);
+          ops.st4(out_stage_word(g * 2 * P::L + P::L + n) * 4, b[j] * s1);
         }
       }
     }

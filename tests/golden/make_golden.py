@@ -1,6 +1,6 @@
 """Regenerates the golden fixtures in this folder from the reference itself.
 
-CPU (this container, where /root/reference exists):
+CPU (where the reference source tree exists and oracle/_ref has been built from it):
     python tests/golden/make_golden.py rng
   compiles nothing itself; needs oracle/_ref/ref_harness (`make -C oracle ref`), which is the reference's
   own src/sffft.cu built in place, and records the first draws of its nrand() for three seeds.

@@ -117,3 +117,30 @@ def bf16_bits(x):
 
 def bf16_from_bits(b):
     return (np.asarray(b, np.uint32) << 16).view(np.float32)
+
+
+# Row scales of the pairing tests: batch rows 2j and 2j+1 share one complex transform, so each pair below
+# puts rows of very different size (or an all-zero row) side by side; the last pair is all tiny.
+PAIR_SCALES = [1.0, 1e-3, 1e-4, 1.0, 0.0, 1.0, 1.0, 1.0, 1e-5, 2e-5]
+
+
+def scaled_pair_inputs(oracle, H, L, io, seed=0):
+    """u [len(PAIR_SCALES)][H][L] with row b scaled by PAIR_SCALES[b], k of the configs' profile; both
+    rounded to bf16 (and returned as fp32 values) for bf16 I/O."""
+    B = len(PAIR_SCALES)
+    u, k = oracle.gen_profile(B, H, L, decay=4.0, sqrt_norm=True, seed=seed)
+    u = (u * np.asarray(PAIR_SCALES, np.float32)[:, None, None]).astype(np.float32)
+    if io == "bf16":
+        u, k = to_bf16(u), to_bf16(k)
+    return u, k
+
+
+def per_row_rel_l2(y, ref):
+    """Relative L2 error of every (b, h) row, with relative_l2's convention for an all-zero reference row
+    (0 if the row is exactly zero, else inf; sfFFT src/selection.h:26-29)."""
+    y = np.asarray(y, np.float64)
+    ref = np.asarray(ref, np.float64)
+    d = np.sum((y - ref) ** 2, axis=-1)
+    r = np.sum(ref ** 2, axis=-1)
+    out = np.where(r > 0, np.sqrt(d / np.where(r > 0, r, 1.0)), np.where(d == 0, 0.0, np.inf))
+    return out

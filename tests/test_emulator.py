@@ -80,3 +80,24 @@ def test_staged_spectrum_partial_groups(oracle):
     # read outside the staged spectrum rows)
     for name in ["16x16/w4", "32x32/w4"]:
         assert run_case(oracle, name, 2, 33) <= TOL[("fp32", "fp32")]
+
+
+@pytest.mark.parametrize("name", ["16x16/w4", "16x16x16/w4"])
+@pytest.mark.parametrize("io,acc", [("fp32", "fp32"), ("bf16", "fp32"), ("fp32", "fp16"), ("bf16", "fp16")])
+def test_pairs_of_very_different_scale(oracle, name, io, acc):
+    # every single row within the tolerance, including rows 1e3 / 1e4 below their pair partner, an all-zero
+    # row beside a full-scale one (exactly zero output), and a pair of tiny rows
+    from tests.oracle_py import PAIR_SCALES, per_row_rel_l2, scaled_pair_inputs
+    R = radices(name)
+    L = int(np.prod(R)) // 2
+    u, k = scaled_pair_inputs(oracle, 2, L, io, seed=21)
+    Kc = spectrum_digit_order(k, R)
+    Kf = np.stack([Kc.real, Kc.imag], -1).astype(np.float32)
+    if io == "bf16":
+        y = bf16_from_bits(sf.emu_conv(name, bf16_bits(u), Kf, io="bf16", acc=acc)).reshape(u.shape)
+    else:
+        y = sf.emu_conv(name, u, Kf, io="fp32", acc=acc)
+    errs = per_row_rel_l2(y, oracle.direct_conv(u, k))
+    assert errs.shape == (len(PAIR_SCALES), 2)
+    assert np.all(errs <= TOL[(io, acc)]), errs
+    assert not y[4].any()

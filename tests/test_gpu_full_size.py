@@ -1,4 +1,4 @@
-"""Parity at the BASELINE.json configurations' full sizes, with the plan each configuration names.
+"""Parity at the benchmark configurations' full sizes, with the plan each configuration names.
 
 Every output is compared with the cuFFT fp32 pipeline on the device (the reference's own run-time oracle,
 src/sffft.cu:365-371), and sampled sequences with the fp64 direct convolution (src/sffft.cu:376-378).

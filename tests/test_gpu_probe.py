@@ -49,3 +49,30 @@ def test_bounded_wait_reports_timeout_and_context_survives():
     Bm, Bb = small_int_halves((16, 16), rng)
     D = sf.umma_probe(0, 0, 128, 0, Ab, Bb)
     np.testing.assert_array_equal(D.view(np.float32), A.astype(np.float32) @ Bm.astype(np.float32).T)
+
+
+@pytest.mark.parametrize("name,B,H", [("64x32/w8", 2, 1), ("32x16x16/w8", 8, 4), ("16x16/w4", 8, 40)])
+def test_fused_kernel_timeout_path(oracle, cuda_device, name, B, H):
+    # One warp of the fused kernel withholds its arrival on a stage barrier, so that group's MMAs are never
+    # issued; with every wait limited to 2 ms the kernel's roles see the abort flag, wait for the MMAs in
+    # flight, free their TMEM and return, and the plan's status word reads SFFFT_ERR_TIMEOUT.  A regular launch
+    # on the same context then passes parity (a CTA that kept its TMEM would block every later allocation on
+    # its SM).  Other CTAs of the launch (H = 4, 40) finish their groups normally.
+    import torch
+
+    from tests.conftest import rel_l2
+    R = [int(x) for x in name.split("/")[0].split("x")]
+    L = int(np.prod(R)) // 2
+    u, k = oracle.gen_profile(B, H, L, seed=7)
+    plan = sf.Plan(L, config=name)
+    ut = torch.from_numpy(u).to(cuda_device)
+    Kf = plan.filter_spectrum(torch.from_numpy(k).to(cuda_device))
+    y = torch.zeros_like(ut)
+    st = sf.lib().sffft_debug_conv_timeout(plan._h, ut.data_ptr(), Kf.data_ptr(), y.data_ptr(), B, H, 2000, None)
+    assert st == sf.OK
+    assert sf.lib().sffft_plan_check(plan._h) == sf.ERR_TIMEOUT
+    assert sf.lib().sffft_plan_check(plan._h) == sf.OK          # the check cleared the status word
+    y2 = plan.conv(ut, Kf)
+    plan.check()
+    assert rel_l2(y2.cpu().numpy(), oracle.direct_conv(u, k)) <= 5e-4
+    plan.close()
