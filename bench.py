@@ -1,22 +1,29 @@
-"""Benchmark of the fused causal long convolution (headline metric: ms per B=8 x H=768 batch and
-fraction of the HBM / tensor roofline).
+"""Benchmark of the fused causal long convolution (headline metric: ms per B=8 x H=768 batch and fraction of
+the HBM / tensor roofline).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--L 1024] [--io fp32]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--L 1024] [--io fp32] ...
     torchrun --nproc-per-node N bench.py --gpus N ...      (one rank per GPU)
 
-Workload (default): the headline configuration configs[1] -- B=8, H=768 channels per GPU, L=1024, fp32 I/O, fp32
-accumulation, u ~ N(0,1), k = N(0,1) exp(-4n/L)/sqrt(L).  A step is one sffft_conv launch over the
-GPU's batch.  With N GPUs each rank owns its own 768-channel slice of an N*768-channel batch (channel
-sharding, weak scaling, no collective on the data path); `value` is the whole job's ms per 8 x 768 batch
-= max-over-ranks step time / N.  Inputs rotate over four independent sets (u, y, Kf) of ~63 MB each so that
-every step reads from HBM, not from the 126 MB L2.
+Workload (default): configuration configs[1] -- one batch of B=8 x H=768 channels, L=1024, fp32 I/O, fp32
+accumulation, u ~ N(0,1), k = N(0,1) exp(-4n/L)/sqrt(L).  A step is one sffft_conv launch per GPU.  With N GPUs
+the batch is sharded by channel (rank r owns sffft_shard_range(768, N, r), its u/y slices and spectrum rows;
+no collective on the data path) and `value` is the fixed batch's ms = max-over-ranks step time (strong
+scaling).  `weak_scaling` adds the per-GPU-fixed variant: every rank convolves a whole 8 x 768 batch of its own
+and the line reports max step time / N per batch.  Inputs rotate over independent sets (u, y, Kf) whose total
+exceeds the 126 MB L2, so every step reads from HBM.
+
+At N = 1 the line also carries `sweep`: the metric's L = 128..8192 x {fp32, bf16} points (B=8, H=768, default
+plan, fp32 accumulation) and configurations 2-4, each with ms per batch, roofline fraction and the cuFFT
+pad/R2C/multiply/C2R/slice pipeline on the same GPU timed the same way.  `parity` compares sampled sequences of
+every rank's output with the fp64 oracle (outside the timed region).
 
 --impl reference times the reference's CPU path for the same metric -- the fp64 direct causal convolution
-(sfFFT src/sffft.cu:376-378, restated in oracle/oracle.c) on all host cores -- on a bounded sample of
-sequences per step, scaled to a full batch; under torchrun only rank 0 runs it.
+(sfFFT src/sffft.cu:376-378, restated in oracle/oracle.c) on all host cores -- on a bounded sample of sequences
+per step, scaled to a full batch; under torchrun only rank 0 runs it.
 """
 import argparse
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -30,7 +37,12 @@ METRIC = "ms/batch and % of roofline, B=8×H=768, L=128–8192, fp32/bf16 I/O"
 UNIT = "ms/batch"
 GB10_PUBLISHED_MS = {(1024, "fp32"): 0.459, (1024, "bf16"): 0.440, (128, "fp32"): 0.033, (4096, "bf16"): 1.342,
                      (8192, "bf16"): 3.434, (8192, "fp32"): 4.184}
-NSETS = 4
+L2_BYTES = 126e6
+# The benchmark's named configurations by (B, H, L, I/O, accumulation); other shapes are "custom".
+NAMED_CONFIGS = {(1, 1, 128, "fp32", "fp32"): "configs[0]", (8, 768, 1024, "fp32", "fp32"): "configs[1]",
+                 (8, 768, 4096, "bf16", "fp32"): "configs[2]", (8, 768, 8192, "bf16", "fp16"): "configs[3]",
+                 (16, 1024, 16384, "fp32", "fp32"): "configs[4]"}
+SWEEP_EXTRA = [(8, 768, 4096, "bf16", "fp32"), (8, 768, 8192, "bf16", "fp16"), (16, 1024, 16384, "fp32", "fp32")]
 
 
 def peaks():
@@ -49,6 +61,20 @@ def flops_per_seq(radices):
     return 4 * radices[0] * N + 16 * N * sum(radices[1:])
 
 
+def roofline(B, H, L, io, radices, ms):
+    """(bound, achieved, peak, unit, frac, alg_bytes, alg_flops, t_roof_ms) of one batch in `ms`."""
+    s_io = 4 if io == "fp32" else 2
+    alg_bytes = 2 * B * H * L * s_io + H * 2 * L * 8
+    alg_flops = B * H * flops_per_seq(radices)
+    hbm, tc, _ = peaks()
+    t_hbm, t_tc = alg_bytes / (hbm * 1e9), alg_flops / (tc * 1e12)
+    if t_hbm >= t_tc:
+        bound, achieved, peak, unit = "hbm", alg_bytes / (ms * 1e-3) / 1e9, hbm, "GB/s"
+    else:
+        bound, achieved, peak, unit = "tensor", alg_flops / (ms * 1e-3) / 1e12, tc, "TFLOP/s"
+    return bound, achieved, peak, unit, achieved / peak, alg_bytes, alg_flops, max(t_hbm, t_tc) * 1e3
+
+
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -57,12 +83,16 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--L", type=int, default=1024)
     ap.add_argument("--B", type=int, default=8)
-    ap.add_argument("--H", type=int, default=768)
+    ap.add_argument("--H", type=int, default=768, help="channels of the whole batch (sharded over the GPUs)")
     ap.add_argument("--io", default="fp32", choices=["fp32", "bf16"])
     ap.add_argument("--acc", default="fp32", choices=["fp32", "fp16"])
     ap.add_argument("--config", default=None)
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--chunks", type=int, default=0, help="chunks of the host-buffer pipeline (0 = 4)")
+    ap.add_argument("--sweep", default="auto", choices=["auto", "on", "off"],
+                    help="metric sweep and configurations 2-4 (auto: at N = 1 only)")
+    ap.add_argument("--weak", default="auto", choices=["auto", "on", "off"],
+                    help="per-GPU-fixed batch beside the sharded one (auto: at N > 1 only)")
     return ap.parse_args()
 
 
@@ -126,15 +156,36 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def make_inputs(torch, dev, B, H, L, io, seed):
+def make_inputs(torch, dev, B, H, L, io, seed, decay=4.0, sqrt_norm=True):
+    """Seeded u [B][H][L] ~ N(0,1) and k [H][L] = N(0,1) exp(-decay n / L) [/ sqrt(L)], both rounded to bf16
+    for bf16 I/O."""
     g = torch.Generator(device=dev)
     g.manual_seed(seed)
     u = torch.randn((B, H, L), device=dev, generator=g)
     n = torch.arange(L, device=dev, dtype=torch.float32)
-    k = torch.randn((H, L), device=dev, generator=g) * torch.exp(-4.0 * n / L) / L ** 0.5
+    k = torch.randn((H, L), device=dev, generator=g) * torch.exp(-decay * n / L)
+    if sqrt_norm:
+        k = k / L ** 0.5
     if io == "bf16":
         u, k = u.to(torch.bfloat16), k.to(torch.bfloat16)
     return u, k
+
+
+def n_sets(B, H, L, io):
+    """Rotating input/output/spectrum sets: enough for their total to exceed L2 about twice."""
+    s_io = 4 if io == "fp32" else 2
+    per = 2 * B * H * L * s_io + H * 2 * L * 8
+    return int(min(64, max(2, math.ceil(2.2 * L2_BYTES / per))))
+
+
+def event_time(torch, stream, fn, steps):
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(steps):
+        fn(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
 
 
 def cpu_baseline_run(args, budget_s=15.0):
@@ -183,7 +234,7 @@ def run_reference(args, world, rank):
     value = statistics.median(ms_steps)
     line = {"impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": args.gpus,
             "steps": len(ms_steps), "warmup": max(1, args.warmup // 3), "ms_per_step": round(value, 4),
-            "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+            "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "f64",
             "data": "synthetic", "config": {"workload": f"causal long conv B={args.B} H={args.H} L={args.L}",
                                             "B": args.B, "H": args.H, "L": args.L, "io": args.io},
             "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": info["cores"], "kind": "port",
@@ -192,10 +243,98 @@ def run_reference(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
-# The benchmark's named configurations by (B, H per GPU, L, I/O, accumulation); other shapes are "custom".
-BASELINE_CONFIGS = {(1, 1, 128, "fp32", "fp32"): "BASELINE configs[0]", (8, 768, 1024, "fp32", "fp32"): "BASELINE configs[1]",
-                    (8, 768, 4096, "bf16", "fp32"): "BASELINE configs[2]", (8, 768, 8192, "bf16", "fp16"): "BASELINE configs[3]",
-                    (16, 1024, 16384, "fp32", "fp32"): "BASELINE configs[4]"}
+class Workload:
+    """A plan and rotating device sets for B x H channels [h0, h0 + H) of a batch."""
+
+    def __init__(self, torch, sf, dev, local, B, H, L, io, acc, config, seed, decay=4.0, sqrt_norm=True,
+                 sets=None):
+        self.torch, self.B, self.H, self.L, self.io = torch, B, H, L, io
+        self.plan = sf.Plan(L, io=io, acc=acc, config=config, device=local)
+        self.stream = torch.cuda.current_stream(dev)
+        self.sets = []
+        for s in range(sets or n_sets(B, H, L, io)):
+            u, k = make_inputs(torch, dev, B, H, L, io, seed + s, decay=decay, sqrt_norm=sqrt_norm)
+            Kf = self.plan.filter_spectrum(k, stream=self.stream)
+            self.sets.append((u, Kf, torch.empty_like(u), k))
+        torch.cuda.synchronize(dev)
+
+    def step(self, i):
+        u, Kf, y, _ = self.sets[i % len(self.sets)]
+        st = self.plan.conv_ptr(u.data_ptr(), Kf.data_ptr(), y.data_ptr(), self.B, self.H, self.stream)
+        if st:
+            import sffft_b200 as sf
+            raise sf.SffftError(st, "conv")
+
+    def time(self, steps, warmup):
+        for i in range(warmup):
+            self.step(i)
+        self.plan.check()
+        ms = event_time(self.torch, self.stream, self.step, steps)
+        self.plan.check()
+        return ms
+
+    def parity(self, oracle, nseq=6):
+        """Max relative L2 of sampled sequences of set 0 against the fp64 oracle (run once more first)."""
+        import numpy as np
+        self.step(0)
+        self.plan.check()
+        u, _, y, k = self.sets[0]
+        un, kn, yn = u.float().cpu().numpy(), k.float().cpu().numpy(), y.float().cpu().numpy()
+        total = self.B * self.H
+        seqs = np.unique(np.linspace(0, total - 1, min(nseq, total)).astype(np.int64))
+        ref = oracle.direct_conv_seqs(un, kn, seqs)
+        got = yn.reshape(total, self.L)[seqs].astype(np.float64)
+        errs = np.sqrt(np.sum((got - ref) ** 2, axis=1) / np.maximum(np.sum(ref ** 2, axis=1), 1e-300))
+        return float(errs.max()), len(seqs)
+
+    def close(self):
+        self.plan.close()
+        self.sets = []
+
+
+def cufft_ms(torch, sf, dev, wl, steps, warmup):
+    """The cuFFT pipeline (sffft_baseline_run, full = pad -> R2C -> x spectrum -> C2R -> slice) on the same
+    rotating sets (fp32: the pipeline's own type), timed like the fused kernel."""
+    fsets = [(u.float(), torch.empty(u.shape, dtype=torch.float32, device=dev)) for u, _, _, _ in wl.sets]
+    k = wl.sets[0][3].float().contiguous()
+    bl = sf.Baseline(wl.L, wl.B, wl.H, k, device=dev.index)
+    stream = torch.cuda.current_stream(dev)
+
+    def step(i):
+        u, y = fsets[i % len(fsets)]
+        bl.run(u, y, full=True, stream=stream)
+
+    for i in range(warmup):
+        step(i)
+    torch.cuda.synchronize(dev)
+    ms = event_time(torch, stream, step, steps)
+    bl.close()
+    del fsets
+    return ms
+
+
+def run_sweep(torch, sf, dev, local, steps, warmup):
+    points = [(8, 768, L, io, "fp32") for io in ("fp32", "bf16") for L in (128, 256, 512, 1024, 2048, 4096, 8192)]
+    points += SWEEP_EXTRA
+    out = []
+    for B, H, L, io, acc in points:
+        decay, sqrt_norm = (8.0, True) if L == 16384 else (4.0, True)
+        wl = Workload(torch, sf, dev, local, B, H, L, io, acc, None, seed=500 + L, decay=decay, sqrt_norm=sqrt_norm)
+        ms = wl.time(steps, warmup)
+        bound, achieved, peak, unit, frac, _, _, _ = roofline(B, H, L, io, wl.plan.radices, ms)
+        try:
+            cms = cufft_ms(torch, sf, dev, wl, steps, warmup)
+        except Exception as exc:   # reported, not fatal: the sweep's fused numbers stand on their own
+            cms = None
+            print(f"cuFFT pipeline failed at L={L}: {exc}", file=sys.stderr)
+        out.append({"config": NAMED_CONFIGS.get((B, H, L, io, acc), "sweep"), "B": B, "H": H, "L": L, "io": io,
+                    "acc": acc, "plan": wl.plan.config, "ms": round(ms, 5), "bound": bound,
+                    "achieved": round(achieved, 2), "unit": unit, "frac": round(frac, 4),
+                    "cufft_ms": round(cms, 5) if cms else None,
+                    "vs_cufft": round(cms / ms, 3) if cms else None, "sets": len(wl.sets)})
+        wl.close()
+        torch.cuda.empty_cache()
+    return out
 
 
 def main():
@@ -208,139 +347,137 @@ def main():
             dist.destroy_process_group()
         return
 
-    import numpy as np
     import torch
+
     import sffft_b200 as sf
+    from tests.oracle_py import Oracle
 
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     B, H, L = args.B, args.H, args.L
-    plan = sf.Plan(L, io=args.io, acc=args.acc, config=args.config, device=local)
-    stream = torch.cuda.current_stream(dev)
-    sets = []
-    for s in range(NSETS):
-        u, k = make_inputs(torch, dev, B, H, L, args.io, seed=1000 * rank + s)
-        Kf = plan.filter_spectrum(k, stream=stream)
-        sets.append((u, Kf, torch.empty_like(u)))
-    # pinned host buffers of the end-to-end leg, made (and y written once on the host) before the timed region
-    u_h = sets[0][0].cpu().pin_memory()
-    y_h = torch.zeros_like(u_h).pin_memory()
-    torch.cuda.synchronize(dev)
-
-    def step(i):
-        u, Kf, y = sets[i % NSETS]
-        st = plan.conv_ptr(u.data_ptr(), Kf.data_ptr(), y.data_ptr(), B, H, stream)
-        if st:
-            raise sf.SffftError(st, "conv")
-
-    for i in range(args.warmup):
-        step(i)
-    plan.check()
+    h0, h1 = sf.shard_range(H, world, rank)
+    Hg = h1 - h0
+    # this rank's channel shard of the batch (its own seeded data of the batch's distribution)
+    wl = Workload(torch, sf, dev, local, B, Hg, L, args.io, args.acc, args.config, seed=1000 + h0)
+    plan = wl.plan
 
     def barrier():
         if world > 1:
             import torch.distributed as dist
             dist.barrier(device_ids=[local])
 
+    def allmax(x):
+        if world == 1:
+            return x
+        import torch.distributed as dist
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for i in range(args.warmup):
+        wl.step(i)
+    plan.check()
     clocks = ClockSampler(local)
     clocks.start()
     barrier()
     torch.cuda.synchronize(dev)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for i in range(args.steps):
-        step(i)
-    e1.record(stream)
-    torch.cuda.synchronize(dev)
+    ms_step = event_time(torch, wl.stream, wl.step, args.steps)
     barrier()
-    ms_total = e0.elapsed_time(e1)
     clk = clocks.stop()
     plan.check()
-    ms_step = ms_total / args.steps
-    if world > 1:
-        import torch.distributed as dist
-        t = torch.tensor([ms_step], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms_step = float(t.item())
+    ms_step = allmax(ms_step)
 
-    # end to end through the public host-buffer call (sffft_conv_host): every step uploads u from pinned host
-    # memory, runs the fused convolution and downloads y, in channel chunks whose copies and kernels overlap
-    Kf_d = sets[0][1]
-    pipe = sf.HostPipe(plan, B, H, args.chunks)
+    # parity of this rank's shard against the fp64 oracle (outside the timed region), max over ranks
+    oracle = Oracle()
+    perr, nchk = wl.parity(oracle)
+    perr = allmax(perr)
+
+    # end to end through the public host-buffer call (sffft_conv_host): every step uploads the shard of u from
+    # pinned host memory, runs the fused convolution and downloads y, in chunks whose copies and kernels overlap
+    u_h = wl.sets[0][0].cpu().pin_memory()
+    y_h = torch.zeros_like(u_h).pin_memory()
+    Kf_d = wl.sets[0][1]
+    pipe = sf.HostPipe(plan, B, Hg, args.chunks)
     pipe_chunks = args.chunks if args.chunks > 0 else 4
-    # pinned buffers fresh from torch.empty(pin_memory=True), never written on the host, transferred at 1.04 ms
-    # per step here against 0.74 ms for the buffers above; warm up the way a caller reusing its buffers would
     for _ in range(max(args.warmup, 30)):
-        pipe.conv(u_h, Kf_d, y_h, stream=stream)
+        pipe.conv(u_h, Kf_d, y_h, stream=wl.stream)
     torch.cuda.synchronize(dev)
     barrier()
-    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    f0.record(stream)
-    for _ in range(args.e2e_steps):
-        pipe.conv(u_h, Kf_d, y_h, stream=stream)
-    f1.record(stream)
-    torch.cuda.synchronize(dev)
+    e2e_step = event_time(torch, wl.stream, lambda i: pipe.conv(u_h, Kf_d, y_h, stream=wl.stream), args.e2e_steps)
     plan.check()
     pipe.close()
-    e2e_step = f0.elapsed_time(f1) / args.e2e_steps
-    if world > 1:
-        import torch.distributed as dist
-        t = torch.tensor([e2e_step], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_step = float(t.item())
+    e2e_step = allmax(e2e_step)
+    # this rank's plain copy rates over PCIe (each direction alone, pinned buffers)
+    u_d = torch.empty_like(wl.sets[0][0])
+    h2d_ms = event_time(torch, wl.stream, lambda i: u_d.copy_(u_h, non_blocking=True), 5)
+    d2h_ms = event_time(torch, wl.stream, lambda i: y_h.copy_(u_d, non_blocking=True), 5)
+    nbytes = u_h.numel() * u_h.element_size()
+
+    # per-GPU-fixed batch (weak scaling): every rank convolves a whole B x H batch of its own
+    weak = None
+    if args.weak == "on" or (args.weak == "auto" and world > 1):
+        wk = Workload(torch, sf, dev, local, B, H, L, args.io, args.acc, args.config, seed=2000 + rank)
+        wms = allmax(wk.time(args.steps, args.warmup))
+        wk.close()
+        weak = {"ms_per_step": round(wms, 5), "value": round(wms / world, 5), "unit": UNIT, "H_per_gpu": H,
+                "H_total": H * world, "what": f"each of the {world} GPUs convolves its own B={B} x H={H} batch; "
+                                              "value = max step time / N per batch"}
+
+    sweep = None
+    if rank == 0 and (args.sweep == "on" or (args.sweep == "auto" and world == 1)):
+        sweep = run_sweep(torch, sf, dev, local, max(10, min(args.steps, 30)), max(3, args.warmup))
 
     if rank == 0:
-        s_io = 4 if args.io == "fp32" else 2
-        N = 2 * L
-        alg_bytes = 2 * B * H * L * s_io + H * N * 8
-        alg_flops = B * H * flops_per_seq(plan.radices)
-        hbm, tc, src = peaks()
-        t_hbm, t_tc = alg_bytes / (hbm * 1e9), alg_flops / (tc * 1e12)
-        bound = "hbm" if t_hbm >= t_tc else "tensor"
-        if bound == "hbm":
-            achieved, peak, unit = alg_bytes / (ms_step * 1e-3) / 1e9, hbm, "GB/s"
-        else:
-            achieved, peak, unit = alg_flops / (ms_step * 1e-3) / 1e12, tc, "TFLOP/s"
+        bound, achieved, peak, unit, frac, alg_bytes, alg_flops, t_roof = roofline(B, H, L, args.io, plan.radices,
+                                                                                   ms_step)
+        _, _, src = peaks()
         traffic = None
         tp = os.path.join(ROOT, "profiles", "traffic.json")
         if os.path.exists(tp):
-            tj = json.load(open(tp))
-            traffic = tj.get(f"{plan.config}|{args.io}|{L}|{B}x{H}")
+            traffic = json.load(open(tp)).get(f"{plan.config}|{args.io}|{L}|{B}x{H}") if world == 1 else None
         cpu_ms, cpu_info = (None, None)
         if world == 1:
             cpu_ms, cpu_info = cpu_baseline_run(args)
-        value = ms_step / world
         pub = GB10_PUBLISHED_MS.get((L, args.io)) if (B, H, args.acc) == (8, 768, "fp32") else None
+        name = NAMED_CONFIGS.get((B, H, L, args.io, args.acc), "custom")
         line = {
-            "metric": METRIC, "value": round(value, 5), "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": False, "scaling": "weak",
-            "vs_baseline": round(value / pub, 4) if pub else None, "dtype": "f16",
+            "metric": METRIC, "value": round(ms_step, 5), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": False, "scaling": "strong",
+            "vs_baseline": round(ms_step / pub, 4) if pub else None, "dtype": "f16",
             "data": "synthetic (seeded torch.randn u; k = N(0,1) exp(-4n/L)/sqrt(L))",
-            "config": {"workload": f"{BASELINE_CONFIGS.get((B, H, L, args.io, args.acc), 'custom')}: causal long conv "
-                                   f"B={B} H={H} per GPU, L={L}, {args.io} I/O, {args.acc} accumulation",
-                       "plan": plan.config, "B": B, "H_per_gpu": H, "H_total": H * world, "L": L, "io": args.io,
-                       "acc": args.acc, "occupancy": plan.info["occupancy"], "smem_bytes": plan.info["smem_bytes"],
-                       "parallelism": f"channel-sharded x{world}, no collective on the data path",
-                       "l2": f"{NSETS} rotating input/output/spectrum sets of {alg_bytes / 1e6:.0f} MB each "
-                             f"(> 126 MB L2 in aggregate)",
+            "config": {"workload": f"{name}: causal long conv B={B} H={H} L={L}, {args.io} I/O, {args.acc} "
+                                   f"accumulation, channel-sharded over {world} GPU(s)",
+                       "plan": plan.config, "B": B, "H_total": H, "H_per_gpu": Hg, "L": L, "io": args.io,
+                       "acc": args.acc, "smem_bytes": plan.info["smem_bytes"],
+                       "parallelism": f"channel-sharded x{world} (fixed batch), no collective on the data path",
+                       "l2": f"{len(wl.sets)} rotating input/output/spectrum sets per GPU "
+                             f"(> 126 MB L2 in aggregate at N = 1)",
                        "vs_baseline_ref": "reference GB10 published ms/batch (README.md:29-35)" if pub else None},
             "roofline": {"bound": bound, "achieved": round(achieved, 2), "peak": peak, "unit": unit,
-                         "frac": round(achieved / peak, 4), "traffic": traffic,
+                         "frac": round(frac, 4), "traffic": traffic,
                          "peak_source": f"{src} (MEASURED_PEAKS.json)" if src == "measured" else src,
-                         "algorithmic_bytes": alg_bytes, "algorithmic_flops": alg_flops,
-                         "t_roof_ms": round(max(t_hbm, t_tc) * 1e3, 5)},
-            "e2e": {"value": round(e2e_step / world, 5), "unit": UNIT, "h2d_bytes_per_step": u_h.numel() * u_h.element_size(),
-                    "d2h_bytes_per_step": y_h.numel() * y_h.element_size(),
-                    "path": f"pinned host u -> sffft_conv_host (C ABI: ~{pipe_chunks} batch-row chunks, upload / fused "
-                            "conv / download overlapped, one stream per stage) -> pinned host y, per step"},
+                         "algorithmic_bytes": alg_bytes, "algorithmic_flops": alg_flops, "t_roof_ms": round(t_roof, 5)},
+            "e2e": {"value": round(e2e_step, 5), "unit": UNIT, "h2d_bytes_per_step": nbytes,
+                    "d2h_bytes_per_step": nbytes, "h2d_gbs": round(nbytes / (h2d_ms * 1e6), 2),
+                    "d2h_gbs": round(nbytes / (d2h_ms * 1e6), 2),
+                    "path": f"pinned host u -> sffft_conv_host (C ABI: ~{pipe_chunks} chunks, upload / fused conv / "
+                            "download overlapped, one stream per stage) -> pinned host y, per step, per GPU shard "
+                            "(h2d_gbs / d2h_gbs: rank 0's plain copy rate of its shard, each direction alone)"},
+            "parity": {"max_rel_l2": perr, "seqs_checked": nchk, "ranks": world,
+                       "what": "sampled sequences of every rank's output vs the fp64 direct convolution"},
             "gpu_launches": args.steps * world,
             "clocks": clk,
         }
+        if weak:
+            line["weak_scaling"] = weak
+        if sweep:
+            line["sweep"] = sweep
         if cpu_ms is not None:
             line["cpu_baseline"] = {"value": round(cpu_ms, 3), "unit": UNIT, "cores": cpu_info["cores"], "kind": "port",
                                     "sample": cpu_info["sample"]}
         print(json.dumps(line), flush=True)
-    plan.close()
+    wl.close()
+    barrier()
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()

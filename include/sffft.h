@@ -173,6 +173,23 @@ int sffft_pipe_create(sffft_pipe_t* pipe, sffft_plan_t plan, int B, int H, int c
 int sffft_conv_host(sffft_pipe_t pipe, const void* u_host, const void* Kf, void* y_host, void* stream);
 int sffft_pipe_destroy(sffft_pipe_t pipe);
 
+/* Channel-sharded convolution over several devices.  No reference counterpart: the reference runs on device 0
+ * only (src/sffft.cu:490).  Shard g of G owns channels [h0, h1) = sffft_shard_range(H, G, g) and runs on the
+ * device of plans[g] (plans share L and the I/O type; one device may hold several shards).
+ *   sffft_conv_multi: device-resident shards, asynchronous: u[g], y[g] are [B][h1 - h0][L] and Kf[g] is
+ *     [h1 - h0][N] on plans[g]'s device; one sffft_conv per shard on streams[g] (NULL: default streams).
+ *   sffft_multi_pipe_create / sffft_conv_host_multi: one [B][H][L] batch in host memory (pinned for overlap);
+ *     every device uploads its channel slice, convolves it with its spectrum rows Kf[g] ([h1 - h0][N] on that
+ *     device) and downloads its slice of y_host, all devices concurrently, each through a host pipe of its own
+ *     (as sffft_pipe_create with `chunks`); the call returns when every device has finished, with the first
+ *     error or device-side status (SFFFT_ERR_TIMEOUT) of any shard. */
+int sffft_conv_multi(const sffft_plan_t* plans, int G, const void* const* u, const void* const* Kf, void* const* y,
+                     int B, int H, void* const* streams);
+typedef struct sffft_multi* sffft_multi_t;
+int sffft_multi_pipe_create(sffft_multi_t* multi, const sffft_plan_t* plans, int G, int B, int H, int chunks);
+int sffft_conv_host_multi(sffft_multi_t multi, const void* u_host, const void* const* Kf, void* y_host);
+int sffft_multi_pipe_destroy(sffft_multi_t multi);
+
 /* Debug: a kernel waits on a barrier that nothing arrives at, using the same bounded wait as the fused
  * kernel; returns SFFFT_ERR_TIMEOUT after about limit_us microseconds (1..1e6) with the context intact.
  * No reference counterpart (the reference has no device-side timeouts). */

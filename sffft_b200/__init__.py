@@ -77,6 +77,11 @@ def _declare(lib):
         "sffft_pipe_create": (I, [ctypes.POINTER(P), P, I, I, I]),
         "sffft_conv_host": (I, [P, V, V, V, V]),
         "sffft_pipe_destroy": (I, [P]),
+        "sffft_conv_multi": (I, [ctypes.POINTER(P), I, ctypes.POINTER(V), ctypes.POINTER(V), ctypes.POINTER(V), I, I,
+                                 ctypes.POINTER(V)]),
+        "sffft_multi_pipe_create": (I, [ctypes.POINTER(P), ctypes.POINTER(P), I, I, I, I]),
+        "sffft_conv_host_multi": (I, [P, V, ctypes.POINTER(V), V]),
+        "sffft_multi_pipe_destroy": (I, [P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -301,6 +306,53 @@ class HostPipe:
     def close(self):
         if self._h:
             lib().sffft_pipe_destroy(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def _ptr_array(items):
+    arr = (ctypes.c_void_p * len(items))()
+    for i, x in enumerate(items):
+        arr[i] = _ptr(x)
+    return arr
+
+
+def conv_multi(plans: Sequence["Plan"], us, Kfs, ys, B: int, H: int, streams=None):
+    """Channel-sharded convolution of device-resident shards (sffft_conv_multi): shard g = channels
+    shard_range(H, len(plans), g) on plans[g]'s device, u[g]/y[g] [B][h1-h0][L], Kf[g] [h1-h0][N]."""
+    G = len(plans)
+    hs = (ctypes.c_void_p * G)(*[p._h.value for p in plans])
+    st = _ptr_array([_stream(s) for s in streams]) if streams is not None else None
+    _check(lib().sffft_conv_multi(hs, G, _ptr_array(us), _ptr_array(Kfs), _ptr_array(ys), B, H, st), "conv_multi")
+    return ys
+
+
+class HostPipeMulti:
+    """One [B][H][L] host batch convolved by several devices (sffft_multi_pipe_create / sffft_conv_host_multi):
+    device g takes channels shard_range(H, len(plans), g) through a host pipe of its own; conv() returns when
+    every device is done."""
+
+    def __init__(self, plans: Sequence["Plan"], B: int, H: int, chunks: int = 0):
+        self._h = ctypes.c_void_p()
+        G = len(plans)
+        hs = (ctypes.c_void_p * G)(*[p._h.value for p in plans])
+        _check(lib().sffft_multi_pipe_create(ctypes.byref(self._h), hs, G, B, H, chunks), "multi_pipe_create")
+        self.plans, self.B, self.H = list(plans), B, H
+
+    def conv(self, u_host, Kfs, y_host):
+        if tuple(u_host.shape) != (self.B, self.H, self.plans[0].L) or tuple(y_host.shape) != tuple(u_host.shape):
+            raise ValueError("u_host / y_host must be [B][H][L] of the pipe's batch")
+        _check(lib().sffft_conv_host_multi(self._h, _ptr(u_host), _ptr_array(Kfs), _ptr(y_host)), "conv_host_multi")
+        return y_host
+
+    def close(self):
+        if self._h:
+            lib().sffft_multi_pipe_destroy(self._h)
             self._h = ctypes.c_void_p()
 
     def __del__(self):

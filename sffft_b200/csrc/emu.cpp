@@ -135,9 +135,12 @@ struct HostOps {
   void store1(uint16_t* p, float v) { *p = (uint16_t)bf16_from_float(v); }
   void store4(float* p, const float* v) { for (int i = 0; i < 4; i++) p[i] = v[i]; }
   void store4(uint16_t* p, const float* v) { for (int i = 0; i < 4; i++) p[i] = (uint16_t)bf16_from_float(v[i]); }
-  // energy of one conversion step (the device sums the SEG lanes of a run with shuffles; the emulated
-  // threads run one after another, so they accumulate)
-  void energy_store(float* part, int e, float ss, int seg) { part[e / (8 * seg)] += ss; }
+  // energies of a thread's conversion steps (the device sums the SEG lanes of a run with shuffles; the
+  // emulated threads run one after another, so they accumulate)
+  template <int NSTEP, int SEG>
+  void energy_store(float* part, const float (&ss)[NSTEP], int tid, int stride) {
+    for (int i = 0; i < NSTEP; i++) part[(tid * 8 + i * stride) / (8 * SEG)] += ss[i];
+  }
   void st4(uint32_t off, float v) {
     if ((off & 3) || (size_t)off + 4 > data_bytes) throw std::out_of_range("staged output outside the data buffer");
     std::memcpy(smem->data() + base + off, &v, 4);
@@ -229,10 +232,10 @@ int run_plan(const void* u, const float* Kf, void* y, int B, int H) {
     // the two conversion passes of the kernel: energies, then (where a pair needs it) scaled input
     std::vector<float> part(Energy<P>::SLOTS, 0.f), psc(2 * P::G), osc(2 * P::G);
     for (int tid = 0; tid < SH::TWARPS * 32; tid++)
-      convert_group<P, TIO, SH::NB>(ops, uu, gp, tid, SH::TWARPS * 32, part.data(), nullptr);
+      convert_group<P, TIO, SH::NB, SH::TWARPS * 32>(ops, uu, gp, tid, part.data(), nullptr);
     if (pair_scales<P>(part.data(), psc.data(), osc.data()))
       for (int tid = 0; tid < SH::TWARPS * 32; tid++)
-        convert_group<P, TIO, SH::NB>(ops, uu, gp, tid, SH::TWARPS * 32, nullptr, psc.data());
+        convert_group<P, TIO, SH::NB, SH::TWARPS * 32>(ops, uu, gp, tid, nullptr, psc.data());
     EpiArgs ea{(uint32_t)(slot * P::TMEM_COLS), Kf, y, B, H, group, nullptr, 0, osc.data()};
     // the loader warp's staging of the group's spectrum rows (same swizzle as the device)
     if constexpr (SH::KSLOT > 0) {

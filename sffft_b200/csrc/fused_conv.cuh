@@ -116,13 +116,35 @@ struct DevOps {
     __nv_bfloat162 a = __floats2bfloat162_rn(v[0], v[1]), b = __floats2bfloat162_rn(v[2], v[3]);
     __stcs(reinterpret_cast<uint2*>(p), make_uint2(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&b)));
   }
-  // Energy of one conversion step: the sum of squares of the 8 values of each of the SEG lanes that share
-  // a run of one sequence, stored by the run's first lane (the steps of a warp are warp-uniform).
-  __device__ __forceinline__ void energy_store(float* part, int e, float ss, int seg) {
+  // Energies of a thread's NSTEP conversion steps (step i covers elements tid * 8 + i * stride .. + 7): the
+  // SEG lanes of a warp that share a run of one sequence are summed per step with a butterfly that halves the
+  // values a lane carries at each exchange (NSTEP / 2 + NSTEP / 4 + ... shuffles instead of NSTEP per level),
+  // after which lane l holds the total of one step and the run's leader lanes store them.
+  template <int NSTEP, int SEG>
+  __device__ __forceinline__ void energy_store(float* part, const float (&ss)[NSTEP], int tid, int stride) {
+    const int lane = tid & 31;
+    float v[NSTEP];
 #pragma unroll
-    for (int m = 16; m > 0; m >>= 1)
-      if (m < seg) ss += __shfl_xor_sync(0xffffffffu, ss, m);
-    if ((threadIdx.x & (seg - 1)) == 0) part[e / (8 * seg)] = ss;
+    for (int i = 0; i < NSTEP; i++) v[i] = ss[i];
+    int idx = 0;
+#pragma unroll
+    for (int lvl = 0, m = SEG / 2; m >= 1; lvl++, m >>= 1) {
+      const int n = NSTEP >> lvl;
+      const bool up = (lane & m) != 0;
+      if (n > 1) {
+#pragma unroll
+        for (int j = 0; j < n / 2; j++) {
+          const float send = up ? v[j] : v[j + n / 2], keep = up ? v[j + n / 2] : v[j];
+          v[j] = keep + __shfl_xor_sync(0xffffffffu, send, m);
+        }
+        if (up) idx += n / 2;
+      } else {
+        v[0] += __shfl_xor_sync(0xffffffffu, v[0], m);
+      }
+    }
+    constexpr int REST = SEG / NSTEP;   // lanes that end up holding the same total
+    if ((lane & (REST - 1)) == 0)
+      part[((tid & ~(SEG - 1)) * 8 + idx * stride) / (8 * SEG)] = v[0];
   }
   __device__ __forceinline__ void st4(uint32_t off, float v) { *reinterpret_cast<float*>(sm + off) = v; }
   __device__ __forceinline__ void ld4_staged(uint32_t off, uint32_t rot, float* v) {
@@ -332,28 +354,39 @@ __device__ __forceinline__ bool team_sync(uint64_t* bar, uint32_t& phase, int la
   return ok;
 }
 
-// The conversion task of a group (a team's first task): the energy pass, a team barrier, the pair scales
-// (computed by lane 0 of every warp, which all write the same values and are read by their own warp) and, for
-// a group with a pair to rescale, the scaled pass -- the same code run a second time, so that the rare pass
-// adds no registers to the kernel's allocation.  Returns false when the team barrier gave up.
-template <class P, class TIO, int NB>
-__device__ __forceinline__ bool convert_task(DevOps& ops, const TIO* u, const GroupPairs& gp, int tid, int nthreads,
-                                             float* en, uint64_t* team_bar, uint32_t& team_phase,
-                                             volatile int* abort_flag) {
-  constexpr int ENS = Energy<P>::SLOTS;
-  const int lane = tid & 31;
-#pragma unroll 1
-  for (int pass = 0; pass < 2; pass++) {
-    convert_group<P, TIO, NB>(ops, u, gp, tid, nthreads, pass == 0 ? en : nullptr, en + ENS);
-    if (pass == 1) break;
-    if (!team_sync(team_bar, team_phase, lane, abort_flag)) return false;
-    int redo = 0;
-    if (lane == 0) redo = pair_scales<P>(en, en + ENS, en + ENS + 2 * P::G) ? 1 : 0;
-    redo = __shfl_sync(0xffffffffu, redo, 0);
-    __syncwarp();   // orders lane 0's stores before the other lanes' reads of the scales
-    if (!redo) break;
+// The second conversion pass of a group with a row to rescale (rare), out of line so that it adds nothing to
+// the register allocation of the kernel's main loop.
+template <class P, class TIO, int NB, int NT>
+__device__ __noinline__ void convert_scaled(DevOps ops, const TIO* u, GroupPairs gp, int tid, const float* psc) {
+  convert_group<P, TIO, NB, NT>(ops, u, gp, tid, nullptr, psc);
+}
+
+// Scales of a group's 2G rows (pair_scales, computed in parallel): the energy slots of row j are summed by
+// the 32 / 2G lanes j * 32 / 2G.., every lane gets its partner row's energy by a shuffle and derives its row's
+// exponent; one lane per row writes the row's input and output scales to en[ENS + j] and en[ENS + 2G + j].
+// Every warp of the team computes and writes the same values and reads only its own.  Returns whether any
+// row of the group is scaled.
+template <class P>
+__device__ __forceinline__ bool group_scales(float* en, int lane) {
+  constexpr int NSQ = 2 * P::G, LPS = 32 / NSQ, SPS = Energy<P>::SPS, ENS = Energy<P>::SLOTS;
+  static_assert(NSQ <= 32 && 32 % NSQ == 0, "rows per group");
+  const int j = lane / LPS, r = lane - j * LPS;
+  float e = 0.f;
+  for (int i = r; i < SPS; i += LPS) e += en[j * SPS + i];
+#pragma unroll
+  for (int m = LPS / 2; m >= 1; m >>= 1) e += __shfl_xor_sync(0xffffffffu, e, m);
+  const float ep = __shfl_sync(0xffffffffu, e, ((j ^ 1) * LPS + r) & 31);
+  int f0, f1;
+  if (j & 1) pair_exponents(ep, e, P::L, &f0, &f1);
+  else pair_exponents(e, ep, P::L, &f0, &f1);
+  const int f = (j & 1) ? f1 : f0;
+  if (r == 0) {
+    en[ENS + j] = ldexpf(1.f, f);
+    en[ENS + NSQ + j] = e == 0.f ? 0.f : ldexpf(1.f, -f);
   }
-  return true;
+  const bool any = __any_sync(0xffffffffu, f != 0) != 0;
+  __syncwarp();   // orders the stores before this warp's later reads of the scales
+  return any;
 }
 
 template <class P, class TIO, bool ACC16>
@@ -374,6 +407,7 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
   uint64_t* team_done = k_empty + 5;           // [NTEAM] a team's warps staged their outputs / copied them out
   volatile int* kstamp = reinterpret_cast<volatile int*>(team_done + SH::NTEAM);   // [2] group being staged
   volatile int* conv_done = kstamp + 2;        // groups whose input has been converted
+  volatile int* rep = conv_done + 1;           // [NS] the next stage request of a slot repeats the last stage
   uint8_t* kstage = sm + SH::K_OFF;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -387,6 +421,7 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
     for (int t = 0; t < SH::NTEAM; t++) mbar_init(team_done + t, SH::TWARPS);
     kstamp[0] = kstamp[1] = -1;
     *conv_done = 0;
+    for (int q = 0; q < NS; q++) rep[q] = 0;
     *abort_flag = 0;
     s_wait_ns = prm.wait_ns ? prm.wait_ns : kWaitLimitNs;
     fence_mbar_init();
@@ -443,12 +478,13 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
     // scans the slots and issues the next stage of any slot whose operand is ready.
     if (lane == 0) {
       DevOps ops{sm, ACC16, nullptr, nullptr, P::N};
-      int done[NS], total[NS];
+      int done[NS], total[NS], ncommit[NS];
       uint32_t ar_bits = 0;
       int left = 0;
 #pragma unroll
       for (int s = 0; s < NS; s++) {
         done[s] = 0;
+        ncommit[s] = 0;
         total[s] = (s < ni ? (ni - s + NS - 1) / NS : 0) * S2;
         left += total[s];
       }
@@ -464,13 +500,20 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
             ar_bits ^= 1u << s;
             tc_fence_after();
             SFFFT_STAMP(1, 3 * nmma + 1);
-            issue_any<P, ACC16, sizeof(TIO) == 4>(done[s] % S2, ops, tmem + (uint32_t)(s * P::TMEM_COLS),
+            // a team that rescaled its group's input asks for stage 0 again (rep, set before its arrival)
+            const bool again = rep[s] != 0;
+            if (again) rep[s] = 0;
+            issue_any<P, ACC16, sizeof(TIO) == 4>((again ? done[s] - 1 : done[s]) % S2, ops,
+                                tmem + (uint32_t)(s * P::TMEM_COLS),
                                 smem_u32(sm + SH::DATA_OFF + s * P::DATA_BYTES), smem_u32(bmat));
             mma_commit(mma_done + s);
             SFFFT_STAMP(1, 3 * nmma + 2);
             nmma++;
-            done[s]++;
-            left--;
+            ncommit[s]++;
+            if (!again) {
+              done[s]++;
+              left--;
+            }
             progressed = true;
           }
         }
@@ -486,9 +529,9 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
       // make sure no MMA is still writing TMEM when the CTA frees it
 #pragma unroll
       for (int s = 0; s < NS; s++) {
-        if (!done[s]) continue;
+        if (!ncommit[s]) continue;
         const uint64_t t0 = global_ns();
-        while (!mbar_try_wait(mma_done + s, (uint32_t)((done[s] - 1) & 1)) && global_ns() - t0 < s_wait_ns) {
+        while (!mbar_try_wait(mma_done + s, (uint32_t)((ncommit[s] - 1) & 1)) && global_ns() - t0 < s_wait_ns) {
         }
       }
     }
@@ -577,19 +620,28 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
         DevOps ops{sm + SH::DATA_OFF + s * P::DATA_BYTES, ACC16, tw_lo, tw_hi, P::N};
         if (lane == 0 && wt == 0) SFFFT_STAMP(2 + team, 3 * ntask);
         if (j == 0) {
-          // first pass: convert unscaled and measure each sequence's energy; once the team's energies are
-          // in, every thread derives the same pair scales, and a group with a pair to rescale is converted
-          // again with them (pair_scales)
+          // convert the group's input (measuring each row's energy) and hand it to the MMA warp at once; the
+          // team then agrees on the rows' scales while the stage-0 MMAs run.  A group with a row to rescale
+          // (rare: rows 2x apart in energy, or tiny) waits for those MMAs, converts again with the scales and
+          // asks the MMA warp to repeat stage 0 (pair_scales).
           float* en = energies + (s * 2 + ((gi / NS) & 1)) * SH::EN_STRIDE;
-          if (!convert_task<P, TIO, SH::NB>(ops, u, gp, ttid, TWT, en, team_done + team, ts_phase, abort_flag)) {
-            ok = false;
-            break;
-          }
+          convert_group<P, TIO, SH::NB, TWT>(ops, u, gp, ttid, en, en + ENS);
           if (lane == 0 && wt == 0) SFFFT_STAMP(2 + team, 3 * ntask + 1);
           fence_async_smem();
           tc_fence_before();
           if (!(prm.debug_skip_arrive == group + 1 && wt == 0)) warp_arrive(a_ready + s, lane);
           if (lane == 0 && wt == 0) atomicAdd((int*)conv_done, 1);
+          if (!team_sync(team_done + team, ts_phase, lane, abort_flag)) { ok = false; break; }
+          if (group_scales<P>(en, lane)) {
+            if (!wait_phase_all(mma_done + s, (md_bits >> l) & 1u, abort_flag)) { ok = false; break; }
+            md_bits ^= 1u << l;
+            tc_fence_after();
+            if (lane == 0 && wt == 0) rep[s] = 1;
+            convert_scaled<P, TIO, SH::NB, TWT>(ops, u, gp, ttid, en + ENS);
+            fence_async_smem();
+            tc_fence_before();
+            warp_arrive(a_ready + s, lane);
+          }
           if (lane == 0 && wt == 0) SFFFT_STAMP(2 + team, 3 * ntask + 2);
         } else {
           const int sid = j - 1;
@@ -631,10 +683,11 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
     }
   }
 
-  if (tid == 0 && *abort_flag) atomicExch(prm.status, SFFFT_ERR_TIMEOUT);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  // after the block barrier every role has finished, so an abort raised by any of them is seen here
+  if (tid == 0 && *abort_flag) atomicExch(prm.status, SFFFT_ERR_TIMEOUT);
   if (warp == 1) tmem_dealloc(tmem, SH::TMEM_ALLOC);
 }
 

@@ -2,7 +2,8 @@
 //
 // The batch is cut into chunks of whole batch-row pairs (u[b0:b1] is contiguous in [B][H][L], so a chunk
 // moves with one 1-D copy each way); only when there are fewer pair rows than chunks are the rows also cut
-// into channel ranges (one 1-D copy per batch row each way: a row's channel range is contiguous).  Each
+// into channel ranges (one pitched copy each way: a row's channel range is contiguous).  A pipe may also
+// cover a channel slice of larger host arrays (sffft_pipe_create_slice, used by the multi-device pipe).  Each
 // stage has a stream of its own -- uploads into device staging, sffft_conv with the chunk's spectrum rows,
 // downloads into y -- and chunk c uses staging slot c % 3, handed from stage to stage by events: the
 // upload of chunk c waits until the slot's previous kernel has read its input, and the kernel waits until
@@ -28,6 +29,7 @@ enum { kUp = 0, kConv = 1, kDown = 2 };   // stage streams
 struct sffft_pipe {
   sffft_plan_t plan;
   int B, H, L, N, sio, nb, hc, device;   // chunk: nb batch rows (even) x hc channels
+  int hp;                    // channels per batch row of the host arrays (H, or more for a channel slice)
   void* u_stage[kStreams];   // device staging [nb][hc][L] per slot
   void* y_stage[kStreams];
   cudaStream_t s[kStreams];  // one per stage
@@ -49,8 +51,10 @@ static void pipe_free(sffft_pipe* q) {
   delete q;
 }
 
-extern "C" int sffft_pipe_create(sffft_pipe_t* pipe, sffft_plan_t plan, int B, int H, int chunks) {
-  if (!pipe || !plan || B < 1 || H < 1 || chunks < 0) return SFFFT_ERR_INVALID_ARGUMENT;
+// A pipe over channels [h0, h0 + H) of host arrays with hp channels per batch row (the caller offsets the
+// host pointers by h0 rows of L); sffft_pipe_create is the whole-array case hp = H.
+int sffft_pipe_create_slice(sffft_pipe_t* pipe, sffft_plan_t plan, int B, int H, int hp, int chunks) {
+  if (!pipe || !plan || B < 1 || H < 1 || hp < H || chunks < 0) return SFFFT_ERR_INVALID_ARGUMENT;
   *pipe = nullptr;
   sffft_plan_info_t info;
   int rc = sffft_plan_info(plan, &info);
@@ -65,7 +69,7 @@ extern "C" int sffft_pipe_create(sffft_pipe_t* pipe, sffft_plan_t plan, int B, i
   if (cudaSetDevice(info.device) != cudaSuccess) return SFFFT_ERR_CUDA;
   sffft_pipe* q = new (std::nothrow) sffft_pipe();
   if (!q) return SFFFT_ERR_INVALID_ARGUMENT;
-  q->plan = plan; q->B = B; q->H = H; q->L = info.L; q->N = info.N; q->device = info.device;
+  q->plan = plan; q->B = B; q->H = H; q->hp = hp; q->L = info.L; q->N = info.N; q->device = info.device;
   q->sio = info.io == SFFFT_IO_BF16 ? 2 : 4;
   if (chunks <= prow) {
     q->nb = 2 * ((prow + chunks - 1) / chunks);
@@ -95,6 +99,10 @@ extern "C" int sffft_pipe_create(sffft_pipe_t* pipe, sffft_plan_t plan, int B, i
   return SFFFT_OK;
 }
 
+extern "C" int sffft_pipe_create(sffft_pipe_t* pipe, sffft_plan_t plan, int B, int H, int chunks) {
+  return sffft_pipe_create_slice(pipe, plan, B, H, H, chunks);
+}
+
 extern "C" int sffft_conv_host(sffft_pipe_t q, const void* u_host, const void* Kf, void* y_host, void* stream) {
   if (!q || !u_host || !Kf || !y_host) return SFFFT_ERR_INVALID_ARGUMENT;
   int prev = 0;
@@ -104,7 +112,7 @@ extern "C" int sffft_conv_host(sffft_pipe_t q, const void* u_host, const void* K
   int rc = SFFFT_OK;
   cudaError_t ce = cudaEventRecord(q->start, user);
   for (int i = 0; i < kStreams && ce == cudaSuccess; i++) ce = cudaStreamWaitEvent(q->s[i], q->start, 0);
-  const size_t row = (size_t)q->H * q->L * q->sio;   // host pitch between batch rows
+  const size_t row = (size_t)q->hp * q->L * q->sio;   // host pitch between batch rows
   const cudaStream_t su = q->s[kUp], sk = q->s[kConv], sd = q->s[kDown];
   int c = 0;
   for (int b0 = 0; b0 < q->B && ce == cudaSuccess && rc == SFFFT_OK; b0 += q->nb) {
@@ -117,12 +125,12 @@ extern "C" int sffft_conv_host(sffft_pipe_t q, const void* u_host, const void* K
       // upload: the slot's input is free once the slot's previous kernel (chunk c - 3, or the previous
       // call's) has run; an event never recorded is complete
       ce = cudaStreamWaitEvent(su, q->conv[k], 0);
-      // a chunk of whole rows is one contiguous copy; a channel range is one contiguous copy per batch row
-      if (ce == cudaSuccess && hn == q->H) {
+      // a chunk of whole rows is one contiguous copy; a channel range is one pitched copy (a contiguous run
+      // per batch row)
+      if (ce == cudaSuccess && width == row) {
         ce = cudaMemcpyAsync(q->u_stage[k], src, width * bn, cudaMemcpyHostToDevice, su);
-      } else {
-        for (int r = 0; r < bn && ce == cudaSuccess; r++)
-          ce = cudaMemcpyAsync((char*)q->u_stage[k] + r * width, src + r * row, width, cudaMemcpyHostToDevice, su);
+      } else if (ce == cudaSuccess) {
+        ce = cudaMemcpy2DAsync(q->u_stage[k], width, src, row, width, bn, cudaMemcpyHostToDevice, su);
       }
       if (ce == cudaSuccess) ce = cudaEventRecord(q->up[k], su);
       // kernel: after the upload, and once the slot's previous download has emptied its output
@@ -134,11 +142,10 @@ extern "C" int sffft_conv_host(sffft_pipe_t q, const void* u_host, const void* K
       ce = cudaEventRecord(q->conv[k], sk);
       // download after the kernel
       if (ce == cudaSuccess) ce = cudaStreamWaitEvent(sd, q->conv[k], 0);
-      if (ce == cudaSuccess && hn == q->H) {
+      if (ce == cudaSuccess && width == row) {
         ce = cudaMemcpyAsync(dst, q->y_stage[k], width * bn, cudaMemcpyDeviceToHost, sd);
-      } else {
-        for (int r = 0; r < bn && ce == cudaSuccess; r++)
-          ce = cudaMemcpyAsync(dst + r * row, (char*)q->y_stage[k] + r * width, width, cudaMemcpyDeviceToHost, sd);
+      } else if (ce == cudaSuccess) {
+        ce = cudaMemcpy2DAsync(dst, row, q->y_stage[k], width, width, bn, cudaMemcpyDeviceToHost, sd);
       }
       if (ce == cudaSuccess) ce = cudaEventRecord(q->down[k], sd);
     }

@@ -90,7 +90,8 @@ SF_HD PairInfo pair_info(int cta, int g, int G, int B, int H, int L) {
 // A group is converted in one or two passes (see pair_scales below):
 //   part != null  first pass: unscaled conversion that also records each sequence's energy: for every run
 //                 of 8 * SEG consecutive elements of one sequence (one step of SEG lanes of a warp) the sum
-//                 of squares, in part[e / (8 * SEG)] (e = element index within the group)
+//                 of squares, in part[e / (8 * SEG)] (e = element index within the group); the NSTEP steps
+//                 of a thread are NT * 8 elements apart
 //   part == null  second pass (only for groups that have a pair to rescale): every value of sequence j is
 //                 multiplied by the power of two psc[j] before the fp16 split.
 // ---------------------------------------------------------------------------------------------
@@ -101,39 +102,35 @@ struct Energy {
   static constexpr int SLOTS = 2 * P::G * SPS;
 };
 
-template <class P, class TIO, int NB, class Ops>
-SF_HD void convert_group(Ops& ops, const TIO* u, const GroupPairs& gp, int tid, int nthreads, float* part,
-                         const float* psc) {
-  constexpr int V0 = P::N / P::R0, MB0 = P::MB(0), NE = 2 * P::G * P::L;
-  const int stride = nthreads * 8;
+template <class P, class TIO, int NB, int NT, class Ops>
+SF_HD void convert_group(Ops& ops, const TIO* u, const GroupPairs& gp, int tid, float* part, const float* psc) {
+  constexpr int V0 = P::N / P::R0, MB0 = P::MB(0), NE = 2 * P::G * P::L, STRIDE = NT * 8, NSTEP = NE / STRIDE;
+  static_assert(NE % STRIDE == 0 && NSTEP <= Energy<P>::SEG, "conversion steps");
   uint32_t w[NB][8];
-  int mrow[NB], krow[NB], eb[NB];
-  auto issue = [&](int b, int e) {
-    krow[b] = -1;
-    eb[b] = e;
-    if (e < NE) {
-      const int j = e / P::L, n = e - j * P::L, g = j >> 1, plane = j & 1;
-      const PairInfo pi = gp.get(g, P::L);
-      const long long off = plane == 0 ? pi.off0 : pi.off1;
-      const int n0 = n / V0, vv = n - n0 * V0;
-      mrow[b] = g * V0 + vv;
-      krow[b] = plane * P::R0 + n0;
-      if (off >= 0) ops.ldraw(u + off + n, w[b]);
-      else {
-        for (int q = 0; q < 8; q++) w[b][q] = 0u;   // zero bits read as 0.0 in both formats
-      }
+  int mrow[NB], krow[NB];
+  float ss[NSTEP];
+  // step i: elements tid * 8 + i * STRIDE .. + 7 (all steps lie below NE: tid * 8 < STRIDE)
+  auto issue = [&](int b, int i) {
+    const int e = tid * 8 + i * STRIDE;
+    const int j = e / P::L, n = e - j * P::L, g = j >> 1, plane = j & 1;
+    const PairInfo pi = gp.get(g, P::L);
+    const long long off = plane == 0 ? pi.off0 : pi.off1;
+    const int n0 = n / V0, vv = n - n0 * V0;
+    mrow[b] = g * V0 + vv;
+    krow[b] = plane * P::R0 + n0;
+    if (off >= 0) ops.ldraw(u + off + n, w[b]);
+    else {
+      for (int q = 0; q < 8; q++) w[b][q] = 0u;   // zero bits read as 0.0 in both formats
     }
   };
-  auto finish = [&](int b) {
-    if (krow[b] < 0) return;   // uniform across a warp: its 256 elements lie all below or all above NE
+  auto finish = [&](int b, int i) -> float {
     float v[8];
     ops.unpack(u, w[b], v);
+    float e2 = 0.f;
     if (part) {
-      float ss = 0.f;
-      for (int q = 0; q < 8; q++) ss += v[q] * v[q];
-      ops.energy_store(part, eb[b], ss, Energy<P>::SEG);
+      for (int q = 0; q < 8; q++) e2 += v[q] * v[q];
     } else {
-      const float s = psc[eb[b] / P::L];
+      const float s = psc[(tid * 8 + i * STRIDE) / P::L];
       for (int q = 0; q < 8; q++) v[q] *= s;
     }
     uint32_t hi[4], lo[4];
@@ -148,16 +145,18 @@ SF_HD void convert_group(Ops& ops, const TIO* u, const GroupPairs& gp, int tid, 
     } else if constexpr (P::R0 == 16) {
       ops.st16(off_lo, 0u, 0u, 0u, 0u);   // bf16 converts exactly: its lo plane is zero
     }
+    return e2;
   };
 #pragma unroll
-  for (int b = 0; b < NB; b++) issue(b, tid * 8 + b * stride);
-  for (int e0 = tid * 8; e0 < NE; e0 += NB * stride) {
+  for (int b = 0; b < NB; b++)
+    if (b < NSTEP) issue(b, b);
 #pragma unroll
-    for (int b = 0; b < NB; b++) {
-      finish(b);
-      issue(b, e0 + (b + NB) * stride);
-    }
+  for (int i = 0; i < NSTEP; i++) {
+    ss[i] = finish(i % NB, i);
+    if (i + NB < NSTEP) issue(i % NB, i + NB);
   }
+  // the step energies of the SEG lanes that share a run of one sequence, summed once after the loads
+  if (part) ops.template energy_store<NSTEP, Energy<P>::SEG>(part, ss, tid, STRIDE);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -184,6 +183,25 @@ SF_HD int round_half_log2(float r) {   // round(log2(r) / 2), |result| <= 100
   return (int)(f < 0.f ? f - 0.5f : f + 0.5f);
 }
 
+// Exponents f0, f1 of the powers of two that scale a pair's two rows, from their energies E0, E1 (sums of
+// squares over L values each).
+SF_HD void pair_exponents(float E0, float E1, int L, int* f0, int* f1) {
+  int f[2] = {0, 0};
+  if (E0 <= 3.0e38f && E1 <= 3.0e38f) {   // false for inf and NaN: such pairs stay unscaled
+    const float Eb = E0 > E1 ? E0 : E1;
+    if (Eb > 0.f && Eb < (float)L * (1.f / 4096.f)) f[0] = f[1] = round_half_log2((float)L / Eb);
+    if (E0 > 0.f && E1 > 0.f) {
+      const float r = E0 / E1;
+      if (r >= 2.f) f[1] += round_half_log2(r);
+      else if (r <= 0.5f) f[0] += round_half_log2(1.f / r);
+    }
+  }
+  *f0 = f[0] > 120 ? 120 : f[0];
+  *f1 = f[1] > 120 ? 120 : f[1];
+}
+
+// Scales of a group's 2G rows from the energy slots of its conversion: psc (input) and osc (output; 0 for an
+// all-zero row).  Returns whether any row is scaled.  (The kernel computes the same per lane in parallel.)
 template <class P>
 SF_HD bool pair_scales(const float* part, float* psc, float* osc) {
   using EN = Energy<P>;
@@ -195,22 +213,12 @@ SF_HD bool pair_scales(const float* part, float* psc, float* osc) {
       for (int i = 0; i < EN::SPS; i++) s += part[(2 * g + p) * EN::SPS + i];
       E[p] = s;
     }
-    int f[2] = {0, 0};
-    const bool finite = E[0] <= 3.0e38f && E[1] <= 3.0e38f;   // false for inf and NaN
-    if (finite) {
-      const float Eb = E[0] > E[1] ? E[0] : E[1];
-      if (Eb > 0.f && Eb < (float)P::L * (1.f / 4096.f)) f[0] = f[1] = round_half_log2((float)P::L / Eb);
-      if (E[0] > 0.f && E[1] > 0.f) {
-        const float r = E[0] / E[1];
-        if (r >= 2.f) f[1] += round_half_log2(r);
-        else if (r <= 0.5f) f[0] += round_half_log2(1.f / r);
-      }
-    }
+    int f[2];
+    pair_exponents(E[0], E[1], P::L, &f[0], &f[1]);
     for (int p = 0; p < 2; p++) {
-      const int e = f[p] > 120 ? 120 : f[p];
-      psc[2 * g + p] = ldexpf(1.f, e);
-      osc[2 * g + p] = E[p] == 0.f ? 0.f : ldexpf(1.f, -e);
-      redo = redo || e != 0;
+      psc[2 * g + p] = ldexpf(1.f, f[p]);
+      osc[2 * g + p] = E[p] == 0.f ? 0.f : ldexpf(1.f, -f[p]);
+      redo = redo || f[p] != 0;
     }
   }
   return redo;
