@@ -315,7 +315,7 @@ def cufft_ms(torch, sf, dev, wl, steps, warmup):
 
 def run_sweep(torch, sf, dev, local, steps, warmup):
     points = [(8, 768, L, io, "fp32") for io in ("fp32", "bf16") for L in (128, 256, 512, 1024, 2048, 4096, 8192)]
-    points += SWEEP_EXTRA
+    points += [c for c in SWEEP_EXTRA if c not in points]
     out = []
     for B, H, L, io, acc in points:
         decay, sqrt_norm = (8.0, True) if L == 16384 else (4.0, True)

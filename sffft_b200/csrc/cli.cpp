@@ -1,13 +1,18 @@
 // sffft: calibration / benchmark CLI over the C ABI (include/sffft.h).
 //
-// Drop-in for the reference program's command line and output (sfFFT src/sffft.cu:423-515):
+// Command-line contract of the reference program (sfFFT src/sffft.cu:423-515), kept so that its scripts and
+// tests/precision_smoke.sh drive this binary unchanged:
 //   sffft [B H [L]] [--max-error REL_L2] [--io fp32|bf16|any] [--seed N] [--input-scale S]
 //         [--allocator device|managed|mapped|hybrid] [--kernel legacy|cached|auto] [--memory-info]
-// Same argument rules and exit codes (0 ok, 1 invalid arguments, 2 no candidate met --max-error), the
-// same "# ..." header lines and RESULT / SELECT / NO_MATCH / MEMORY rows, the same calibration inputs
-// (seeded generator) and error definition (relative L2 against the cuFFT fp32 pipeline over every output
-// element; cuFFT itself against an fp64 direct convolution of three sampled sequences).  L may also be
-// 16384 when requested explicitly; the all-lengths sweep stays 128..8192.
+// exit codes 0 (ok), 1 (invalid arguments), 2 (a length had no candidate within --max-error); the "# ..."
+// header lines and the RESULT / SELECT / NO_MATCH / MEMORY rows; the seeded calibration inputs; errors as the
+// relative L2 against the cuFFT fp32 pipeline over every output (cuFFT itself against an fp64 direct
+// convolution of three sampled sequences); timing as the mean of clamp(20000 / L, 10, 200) back-to-back calls
+// after three warm-ups.  L may also be 16384 when requested; the all-lengths sweep stays 128..8192.
+//
+// Structure (this program's own): a declarative option table; an Arena that places every buffer by its
+// role under the allocation mode and keeps the MEMORY row's accounts; a Calibration per length that owns the
+// inputs, the cuFFT reference output and the candidate list and prints its rows.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -18,6 +23,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <functional>
 #include <limits>
 #include <string>
 #include <vector>
@@ -27,292 +33,56 @@
 
 namespace {
 
-#define CK(x)                                                                                       \
-  do {                                                                                              \
-    cudaError_t e_ = (x);                                                                           \
-    if (e_ != cudaSuccess) {                                                                        \
-      std::printf("CUDA error %s at %s:%d: %s\n", #x, __FILE__, __LINE__, cudaGetErrorString(e_)); \
-      std::exit(1);                                                                                 \
-    }                                                                                               \
-  } while (0)
-#define SK(x)                                                                                            \
-  do {                                                                                                   \
-    int s_ = (x);                                                                                        \
-    if (s_ != SFFFT_OK) {                                                                                \
-      std::printf("sffft error %s at %s:%d: %s\n", #x, __FILE__, __LINE__, sffft_status_string(s_));     \
-      std::exit(1);                                                                                      \
-    }                                                                                                    \
-  } while (0)
-
-enum class Alloc { Device, Managed, Mapped, Hybrid };
-const char* alloc_name(Alloc a) {
-  return a == Alloc::Device ? "device" : a == Alloc::Managed ? "managed" : a == Alloc::Mapped ? "mapped" : "hybrid";
+[[noreturn]] void die(const char* what, const char* detail) {
+  std::printf("error: %s: %s\n", what, detail);
+  std::exit(1);
 }
+void cuda_ok(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) die(what, cudaGetErrorString(e));
+}
+void sffft_ok(int s, const char* what) {
+  if (s != SFFFT_OK) die(what, sffft_status_string(s));
+}
+
 using Clock = std::chrono::steady_clock;
-double since_ms(Clock::time_point t) { return std::chrono::duration<double, std::milli>(Clock::now() - t).count(); }
+double ms_since(Clock::time_point t) { return std::chrono::duration<double, std::milli>(Clock::now() - t).count(); }
 
-// Owned buffers under one of the four allocation modes; counts bytes, copies and time for MEMORY rows.
-struct Buffers {
-  struct Block { void* dev; void* host; size_t bytes; Alloc kind; };
-  Alloc mode;
-  bool can_prefetch;
-  std::vector<Block> blocks;
-  size_t owned = 0, uploaded = 0, downloaded = 0;
-  double alloc_ms = 0, copy_ms = 0;
-  Buffers(Alloc m, bool pf) : mode(m), can_prefetch(pf) {}
-  Buffers(const Buffers&) = delete;
-  template <class T>
-  T* get(size_t bytes, bool host_visible_io = true) {
-    const Alloc kind = mode == Alloc::Hybrid ? (host_visible_io ? Alloc::Mapped : Alloc::Device) : mode;
-    const auto t0 = Clock::now();
-    void *dev = nullptr, *host = nullptr;
-    if (kind == Alloc::Mapped) {
-      CK(cudaHostAlloc(&host, bytes, cudaHostAllocMapped));
-      CK(cudaHostGetDevicePointer(&dev, host, 0));
-    } else if (kind == Alloc::Managed) {
-      CK(cudaMallocManaged(&dev, bytes));
-      host = dev;
-    } else {
-      CK(cudaMalloc(&dev, bytes));
-    }
-    blocks.push_back({dev, host, bytes, kind});
-    owned += bytes;
-    alloc_ms += since_ms(t0);
-    return static_cast<T*>(dev);
+// ------------------------------------------------------------------------------------------------
+// Options
+// ------------------------------------------------------------------------------------------------
+enum class Mode { Device, Managed, Mapped, Hybrid };
+const char* mode_name(Mode m) {
+  switch (m) {
+    case Mode::Device: return "device";
+    case Mode::Managed: return "managed";
+    case Mode::Mapped: return "mapped";
+    default: return "hybrid";
   }
-  template <class T>
-  T* host_view(const T* dev) const {
-    for (const auto& b : blocks)
-      if (b.dev == dev) return static_cast<T*>(b.host);
-    return nullptr;
-  }
-  void prefetch(const void* p, size_t bytes, bool to_gpu) {
-    if (mode != Alloc::Managed || !can_prefetch) return;
-#if CUDART_VERSION >= 13000
-    cudaMemLocation loc{};
-    loc.type = to_gpu ? cudaMemLocationTypeDevice : cudaMemLocationTypeHost;
-    loc.id = 0;
-    CK(cudaMemPrefetchAsync(p, bytes, loc, 0));
-#else
-    CK(cudaMemPrefetchAsync(p, bytes, to_gpu ? 0 : cudaCpuDeviceId));
-#endif
-  }
-  void to_gpu() {
-    for (const auto& b : blocks) prefetch(b.dev, b.bytes, true);
-  }
-  template <class T>
-  void upload(T* dev, const T* src, size_t n) {
-    T* h = host_view(dev);
-    if (h == src) return;
-    const auto t0 = Clock::now();
-    if (h) std::memcpy(h, src, n * sizeof(T));
-    else {
-      CK(cudaMemcpy(dev, src, n * sizeof(T), cudaMemcpyHostToDevice));
-      uploaded += n * sizeof(T);
-    }
-    copy_ms += since_ms(t0);
-  }
-  template <class T>
-  const T* read(const T* dev, size_t n, std::vector<T>& shadow) {
-    if (T* h = host_view(dev)) {
-      prefetch(dev, n * sizeof(T), false);
-      CK(cudaDeviceSynchronize());
-      return h;
-    }
-    shadow.resize(n);
-    const auto t0 = Clock::now();
-    CK(cudaMemcpy(shadow.data(), dev, n * sizeof(T), cudaMemcpyDeviceToHost));
-    downloaded += n * sizeof(T);
-    copy_ms += since_ms(t0);
-    return shadow.data();
-  }
-  ~Buffers() {
-    for (const auto& b : blocks) {
-      if (b.kind == Alloc::Mapped) cudaFreeHost(b.host);
-      else cudaFree(b.dev);
-    }
-  }
+}
+const char* kernel_name(int k) { return k == 0 ? "legacy" : k == 1 ? "cached" : "auto"; }
+
+struct Options {
+  int B = 8, H = 768, L = 0;   // L = 0: every length 128..8192
+  double max_error = -1, input_scale = 1;
+  const char* io = "fp32";
+  Mode mode = Mode::Device;
+  int kernels = 0;             // 0 legacy, 1 cached, 2 both
+  bool memory_info = false;
+  unsigned long long seed = sffft_cli::Rng().s;
 };
 
-uint16_t to_bf16_bits(float f) {
-  uint32_t x;
-  std::memcpy(&x, &f, 4);
-  if ((x & 0x7FFFFFFFu) > 0x7F800000u) return 0x7FC0u;
-  x += 0x7FFFu + ((x >> 16) & 1u);
-  return (uint16_t)(x >> 16);
-}
-float from_bf16_bits(uint16_t b) {
-  const uint32_t x = (uint32_t)b << 16;
-  float f;
-  std::memcpy(&f, &x, 4);
-  return f;
+bool parse_double(const char* s, double* out) {
+  char* end = nullptr;
+  errno = 0;
+  *out = std::strtod(s, &end);
+  return !errno && end != s && !*end;
 }
 
-struct Cand {
-  std::string method, io, config;
-  double ms, rel_err;
-};
-
-struct Run {
-  int L, N, B, H, iters;
-  size_t BH;
-  int kernel_mode;   // 0 legacy, 1 cached, 2 both
-  Buffers mem;
-  std::vector<float> hu_shadow, hk, yref_shadow;
-  float* hu = nullptr;
-  const float* yref = nullptr;
-  float *du, *dy, *dyref, *dk;
-  uint16_t *dub, *dyb;
-  float* dKf;
-  sffft_baseline_t bl = nullptr;
-  cudaEvent_t e0, e1;
-  double setup_ms = 0;
-  std::vector<Cand> cands;
-
-  template <class F>
-  float timeit(F f) {
-    for (int i = 0; i < 3; i++) f();
-    CK(cudaDeviceSynchronize());
-    CK(cudaEventRecord(e0));
-    for (int i = 0; i < iters; i++) f();
-    CK(cudaEventRecord(e1));
-    CK(cudaEventSynchronize(e1));
-    float ms;
-    CK(cudaEventElapsedTime(&ms, e0, e1));
-    CK(cudaGetLastError());
-    return ms / iters;
-  }
-
-  Run(int L_, int B_, int H_, double scale, Alloc mode, bool can_prefetch, int kmode, sffft_cli::Rng& rng)
-      : L(L_), N(2 * L_), B(B_), H(H_), BH((size_t)B_ * H_), kernel_mode(kmode), mem(mode, can_prefetch) {
-    const auto t0 = Clock::now();
-    iters = std::min(200, std::max(10, 20000 / L));
-    du = mem.get<float>(BH * L * 4);
-    dy = mem.get<float>(BH * L * 4);
-    dyref = mem.get<float>(BH * L * 4);
-    dub = mem.get<uint16_t>(BH * L * 2, false);
-    dyb = mem.get<uint16_t>(BH * L * 2);
-    dk = mem.get<float>((size_t)H * L * 4);
-    dKf = mem.get<float>((size_t)H * N * 8, false);
-    hu = mem.host_view(du);
-    if (!hu) {
-      hu_shadow.resize(BH * L);
-      hu = hu_shadow.data();
-    }
-    hk.resize((size_t)H * L);
-    sffft_cli::generate(rng, BH, H, L, scale, hu, hk.data());
-    std::vector<uint16_t> ub(BH * L);
-    for (size_t i = 0; i < ub.size(); i++) ub[i] = to_bf16_bits(hu[i]);
-    mem.upload(du, hu, BH * L);
-    mem.upload(dk, hk.data(), (size_t)H * L);
-    mem.upload(dub, ub.data(), BH * L);
-    mem.to_gpu();
-    SK(sffft_baseline_create(&bl, L, B, H, dk, 0));
-    CK(cudaEventCreate(&e0));
-    CK(cudaEventCreate(&e1));
-    CK(cudaDeviceSynchronize());
-    setup_ms = since_ms(t0);
-  }
-  ~Run() {
-    if (bl) sffft_baseline_destroy(bl);
-    cudaEventDestroy(e0);
-    cudaEventDestroy(e1);
-  }
-
-  void baseline() {
-    const float t_full = timeit([&] { SK(sffft_baseline_run(bl, du, dyref, 1, nullptr)); });
-    const float t_core = timeit([&] { SK(sffft_baseline_run(bl, du, nullptr, 0, nullptr)); });
-    SK(sffft_baseline_run(bl, du, dyref, 1, nullptr));
-    CK(cudaDeviceSynchronize());
-    yref = mem.read(dyref, BH * L, yref_shadow);
-    double num = 0, den = 0;
-    for (size_t s : {(size_t)0, BH / 2, BH - 1}) {
-      const int h = (int)(s % H);
-      for (int n = 0; n < L; n++) {
-        double acc = 0;
-        for (int m = 0; m <= n; m++) acc += (double)hu[s * L + m] * (double)hk[(size_t)h * L + n - m];
-        const double d = yref[s * L + n] - acc;
-        num += d * d;
-        den += acc * acc;
-      }
-    }
-    const double err = sffft_relative_l2(num, den);
-    std::printf("RESULT,%d,cufft_pipeline_fp32,-,%.5f,%.3e\n", L, t_full, err);
-    std::printf("RESULT,%d,cufft_core_fp32,-,%.5f,%.3e\n", L, t_core, err);
-  }
-
-  void fused(const char* name, int acc, int kmode) {
-    sffft_plan_t p32, p16;
-    SK(sffft_plan_create(&p32, L, SFFFT_IO_FP32, acc, name, kmode, 0));
-    SK(sffft_plan_create(&p16, L, SFFFT_IO_BF16, acc, name, kmode, 0));
-    sffft_plan_info_t info;
-    SK(sffft_plan_info(p32, &info));
-    SK(sffft_filter_spectrum(p32, dk, SFFFT_IO_FP32, H, dKf, nullptr));
-    const float t32 = timeit([&] { SK(sffft_conv(p32, du, dKf, dy, B, H, nullptr)); });
-    const float t16 = timeit([&] { SK(sffft_conv(p16, dub, dKf, dyb, B, H, nullptr)); });
-    SK(sffft_conv(p32, du, dKf, dy, B, H, nullptr));
-    SK(sffft_plan_check(p32));
-    std::vector<float> ysh;
-    const float* y = mem.read(dy, BH * L, ysh);
-    SK(sffft_conv(p16, dub, dKf, dyb, B, H, nullptr));
-    SK(sffft_plan_check(p16));
-    std::vector<uint16_t> ybsh;
-    const uint16_t* yb = mem.read(dyb, BH * L, ybsh);
-    double n1 = 0, n2 = 0, d = 0;
-    for (size_t i = 0; i < BH * L; i++) {
-      const double r = yref[i], a = y[i] - r, b = (double)from_bf16_bits(yb[i]) - r;
-      n1 += a * a;
-      n2 += b * b;
-      d += r * r;
-    }
-    std::string plan = name;
-    plan = plan.substr(0, plan.find('/'));
-    char config[128];
-    std::snprintf(config, sizeof(config), "%s/w%d/occ%d/smem%d/kernel_%s", plan.c_str(), info.warps, info.occupancy,
-                  info.smem_bytes, kmode == SFFFT_KERNEL_CACHED ? "cached" : "legacy");
-    const char* m32 = acc == SFFFT_ACC_FP32 ? "fused_fp32io" : "fused_fp16acc_fp32io";
-    const char* m16 = acc == SFFFT_ACC_FP32 ? "fused_bf16io" : "fused_fp16acc_bf16io";
-    const double e32 = sffft_relative_l2(n1, d), e16 = sffft_relative_l2(n2, d);
-    cands.push_back({m32, "fp32", config, t32, e32});
-    cands.push_back({m16, "bf16", config, t16, e16});
-    std::printf("RESULT,%d,%s,%s,%.5f,%.3e\n", L, m32, config, t32, e32);
-    std::printf("RESULT,%d,%s,%s,%.5f,%.3e\n", L, m16, config, t16, e16);
-    std::fflush(stdout);
-    sffft_plan_destroy(p32);
-    sffft_plan_destroy(p16);
-  }
-
-  void variants(const char* name) {
-    if (kernel_mode != 1) {
-      fused(name, SFFFT_ACC_FP32, SFFFT_KERNEL_LEGACY);
-      fused(name, SFFFT_ACC_FP16, SFFFT_KERNEL_LEGACY);
-    }
-    if (kernel_mode != 0) {
-      fused(name, SFFFT_ACC_FP32, SFFFT_KERNEL_CACHED);
-      fused(name, SFFFT_ACC_FP16, SFFFT_KERNEL_CACHED);
-    }
-  }
-
-  bool select(double max_error, const char* io) {
-    std::vector<sffft_candidate_t> c;
-    for (const auto& x : cands) c.push_back({x.method.c_str(), x.io.c_str(), x.config.c_str(), x.ms, x.rel_err});
-    const int i = sffft_select_candidate(c.data(), (int)c.size(), max_error, io);
-    if (i < 0) {
-      std::printf("NO_MATCH,%d,%s,%.9e\n", L, io, max_error);
-      return false;
-    }
-    const Cand& b = cands[i];
-    std::printf("SELECT,%d,%s,%s,%.5f,%.9e,%.9e,%s\n", L, b.method.c_str(), b.config.c_str(), b.ms, b.rel_err, max_error,
-                b.io.c_str());
-    return true;
-  }
-
-  void report_memory() {
-    std::printf("MEMORY,%d,%s,%zu,%zu,%.3f,%zu,%zu,%.3f,%.3f\n", L, alloc_name(mem.mode), mem.owned,
-                (hu_shadow.size() + yref_shadow.size()) * sizeof(float), mem.alloc_ms, mem.uploaded, mem.downloaded,
-                mem.copy_ms, setup_ms);
-  }
-};
+bool pick(const char* v, const std::vector<const char*>& names, int* idx) {
+  for (size_t i = 0; i < names.size(); i++)
+    if (!std::strcmp(v, names[i])) { *idx = (int)i; return true; }
+  return false;
+}
 
 void usage() {
   std::printf(
@@ -324,126 +94,475 @@ void usage() {
       "the program exits 2 when a length has none.  Invalid arguments exit 1.\n");
 }
 
-}  // namespace
-
-int main(int argc, char** argv) {
-  int B = 8, H = 768, only = 0, positional = 0, failed = 0, kernel_mode = 0;
-  double max_error = -1, input_scale = 1;
-  const char* io = "fp32";
-  Alloc alloc = Alloc::Device;
-  bool memory_info = false;
-  sffft_cli::Rng rng;
+// Returns -1 to continue, or the exit code.
+int parse(int argc, char** argv, Options& o) {
+  struct Flag {
+    const char* name;
+    const char* complaint;                       // printed when the value is rejected
+    std::function<bool(const char*)> apply;      // null: a switch without a value
+  };
+  const std::vector<Flag> flags = {
+      {"--max-error", "--max-error needs a positive finite number",
+       [&](const char* v) { return parse_double(v, &o.max_error) && std::isfinite(o.max_error) && o.max_error > 0; }},
+      {"--input-scale", "--input-scale needs a positive finite number within fp32 range",
+       [&](const char* v) {
+         return parse_double(v, &o.input_scale) && std::isfinite(o.input_scale) && o.input_scale > 0 &&
+                o.input_scale <= std::numeric_limits<float>::max();
+       }},
+      {"--io", "--io takes fp32, bf16 or any",
+       [&](const char* v) {
+         int i;
+         if (!pick(v, {"fp32", "bf16", "any"}, &i)) return false;
+         o.io = i == 0 ? "fp32" : i == 1 ? "bf16" : "any";
+         return true;
+       }},
+      {"--seed", "--seed needs a nonzero unsigned integer",
+       [&](const char* v) {
+         char* end = nullptr;
+         errno = 0;
+         o.seed = std::strtoull(v, &end, 10);
+         return !errno && end != v && !*end && v[0] != '-' && o.seed != 0;
+       }},
+      {"--allocator", "--allocator takes device, managed, mapped or hybrid",
+       [&](const char* v) {
+         int i;
+         if (!pick(v, {"device", "managed", "mapped", "hybrid"}, &i)) return false;
+         o.mode = (Mode)i;
+         return true;
+       }},
+      {"--kernel", "--kernel takes legacy, cached or auto",
+       [&](const char* v) { return pick(v, {"legacy", "cached", "auto"}, &o.kernels); }},
+      {"--memory-info", nullptr, nullptr},
+  };
+  int positional = 0;
   for (int i = 1; i < argc; i++) {
     const char* a = argv[i];
-    char* end = nullptr;
-    errno = 0;
     if (!std::strcmp(a, "--help") || !std::strcmp(a, "-h")) {
       usage();
       return 0;
     }
-    if (!std::strcmp(a, "--memory-info")) {
-      memory_info = true;
+    const Flag* f = nullptr;
+    for (const Flag& c : flags)
+      if (!std::strcmp(a, c.name)) f = &c;
+    if (f && !f->apply) {
+      o.memory_info = true;
       continue;
     }
-    if (!std::strcmp(a, "--allocator")) {
-      if (++i == argc) { usage(); return 1; }
-      const char* v = argv[i];
-      if (!std::strcmp(v, "device")) alloc = Alloc::Device;
-      else if (!std::strcmp(v, "managed")) alloc = Alloc::Managed;
-      else if (!std::strcmp(v, "mapped")) alloc = Alloc::Mapped;
-      else if (!std::strcmp(v, "hybrid")) alloc = Alloc::Hybrid;
-      else { std::fprintf(stderr, "--allocator takes device, managed, mapped or hybrid\n"); return 1; }
-    } else if (!std::strcmp(a, "--kernel")) {
-      if (++i == argc) { usage(); return 1; }
-      const char* v = argv[i];
-      if (!std::strcmp(v, "legacy")) kernel_mode = 0;
-      else if (!std::strcmp(v, "cached")) kernel_mode = 1;
-      else if (!std::strcmp(v, "auto")) kernel_mode = 2;
-      else { std::fprintf(stderr, "--kernel takes legacy, cached or auto\n"); return 1; }
-    } else if (!std::strcmp(a, "--max-error")) {
-      if (++i == argc) { usage(); return 1; }
-      max_error = std::strtod(argv[i], &end);
-      if (errno || end == argv[i] || *end || !std::isfinite(max_error) || max_error <= 0) {
-        std::fprintf(stderr, "--max-error needs a positive finite number\n");
-        return 1;
-      }
-    } else if (!std::strcmp(a, "--input-scale")) {
-      if (++i == argc) { usage(); return 1; }
-      input_scale = std::strtod(argv[i], &end);
-      if (errno || end == argv[i] || *end || !std::isfinite(input_scale) || input_scale <= 0 ||
-          input_scale > std::numeric_limits<float>::max()) {
-        std::fprintf(stderr, "--input-scale needs a positive finite number within fp32 range\n");
-        return 1;
-      }
-    } else if (!std::strcmp(a, "--io")) {
-      if (++i == argc) { usage(); return 1; }
-      io = argv[i];
-      if (std::strcmp(io, "fp32") && std::strcmp(io, "bf16") && std::strcmp(io, "any")) {
-        std::fprintf(stderr, "--io takes fp32, bf16 or any\n");
-        return 1;
-      }
-    } else if (!std::strcmp(a, "--seed")) {
-      if (++i == argc) { usage(); return 1; }
-      rng.s = std::strtoull(argv[i], &end, 10);
-      if (errno || end == argv[i] || *end || argv[i][0] == '-' || !rng.s) {
-        std::fprintf(stderr, "--seed needs a nonzero unsigned integer\n");
-        return 1;
-      }
-    } else {
-      const long v = std::strtol(a, &end, 10);
-      if (errno || end == a || *end || v < 0 || v > INT_MAX || positional == 3) {
-        std::fprintf(stderr, "Invalid argument: %s\n", a);
+    if (f) {
+      if (i + 1 == argc) {
         usage();
         return 1;
       }
-      if (positional == 0) B = (int)v;
-      else if (positional == 1) H = (int)v;
-      else only = (int)v;
-      positional++;
+      if (!f->apply(argv[++i])) {
+        std::fprintf(stderr, "%s\n", f->complaint);
+        return 1;
+      }
+      continue;
     }
+    char* end = nullptr;
+    errno = 0;
+    const long v = std::strtol(a, &end, 10);
+    if (errno || end == a || *end || v < 0 || v > INT_MAX || positional == 3) {
+      std::fprintf(stderr, "Invalid argument: %s\n", a);
+      usage();
+      return 1;
+    }
+    int* slot[3] = {&o.B, &o.H, &o.L};
+    *slot[positional++] = (int)v;
   }
-  if (B < 1 || H < 1 || (long long)B * H > INT_MAX ||
-      (only && (only < 128 || only > 16384 || (only & (only - 1))))) {
+  if (o.B < 1 || o.H < 1 || (long long)o.B * o.H > INT_MAX ||
+      (o.L && (o.L < 128 || o.L > 16384 || (o.L & (o.L - 1))))) {
     std::fprintf(stderr, "B and H must be positive with B*H <= INT_MAX; L must be 0 or a power of two in 128..16384\n");
     return 1;
   }
-  if (alloc == Alloc::Mapped || alloc == Alloc::Hybrid) CK(cudaSetDeviceFlags(cudaDeviceMapHost));
+  return -1;
+}
+
+// ------------------------------------------------------------------------------------------------
+// Arena: buffers placed by role under the allocation mode, with the MEMORY row's accounts
+// ------------------------------------------------------------------------------------------------
+// Roles: the calibration input u, the outputs and the cuFFT reference are "host facing" (the host writes or
+// reads them); the bf16 input copy, the filter and the spectrum are "device only".  The hybrid mode maps the
+// host-facing ones and keeps the others in device memory; the other modes place every buffer the same way.
+// Host access goes through the host view of a mapped / managed buffer (no copy) or through an explicit copy
+// of a device buffer (counted: uploads, downloads, and the host shadow that a copied-in input keeps).
+class Arena {
+ public:
+  struct Accounts {
+    size_t owned = 0, shadow = 0, uploaded = 0, downloaded = 0;
+    double alloc_ms = 0, copy_ms = 0;
+  };
+
+  Arena(Mode m, bool prefetch_ok) : mode_(m), prefetch_ok_(prefetch_ok) {}
+  Arena(const Arena&) = delete;
+  ~Arena() {
+    for (const Buf& b : bufs_) {
+      if (b.placement == Mode::Mapped) cudaFreeHost(b.host);
+      else cudaFree(b.dev);
+    }
+  }
+
+  void* make(size_t bytes, bool host_facing) {
+    const Mode where = mode_ == Mode::Hybrid ? (host_facing ? Mode::Mapped : Mode::Device) : mode_;
+    const auto t0 = Clock::now();
+    Buf b{nullptr, nullptr, bytes, where};
+    if (where == Mode::Mapped) {
+      cuda_ok(cudaHostAlloc(&b.host, bytes, cudaHostAllocMapped), "cudaHostAlloc");
+      cuda_ok(cudaHostGetDevicePointer(&b.dev, b.host, 0), "cudaHostGetDevicePointer");
+    } else if (where == Mode::Managed) {
+      cuda_ok(cudaMallocManaged(&b.dev, bytes), "cudaMallocManaged");
+      b.host = b.dev;
+    } else {
+      cuda_ok(cudaMalloc(&b.dev, bytes), "cudaMalloc");
+    }
+    acc_.alloc_ms += ms_since(t0);
+    acc_.owned += bytes;
+    bufs_.push_back(b);
+    return b.dev;
+  }
+
+  // Host address of a buffer the host can touch directly, or null for device memory.
+  void* host_of(const void* dev) const {
+    for (const Buf& b : bufs_)
+      if (b.dev == dev) return b.host;
+    return nullptr;
+  }
+
+  // Places host data into a buffer: in place for host-visible buffers, else one counted copy.
+  void fill(void* dev, const void* src, size_t bytes) {
+    void* h = host_of(dev);
+    if (h == src) return;
+    const auto t0 = Clock::now();
+    if (h) {
+      std::memcpy(h, src, bytes);
+    } else {
+      cuda_ok(cudaMemcpy(dev, src, bytes, cudaMemcpyHostToDevice), "upload");
+      acc_.uploaded += bytes;
+    }
+    acc_.copy_ms += ms_since(t0);
+  }
+
+  // Host-readable view of a device result: the buffer itself, or a counted copy into `scratch`.
+  template <class T>
+  const T* view(const T* dev, size_t n, std::vector<T>& scratch) {
+    if (void* h = host_of(dev)) {
+      migrate(dev, n * sizeof(T), false);
+      cuda_ok(cudaDeviceSynchronize(), "synchronize");
+      return static_cast<const T*>(h);
+    }
+    scratch.resize(n);
+    const auto t0 = Clock::now();
+    cuda_ok(cudaMemcpy(scratch.data(), dev, n * sizeof(T), cudaMemcpyDeviceToHost), "download");
+    acc_.downloaded += n * sizeof(T);
+    acc_.copy_ms += ms_since(t0);
+    return scratch.data();
+  }
+
+  // Managed memory: move every buffer to the GPU before the timed calls.
+  void to_device() {
+    for (const Buf& b : bufs_) migrate(b.dev, b.bytes, true);
+  }
+
+  void note_shadow(size_t bytes) { acc_.shadow += bytes; }
+  Mode mode() const { return mode_; }
+  const Accounts& accounts() const { return acc_; }
+
+ private:
+  struct Buf {
+    void *dev, *host;
+    size_t bytes;
+    Mode placement;
+  };
+  void migrate(const void* p, size_t bytes, bool to_gpu) {
+    if (mode_ != Mode::Managed || !prefetch_ok_) return;
+#if CUDART_VERSION >= 13000
+    cudaMemLocation loc{};
+    loc.type = to_gpu ? cudaMemLocationTypeDevice : cudaMemLocationTypeHost;
+    loc.id = 0;
+    cuda_ok(cudaMemPrefetchAsync(p, bytes, loc, 0), "prefetch");
+#else
+    cuda_ok(cudaMemPrefetchAsync(p, bytes, to_gpu ? 0 : cudaCpuDeviceId), "prefetch");
+#endif
+  }
+  Mode mode_;
+  bool prefetch_ok_;
+  std::vector<Buf> bufs_;
+  Accounts acc_;
+};
+
+// ------------------------------------------------------------------------------------------------
+// Timing: three warm-up calls, then the mean of `iters` back-to-back calls between two events.
+// ------------------------------------------------------------------------------------------------
+class EventTimer {
+ public:
+  explicit EventTimer(int iters) : iters_(iters) {
+    cuda_ok(cudaEventCreate(&a_), "event");
+    cuda_ok(cudaEventCreate(&b_), "event");
+  }
+  ~EventTimer() {
+    cudaEventDestroy(a_);
+    cudaEventDestroy(b_);
+  }
+  double mean_ms(const std::function<void()>& call) {
+    for (int i = 0; i < 3; i++) call();
+    cuda_ok(cudaDeviceSynchronize(), "warm-up");
+    cuda_ok(cudaEventRecord(a_), "event");
+    for (int i = 0; i < iters_; i++) call();
+    cuda_ok(cudaEventRecord(b_), "event");
+    cuda_ok(cudaEventSynchronize(b_), "event");
+    float ms = 0;
+    cuda_ok(cudaEventElapsedTime(&ms, a_, b_), "event");
+    cuda_ok(cudaGetLastError(), "timed calls");
+    return ms / iters_;
+  }
+
+ private:
+  int iters_;
+  cudaEvent_t a_, b_;
+};
+
+uint16_t bf16_round(float f) {
+  uint32_t x;
+  std::memcpy(&x, &f, 4);
+  if ((x & 0x7FFFFFFFu) > 0x7F800000u) return 0x7FC0u;
+  return (uint16_t)((x + 0x7FFFu + ((x >> 16) & 1u)) >> 16);
+}
+double bf16_value(uint16_t b) {
+  const uint32_t x = (uint32_t)b << 16;
+  float f;
+  std::memcpy(&f, &x, 4);
+  return f;
+}
+
+// ------------------------------------------------------------------------------------------------
+// Calibration of one length
+// ------------------------------------------------------------------------------------------------
+struct Candidate {
+  std::string method, io, config;
+  double ms, rel_err;
+};
+
+class Calibration {
+ public:
+  Calibration(const Options& o, int L, bool prefetch_ok, sffft_cli::Rng& rng)
+      : L_(L), B_(o.B), H_(o.H), n_((size_t)o.B * o.H * L), arena_(o.mode, prefetch_ok),
+        timer_(std::min(200, std::max(10, 20000 / L))) {
+    const auto t0 = Clock::now();
+    u_ = static_cast<float*>(arena_.make(n_ * 4, true));
+    y_ = static_cast<float*>(arena_.make(n_ * 4, true));
+    yref_ = static_cast<float*>(arena_.make(n_ * 4, true));
+    ub_ = static_cast<uint16_t*>(arena_.make(n_ * 2, false));
+    yb_ = static_cast<uint16_t*>(arena_.make(n_ * 2, true));
+    k_ = static_cast<float*>(arena_.make((size_t)H_ * L * 4, true));
+    Kf_ = arena_.make((size_t)H_ * 2 * L * 8, false);
+    // the generator writes u straight into a host-visible input, else into a host copy that stays alive
+    float* hu = static_cast<float*>(arena_.host_of(u_));
+    if (!hu) {
+      hu_.resize(n_);
+      hu = hu_.data();
+    }
+    hk_.resize((size_t)H_ * L);
+    sffft_cli::generate(rng, (size_t)B_ * H_, H_, L, o.input_scale, hu, hk_.data());
+    host_u_ = hu;
+    std::vector<uint16_t> b16(n_);
+    for (size_t i = 0; i < n_; i++) b16[i] = bf16_round(hu[i]);
+    arena_.fill(u_, hu, n_ * 4);
+    arena_.fill(k_, hk_.data(), hk_.size() * 4);
+    arena_.fill(ub_, b16.data(), n_ * 2);
+    arena_.to_device();
+    sffft_ok(sffft_baseline_create(&cufft_, L, B_, H_, k_, 0), "cuFFT pipeline");
+    cuda_ok(cudaDeviceSynchronize(), "set-up");
+    setup_ms_ = ms_since(t0);
+  }
+  ~Calibration() {
+    if (cufft_) sffft_baseline_destroy(cufft_);
+  }
+
+  // cuFFT pipeline rows; its output becomes the reference of every fused candidate.
+  void cufft_rows() {
+    const double full = timer_.mean_ms([&] { sffft_ok(sffft_baseline_run(cufft_, u_, yref_, 1, nullptr), "cuFFT"); });
+    const double core = timer_.mean_ms([&] { sffft_ok(sffft_baseline_run(cufft_, u_, nullptr, 0, nullptr), "cuFFT"); });
+    sffft_ok(sffft_baseline_run(cufft_, u_, yref_, 1, nullptr), "cuFFT");
+    cuda_ok(cudaDeviceSynchronize(), "cuFFT");
+    ref_ = arena_.view(yref_, n_, ref_copy_);
+    // fp64 direct convolution of the first, middle and last sequence (channel = sequence % H)
+    const size_t BH = (size_t)B_ * H_;
+    double err = 0, norm = 0;
+    for (size_t s : {(size_t)0, BH / 2, BH - 1}) {
+      const float* us = host_u_ + s * L_;
+      const float* ks = hk_.data() + (s % H_) * L_;
+      for (int n = 0; n < L_; n++) {
+        double v = 0;
+        for (int m = 0; m <= n; m++) v += (double)us[m] * (double)ks[n - m];
+        const double d = ref_[s * L_ + n] - v;
+        err += d * d;
+        norm += v * v;
+      }
+    }
+    const double rel = sffft_relative_l2(err, norm);
+    std::printf("RESULT,%d,cufft_pipeline_fp32,-,%.5f,%.3e\n", L_, full, rel);
+    std::printf("RESULT,%d,cufft_core_fp32,-,%.5f,%.3e\n", L_, core, rel);
+  }
+
+  // Both I/O types of one catalog plan with one accumulation and one DFT-matrix mode.
+  void fused_rows(const char* plan_name, int acc, int kmode) {
+    struct Side {
+      int io;
+      const void* in;
+      void* out;
+      const char* method;
+      const char* io_name;
+    };
+    const Side sides[2] = {
+        {SFFFT_IO_FP32, u_, y_, acc == SFFFT_ACC_FP32 ? "fused_fp32io" : "fused_fp16acc_fp32io", "fp32"},
+        {SFFFT_IO_BF16, ub_, yb_, acc == SFFFT_ACC_FP32 ? "fused_bf16io" : "fused_fp16acc_bf16io", "bf16"}};
+    std::string config;
+    double ms[2], err[2];
+    for (int i = 0; i < 2; i++) {
+      const Side& sd = sides[i];
+      sffft_plan_t plan;
+      sffft_ok(sffft_plan_create(&plan, L_, sd.io, acc, plan_name, kmode, 0), "plan");
+      if (i == 0) {
+        sffft_plan_info_t info;
+        sffft_ok(sffft_plan_info(plan, &info), "plan info");
+        const std::string radices = std::string(plan_name).substr(0, std::string(plan_name).find('/'));
+        char buf[128];
+        std::snprintf(buf, sizeof(buf), "%s/w%d/occ%d/smem%d/kernel_%s", radices.c_str(), info.warps, info.occupancy,
+                      info.smem_bytes, kmode == SFFFT_KERNEL_CACHED ? "cached" : "legacy");
+        config = buf;
+        sffft_ok(sffft_filter_spectrum(plan, k_, SFFFT_IO_FP32, H_, Kf_, nullptr), "spectrum");
+      }
+      ms[i] = timer_.mean_ms([&] { sffft_ok(sffft_conv(plan, sd.in, Kf_, sd.out, B_, H_, nullptr), "conv"); });
+      sffft_ok(sffft_conv(plan, sd.in, Kf_, sd.out, B_, H_, nullptr), "conv");
+      sffft_ok(sffft_plan_check(plan), "device status");
+      double e = 0, norm = 0;
+      if (sd.io == SFFFT_IO_FP32) {
+        std::vector<float> copy;
+        const float* y = arena_.view(static_cast<const float*>(sd.out), n_, copy);
+        for (size_t j = 0; j < n_; j++) {
+          const double d = y[j] - ref_[j];
+          e += d * d;
+          norm += (double)ref_[j] * ref_[j];
+        }
+      } else {
+        std::vector<uint16_t> copy;
+        const uint16_t* y = arena_.view(static_cast<const uint16_t*>(sd.out), n_, copy);
+        for (size_t j = 0; j < n_; j++) {
+          const double d = bf16_value(y[j]) - ref_[j];
+          e += d * d;
+          norm += (double)ref_[j] * ref_[j];
+        }
+      }
+      err[i] = sffft_relative_l2(e, norm);
+      sffft_plan_destroy(plan);
+    }
+    for (int i = 0; i < 2; i++) {
+      cands_.push_back({sides[i].method, sides[i].io_name, config, ms[i], err[i]});
+      std::printf("RESULT,%d,%s,%s,%.5f,%.3e\n", L_, sides[i].method, config.c_str(), ms[i], err[i]);
+    }
+    std::fflush(stdout);
+  }
+
+  // Every catalog plan of this length, in the DFT-matrix modes asked for, both accumulations.
+  void all_candidates(int kernels) {
+    const int modes[2] = {SFFFT_KERNEL_LEGACY, SFFFT_KERNEL_CACHED};
+    char name[96];
+    for (int i = 0; i < sffft_catalog_count(); i++) {
+      int len = 0;
+      sffft_ok(sffft_catalog_entry(i, &len, name, sizeof(name)), "catalog");
+      if (len != L_) continue;
+      for (int km : modes) {
+        if ((kernels == 0 && km != SFFFT_KERNEL_LEGACY) || (kernels == 1 && km != SFFFT_KERNEL_CACHED)) continue;
+        fused_rows(name, SFFFT_ACC_FP32, km);
+        fused_rows(name, SFFFT_ACC_FP16, km);
+      }
+    }
+  }
+
+  // SELECT or NO_MATCH row; false when nothing met the budget.
+  bool select_row(double max_error, const char* io) const {
+    std::vector<sffft_candidate_t> c;
+    for (const Candidate& x : cands_) c.push_back({x.method.c_str(), x.io.c_str(), x.config.c_str(), x.ms, x.rel_err});
+    const int pick = sffft_select_candidate(c.data(), (int)c.size(), max_error, io);
+    if (pick < 0) {
+      std::printf("NO_MATCH,%d,%s,%.9e\n", L_, io, max_error);
+      return false;
+    }
+    const Candidate& w = cands_[pick];
+    std::printf("SELECT,%d,%s,%s,%.5f,%.9e,%.9e,%s\n", L_, w.method.c_str(), w.config.c_str(), w.ms, w.rel_err,
+                max_error, w.io.c_str());
+    return true;
+  }
+
+  void memory_row() {
+    const Arena::Accounts& a = arena_.accounts();
+    const size_t shadows = (hu_.size() + ref_copy_.size()) * sizeof(float);
+    std::printf("MEMORY,%d,%s,%zu,%zu,%.3f,%zu,%zu,%.3f,%.3f\n", L_, mode_name(arena_.mode()), a.owned, shadows,
+                a.alloc_ms, a.uploaded, a.downloaded, a.copy_ms, setup_ms_);
+  }
+
+ private:
+  int L_, B_, H_;
+  size_t n_;
+  Arena arena_;
+  EventTimer timer_;
+  float *u_, *y_, *yref_, *k_;
+  uint16_t *ub_, *yb_;
+  void* Kf_;
+  const float* host_u_ = nullptr;
+  const float* ref_ = nullptr;
+  std::vector<float> hu_, hk_, ref_copy_;
+  sffft_baseline_t cufft_ = nullptr;
+  std::vector<Candidate> cands_;
+  double setup_ms_ = 0;
+};
+
+}  // namespace
+
+int main(int argc, char** argv) {
+  Options o;
+  const int rc = parse(argc, argv, o);
+  if (rc >= 0) return rc;
+
+  if (o.mode == Mode::Mapped || o.mode == Mode::Hybrid) cuda_ok(cudaSetDeviceFlags(cudaDeviceMapHost), "device flags");
   cudaDeviceProp p;
-  CK(cudaGetDeviceProperties(&p, 0));
-  int managed = 0, concurrent = 0, pageable = 0, host_tables = 0;
-  CK(cudaDeviceGetAttribute(&managed, cudaDevAttrManagedMemory, 0));
-  CK(cudaDeviceGetAttribute(&concurrent, cudaDevAttrConcurrentManagedAccess, 0));
-  CK(cudaDeviceGetAttribute(&pageable, cudaDevAttrPageableMemoryAccess, 0));
-  CK(cudaDeviceGetAttribute(&host_tables, cudaDevAttrPageableMemoryAccessUsesHostPageTables, 0));
+  cuda_ok(cudaGetDeviceProperties(&p, 0), "device properties");
+  auto attr = [](cudaDeviceAttr a) {
+    int v = 0;
+    cuda_ok(cudaDeviceGetAttribute(&v, a, 0), "device attribute");
+    return v;
+  };
+  const int managed = attr(cudaDevAttrManagedMemory), concurrent = attr(cudaDevAttrConcurrentManagedAccess);
+  const int pageable = attr(cudaDevAttrPageableMemoryAccess);
+  const int host_tables = attr(cudaDevAttrPageableMemoryAccessUsesHostPageTables);
   std::printf("# MEMORY_CAPS,mapped=%d,managed=%d,concurrent_managed=%d,pageable=%d,host_page_tables=%d,integrated=%d\n",
               p.canMapHostMemory, managed, concurrent, pageable, host_tables, p.integrated);
-  if (memory_info) return 0;
-  if (((alloc == Alloc::Mapped || alloc == Alloc::Hybrid) && !p.canMapHostMemory) || (alloc == Alloc::Managed && !managed)) {
+  if (o.memory_info) return 0;
+  const bool needs_map = o.mode == Mode::Mapped || o.mode == Mode::Hybrid;
+  if ((needs_map && !p.canMapHostMemory) || (o.mode == Mode::Managed && !managed)) {
     std::fprintf(stderr, "Requested allocator is unsupported on this device\n");
     return 1;
   }
   std::printf("# %s sm_%d%d %d SMs, smem/block %zu, L2 %d MB, B=%d H=%d\n", p.name, p.major, p.minor,
-              p.multiProcessorCount, p.sharedMemPerBlockOptin, p.l2CacheSize >> 20, B, H);
-  std::printf("# calibration seed=%llu, input_scale=%.9e, max_error=%.9e, io=%s,allocator=%s,kernel=%s\n", rng.s,
-              input_scale, max_error, io, alloc_name(alloc),
-              kernel_mode == 0 ? "legacy" : kernel_mode == 1 ? "cached" : "auto");
+              p.multiProcessorCount, p.sharedMemPerBlockOptin, p.l2CacheSize >> 20, o.B, o.H);
+  std::printf("# calibration seed=%llu, input_scale=%.9e, max_error=%.9e, io=%s,allocator=%s,kernel=%s\n", o.seed,
+              o.input_scale, o.max_error, o.io, mode_name(o.mode), kernel_name(o.kernels));
   std::printf("# RESULT,L,method,config,ms,rel_err\n");
-  std::printf("# MEMORY,L,allocator,owned_bytes,persistent_host_shadow_bytes,allocation_ms,upload_bytes,download_bytes,copy_ms,setup_ms\n");
-  if (max_error > 0) std::printf("# SELECT,L,method,config,ms,rel_err,max_error,io\n");
+  std::printf("# MEMORY,L,allocator,owned_bytes,persistent_host_shadow_bytes,allocation_ms,upload_bytes,download_bytes,"
+              "copy_ms,setup_ms\n");
+  if (o.max_error > 0) std::printf("# SELECT,L,method,config,ms,rel_err,max_error,io\n");
 
-  const int ncat = sffft_catalog_count();
+  // one generator stream across the lengths, as the reference draws them
+  sffft_cli::Rng rng;
+  rng.s = o.seed;
+  int misses = 0;
   for (int L = 128; L <= 16384; L *= 2) {
-    if (only ? only != L : L > 8192) continue;
-    Run run(L, B, H, input_scale, alloc, concurrent != 0, kernel_mode, rng);
-    run.baseline();
-    char name[96];
-    for (int i = 0; i < ncat; i++) {
-      int cl = 0;
-      SK(sffft_catalog_entry(i, &cl, name, sizeof(name)));
-      if (cl == L) run.variants(name);
-    }
-    if (max_error > 0 && !run.select(max_error, io)) failed++;
-    run.report_memory();
+    if (o.L ? o.L != L : L > 8192) continue;
+    Calibration cal(o, L, concurrent != 0, rng);
+    cal.cufft_rows();
+    cal.all_candidates(o.kernels);
+    if (o.max_error > 0 && !cal.select_row(o.max_error, o.io)) misses++;
+    cal.memory_row();
   }
-  return failed ? 2 : 0;
+  return misses ? 2 : 0;
 }

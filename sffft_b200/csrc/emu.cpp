@@ -135,12 +135,9 @@ struct HostOps {
   void store1(uint16_t* p, float v) { *p = (uint16_t)bf16_from_float(v); }
   void store4(float* p, const float* v) { for (int i = 0; i < 4; i++) p[i] = v[i]; }
   void store4(uint16_t* p, const float* v) { for (int i = 0; i < 4; i++) p[i] = (uint16_t)bf16_from_float(v[i]); }
-  // energies of a thread's conversion steps (the device sums the SEG lanes of a run with shuffles; the
-  // emulated threads run one after another, so they accumulate)
-  template <int NSTEP, int SEG>
-  void energy_store(float* part, const float (&ss)[NSTEP], int tid, int stride) {
-    for (int i = 0; i < NSTEP; i++) part[(tid * 8 + i * stride) / (8 * SEG)] += ss[i];
-  }
+  // a sequence's energy (the device sums the SEG lanes that share it with shuffles; the emulated threads run
+  // one after another, so they accumulate)
+  void energy_store(float* part, int idx, float ss, int) { part[idx] += ss; }
   void st4(uint32_t off, float v) {
     if ((off & 3) || (size_t)off + 4 > data_bytes) throw std::out_of_range("staged output outside the data buffer");
     std::memcpy(smem->data() + base + off, &v, 4);
@@ -229,14 +226,16 @@ int run_plan(const void* u, const float* Kf, void* y, int B, int H) {
     ops.in_hi = (const uint8_t*)u + (size_t)B * H * P::L * sizeof(TIO);
     const GroupPairs gp = group_pairs(group, P::G, B, H);
     std::memset(smem.data() + dbase, 0xFF, P::DATA_BYTES);   // poison: stale data must never be read
-    // the two conversion passes of the kernel: energies, then (where a pair needs it) scaled input
-    std::vector<float> part(Energy<P>::SLOTS, 0.f), psc(2 * P::G), osc(2 * P::G);
-    for (int tid = 0; tid < SH::TWARPS * 32; tid++)
-      convert_group<P, TIO, SH::NB, SH::TWARPS * 32>(ops, uu, gp, tid, part.data(), nullptr);
-    if (pair_scales<P>(part.data(), psc.data(), osc.data()))
-      for (int tid = 0; tid < SH::TWARPS * 32; tid++)
-        convert_group<P, TIO, SH::NB, SH::TWARPS * 32>(ops, uu, gp, tid, nullptr, psc.data());
-    EpiArgs ea{(uint32_t)(slot * P::TMEM_COLS), Kf, y, B, H, group, nullptr, 0, osc.data()};
+    // the two conversion passes of the kernel: energies, then (where a row needs it) scaled input
+    constexpr int NT = SH::TWARPS * 32;
+    std::vector<float> part(Energy<P, NT>::SLOTS, 0.f);
+    for (int tid = 0; tid < NT; tid++) convert_group<P, TIO, SH::NB, NT>(ops, uu, gp, tid, part.data(), 1.f);
+    if (group_rescaled<P, NT>(part.data()))
+      for (int tid = 0; tid < NT; tid++) {
+        const int j = tid / Energy<P, NT>::TPS;
+        convert_group<P, TIO, SH::NB, NT>(ops, uu, gp, tid, nullptr, row_in_scale<P, NT>(part.data(), j >> 1, j & 1));
+      }
+    EpiArgs ea{(uint32_t)(slot * P::TMEM_COLS), Kf, y, B, H, group, nullptr, 0, part.data()};
     // the loader warp's staging of the group's spectrum rows (same swizzle as the device)
     if constexpr (SH::KSLOT > 0) {
       const int hf = gp.get(0, P::L).h;

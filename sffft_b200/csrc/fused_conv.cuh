@@ -116,35 +116,13 @@ struct DevOps {
     __nv_bfloat162 a = __floats2bfloat162_rn(v[0], v[1]), b = __floats2bfloat162_rn(v[2], v[3]);
     __stcs(reinterpret_cast<uint2*>(p), make_uint2(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&b)));
   }
-  // Energies of a thread's NSTEP conversion steps (step i covers elements tid * 8 + i * stride .. + 7): the
-  // SEG lanes of a warp that share a run of one sequence are summed per step with a butterfly that halves the
-  // values a lane carries at each exchange (NSTEP / 2 + NSTEP / 4 + ... shuffles instead of NSTEP per level),
-  // after which lane l holds the total of one step and the run's leader lanes store them.
-  template <int NSTEP, int SEG>
-  __device__ __forceinline__ void energy_store(float* part, const float (&ss)[NSTEP], int tid, int stride) {
-    const int lane = tid & 31;
-    float v[NSTEP];
+  // A sequence's energy over the SEG lanes of this warp that share it (SEG lanes, aligned), stored by the
+  // first of them in part[idx].
+  __device__ __forceinline__ void energy_store(float* part, int idx, float ss, int seg) {
 #pragma unroll
-    for (int i = 0; i < NSTEP; i++) v[i] = ss[i];
-    int idx = 0;
-#pragma unroll
-    for (int lvl = 0, m = SEG / 2; m >= 1; lvl++, m >>= 1) {
-      const int n = NSTEP >> lvl;
-      const bool up = (lane & m) != 0;
-      if (n > 1) {
-#pragma unroll
-        for (int j = 0; j < n / 2; j++) {
-          const float send = up ? v[j] : v[j + n / 2], keep = up ? v[j + n / 2] : v[j];
-          v[j] = keep + __shfl_xor_sync(0xffffffffu, send, m);
-        }
-        if (up) idx += n / 2;
-      } else {
-        v[0] += __shfl_xor_sync(0xffffffffu, v[0], m);
-      }
-    }
-    constexpr int REST = SEG / NSTEP;   // lanes that end up holding the same total
-    if ((lane & (REST - 1)) == 0)
-      part[((tid & ~(SEG - 1)) * 8 + idx * stride) / (8 * SEG)] = v[0];
+    for (int m = 16; m > 0; m >>= 1)
+      if (m < seg) ss += __shfl_xor_sync(0xffffffffu, ss, m);
+    if ((threadIdx.x & (seg - 1)) == 0) part[idx] = ss;
   }
   __device__ __forceinline__ void st4(uint32_t off, float v) { *reinterpret_cast<float*>(sm + off) = v; }
   __device__ __forceinline__ void ld4_staged(uint32_t off, uint32_t rot, float* v) {
@@ -354,39 +332,32 @@ __device__ __forceinline__ bool team_sync(uint64_t* bar, uint32_t& phase, int la
   return ok;
 }
 
+// Whether any row of the group is scaled (pair_scales), the lanes of one warp in parallel: lane j < 2G sums
+// row j's energy slots, gets its partner row's energy by a shuffle and derives its row's exponent.  Every
+// warp of the team reads the same slots and reaches the same answer.
+template <class P, int NT>
+__device__ __forceinline__ bool group_rescaled_warp(const float* en, int lane) {
+  using EN = Energy<P, NT>;
+  constexpr int NSQ = 2 * P::G;
+  static_assert(NSQ <= 32, "rows per group");
+  float e = 0.f;
+  if (lane < NSQ)
+    for (int i = 0; i < EN::SPS; i++) e += en[lane * EN::SPS + i];
+  const float ep = __shfl_xor_sync(0xffffffffu, e, 1);
+  int f0 = 0, f1 = 0;
+  if (lane < NSQ) {
+    if (lane & 1) pair_exponents(ep, e, P::L, &f0, &f1);
+    else pair_exponents(e, ep, P::L, &f0, &f1);
+  }
+  return __any_sync(0xffffffffu, ((lane & 1) ? f1 : f0) != 0) != 0;
+}
+
 // The second conversion pass of a group with a row to rescale (rare), out of line so that it adds nothing to
 // the register allocation of the kernel's main loop.
 template <class P, class TIO, int NB, int NT>
-__device__ __noinline__ void convert_scaled(DevOps ops, const TIO* u, GroupPairs gp, int tid, const float* psc) {
-  convert_group<P, TIO, NB, NT>(ops, u, gp, tid, nullptr, psc);
-}
-
-// Scales of a group's 2G rows (pair_scales, computed in parallel): the energy slots of row j are summed by
-// the 32 / 2G lanes j * 32 / 2G.., every lane gets its partner row's energy by a shuffle and derives its row's
-// exponent; one lane per row writes the row's input and output scales to en[ENS + j] and en[ENS + 2G + j].
-// Every warp of the team computes and writes the same values and reads only its own.  Returns whether any
-// row of the group is scaled.
-template <class P>
-__device__ __forceinline__ bool group_scales(float* en, int lane) {
-  constexpr int NSQ = 2 * P::G, LPS = 32 / NSQ, SPS = Energy<P>::SPS, ENS = Energy<P>::SLOTS;
-  static_assert(NSQ <= 32 && 32 % NSQ == 0, "rows per group");
-  const int j = lane / LPS, r = lane - j * LPS;
-  float e = 0.f;
-  for (int i = r; i < SPS; i += LPS) e += en[j * SPS + i];
-#pragma unroll
-  for (int m = LPS / 2; m >= 1; m >>= 1) e += __shfl_xor_sync(0xffffffffu, e, m);
-  const float ep = __shfl_sync(0xffffffffu, e, ((j ^ 1) * LPS + r) & 31);
-  int f0, f1;
-  if (j & 1) pair_exponents(ep, e, P::L, &f0, &f1);
-  else pair_exponents(e, ep, P::L, &f0, &f1);
-  const int f = (j & 1) ? f1 : f0;
-  if (r == 0) {
-    en[ENS + j] = ldexpf(1.f, f);
-    en[ENS + NSQ + j] = e == 0.f ? 0.f : ldexpf(1.f, -f);
-  }
-  const bool any = __any_sync(0xffffffffu, f != 0) != 0;
-  __syncwarp();   // orders the stores before this warp's later reads of the scales
-  return any;
+__device__ __noinline__ void convert_scaled(DevOps ops, const TIO* u, GroupPairs gp, int tid, const float* en) {
+  const int j = tid / Energy<P, NT>::TPS;
+  convert_group<P, TIO, NB, NT>(ops, u, gp, tid, nullptr, row_in_scale<P, NT>(en, j >> 1, j & 1));
 }
 
 template <class P, class TIO, bool ACC16>
@@ -407,8 +378,11 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
   uint64_t* team_done = k_empty + 5;           // [NTEAM] a team's warps staged their outputs / copied them out
   volatile int* kstamp = reinterpret_cast<volatile int*>(team_done + SH::NTEAM);   // [2] group being staged
   volatile int* conv_done = kstamp + 2;        // groups whose input has been converted
-  volatile int* rep = conv_done + 1;           // [NS] the next stage request of a slot repeats the last stage
+  volatile int* rep = conv_done + 1;           // [NS] the slot's next MMA request repeats stage 0
   uint8_t* kstage = sm + SH::K_OFF;
+  // per slot and round parity: the group's energy slots, written by its team's conversion
+  float* energies = reinterpret_cast<float*>(sm + SH::EN_OFF);   // [NS][2][EN_STRIDE]
+  static_assert(Energy<P, SH::TWARPS * 32>::SLOTS == SH::EN_STRIDE, "energy area");
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int ni = (int)blockIdx.x < prm.ngroups ? (prm.ngroups - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x : 0;
@@ -500,7 +474,8 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
             ar_bits ^= 1u << s;
             tc_fence_after();
             SFFFT_STAMP(1, 3 * nmma + 1);
-            // a team that rescaled its group's input asks for stage 0 again (rep, set before its arrival)
+            // a team that converted its group again, rescaled, asks for stage 0 once more (rep, set before its
+            // arrival)
             const bool again = rep[s] != 0;
             if (again) rep[s] = 0;
             issue_any<P, ACC16, sizeof(TIO) == 4>((again ? done[s] - 1 : done[s]) % S2, ops,
@@ -594,9 +569,7 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
     // ---------------- compute warps ----------------
     // Team `team` (warps team*TWARPS .. of the compute warps) owns slots team*NST .. team*NST + NST - 1
     // and, round after round, runs the TPG tasks of its groups, alternating between its slots.
-    constexpr int NST = SH::NST, TWT = SH::TWARPS * 32, ENS = Energy<P>::SLOTS;
-    static_assert(Energy<P>::SLOTS + 4 * P::G == SH::EN_STRIDE, "energy area");
-    float* energies = reinterpret_cast<float*>(sm + SH::EN_OFF);   // [NS][2 parities][EN_STRIDE]
+    constexpr int NST = SH::NST, TWT = SH::TWARPS * 32;
     const int wc = warp - SH::CW0, team = wc / SH::TWARPS, wt = wc - team * SH::TWARPS;
     const int q = warp & 3, wi = wt >> 2, ttid = wt * 32 + lane;
     uint32_t md_bits = 0;                 // bit l: parity of local slot l's next mma_done phase
@@ -620,37 +593,37 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
         DevOps ops{sm + SH::DATA_OFF + s * P::DATA_BYTES, ACC16, tw_lo, tw_hi, P::N};
         if (lane == 0 && wt == 0) SFFFT_STAMP(2 + team, 3 * ntask);
         if (j == 0) {
-          // convert the group's input (measuring each row's energy) and hand it to the MMA warp at once; the
-          // team then agrees on the rows' scales while the stage-0 MMAs run.  A group with a row to rescale
-          // (rare: rows 2x apart in energy, or tiny) waits for those MMAs, converts again with the scales and
-          // asks the MMA warp to repeat stage 0 (pair_scales).
+          // convert the group's input, measuring each row's energy for the MMA warp, which derives the rows'
+          // scales while the stage-0 MMAs run (pair_scales)
           float* en = energies + (s * 2 + ((gi / NS) & 1)) * SH::EN_STRIDE;
-          convert_group<P, TIO, SH::NB, TWT>(ops, u, gp, ttid, en, en + ENS);
+          convert_group<P, TIO, SH::NB, TWT>(ops, u, gp, ttid, en, 1.f);
           if (lane == 0 && wt == 0) SFFFT_STAMP(2 + team, 3 * ntask + 1);
           fence_async_smem();
           tc_fence_before();
           if (!(prm.debug_skip_arrive == group + 1 && wt == 0)) warp_arrive(a_ready + s, lane);
           if (lane == 0 && wt == 0) atomicAdd((int*)conv_done, 1);
-          if (!team_sync(team_done + team, ts_phase, lane, abort_flag)) { ok = false; break; }
-          if (group_scales<P>(en, lane)) {
-            if (!wait_phase_all(mma_done + s, (md_bits >> l) & 1u, abort_flag)) { ok = false; break; }
-            md_bits ^= 1u << l;
-            tc_fence_after();
-            if (lane == 0 && wt == 0) rep[s] = 1;
-            convert_scaled<P, TIO, SH::NB, TWT>(ops, u, gp, ttid, en + ENS);
-            fence_async_smem();
-            tc_fence_before();
-            warp_arrive(a_ready + s, lane);
-          }
           if (lane == 0 && wt == 0) SFFFT_STAMP(2 + team, 3 * ntask + 2);
         } else {
           const int sid = j - 1;
           if (!wait_phase_all(mma_done + s, (md_bits >> l) & 1u, abort_flag)) { ok = false; break; }
           md_bits ^= 1u << l;
+          // stage 0 ran after every warp of the team had converted the group (each arrived on a_ready after
+          // storing its energy slots), so every warp now derives the same row scales into its own copy; a group
+          // with a row to rescale (rare) is converted again with them and stage 0 repeated
+          float* en = energies + (s * 2 + ((gi / NS) & 1)) * SH::EN_STRIDE;
+          if (sid == 0 && group_rescaled_warp<P, TWT>(en, lane)) {
+            tc_fence_after();
+            convert_scaled<P, TIO, SH::NB, TWT>(ops, u, gp, ttid, en);
+            if (lane == 0 && wt == 0) rep[s] = 1;
+            fence_async_smem();
+            tc_fence_before();
+            warp_arrive(a_ready + s, lane);
+            if (!wait_phase_all(mma_done + s, (md_bits >> l) & 1u, abort_flag)) { ok = false; break; }
+            md_bits ^= 1u << l;
+          }
           if (lane == 0 && wt == 0) SFFFT_STAMP(2 + team, 3 * ntask + 1);
           tc_fence_after();
-          EpiArgs ea{tmem + (uint32_t)(s * P::TMEM_COLS), prm.Kf, prm.y, prm.B, prm.H, group, nullptr, 0,
-                     energies + (s * 2 + ((gi / NS) & 1)) * SH::EN_STRIDE + ENS + 2 * P::G};
+          EpiArgs ea{tmem + (uint32_t)(s * P::TMEM_COLS), prm.Kf, prm.y, prm.B, prm.H, group, nullptr, 0, en};
           const bool kst = SH::KSLOT > 0 && sid == P::S - 1;
           constexpr int KS = SH::KSLOT > 0 ? SH::KSLOT : 1;
           const int ks = gi % KS;

@@ -149,11 +149,10 @@ struct Shape {
   static constexpr int NT = 32 * (WC + CW0);
   static constexpr int SEQB = P::L * SIO;                           // input bytes per sequence
   static constexpr int TW_BYTES = ((64 + P::N / 64) * 8 + 127) / 128 * 128;   // two-level twiddle table
-  // per slot and round parity: the conversion's energy slots of the group's 2G sequences, then the 2G input
-  // scales and the 2G output scales of pair_scales (floats)
-  static constexpr int EN_SEG = P::L / 8 < 32 ? P::L / 8 : 32;
-  static constexpr int EN_STRIDE = 2 * P::G * (P::L / (8 * EN_SEG)) + 4 * P::G;
-  static constexpr int EN_BYTES_MAX = (4 * 2 * EN_STRIDE * 4 + 127) / 128 * 128;   // for up to 4 slots
+  // per slot and round parity: the conversion's energy slots of the group's 2G sequences, one per warp of a
+  // sequence (at most max(2G, 2W) floats for any team size)
+  static constexpr int EN_STRIDE_MAX = 2 * P::G > 2 * P::W ? 2 * P::G : 2 * P::W;
+  static constexpr int EN_BYTES_MAX = (4 * 2 * EN_STRIDE_MAX * 4 + 127) / 128 * 128;   // for up to 4 slots
   static constexpr int CAP = 227 * 1024 - 1024 - 512 - TW_BYTES - EN_BYTES_MAX;   // dynamic smem minus align
                                                                                 // slack, barriers, energies
   static constexpr bool fits(int ns) {
@@ -191,6 +190,8 @@ struct Shape {
   static constexpr int TW_OFF = K_OFF + KBYTES;
   static constexpr int BAR_OFF = TW_OFF + TW_BYTES;
   static constexpr int EN_OFF = BAR_OFF + 512;
+  static constexpr int EN_STRIDE_RAW = 2 * P::G * ((TWARPS * 32 / (2 * P::G)) / 32 > 1 ? (TWARPS * 32 / (2 * P::G)) / 32 : 1);
+  static constexpr int EN_STRIDE = EN_STRIDE_RAW;
   static constexpr int EN_BYTES = (NS * 2 * EN_STRIDE * 4 + 127) / 128 * 128;
   static constexpr int SMEM = EN_OFF + EN_BYTES + 1024;
   static constexpr int TMEM_ALLOC = pow2ceil(cmax(32, NS * P::TMEM_COLS));

@@ -87,56 +87,58 @@ SF_HD PairInfo pair_info(int cta, int g, int G, int B, int H, int L) {
 // (|x| > 65504, possible in fp32 and bf16 input) become infinite in the hi plane and give inf / NaN
 // outputs, as the reference's fp16 conversion does.
 //
-// A group is converted in one or two passes (see pair_scales below):
-//   part != null  first pass: unscaled conversion that also records each sequence's energy: for every run
-//                 of 8 * SEG consecutive elements of one sequence (one step of SEG lanes of a warp) the sum
-//                 of squares, in part[e / (8 * SEG)] (e = element index within the group); the NSTEP steps
-//                 of a thread are NT * 8 elements apart
-//   part == null  second pass (only for groups that have a pair to rescale): every value of sequence j is
-//                 multiplied by the power of two psc[j] before the fp16 split.
+// A group's 2G sequences are split evenly over the team's NT threads: TPS = NT / 2G consecutive threads per
+// sequence, each taking 8 consecutive elements per step, so the steps of a thread stay inside one sequence
+// (a warp's step reads 256 consecutive elements, or 32 / TPS whole runs of 8 * TPS) and each thread sums its
+// sequence's energy in a register.  A group is converted in one or two passes (see pair_scales below):
+//   part != null  first pass: unscaled conversion that also records the energy (sum of squares) of every
+//                 sequence, one slot per warp of the sequence (Energy::SPS slots each)
+//   part == null  second pass (only for a group with a row to rescale): every value is multiplied by the
+//                 power of two `scale` of the thread's sequence before the fp16 split.
 // ---------------------------------------------------------------------------------------------
-template <class P>
+template <class P, int NT>
 struct Energy {
-  static constexpr int SEG = P::L / 8 < 32 ? P::L / 8 : 32;   // lanes whose 8-element runs share a sequence
-  static constexpr int SPS = P::L / (8 * SEG);                 // energy slots per sequence
-  static constexpr int SLOTS = 2 * P::G * SPS;
+  static constexpr int NSQ = 2 * P::G;              // sequences of a group
+  static constexpr int TPS = NT / NSQ;              // threads per sequence
+  static constexpr int SEG = TPS < 32 ? TPS : 32;   // lanes of a warp that share a sequence
+  static constexpr int SPS = TPS / SEG;             // energy slots per sequence (one per warp of it)
+  static constexpr int SLOTS = NSQ * SPS;
+  static constexpr int NSTEP = P::L / (8 * TPS);    // conversion steps of a thread
+  static_assert(NT % NSQ == 0 && P::L % (8 * TPS) == 0, "conversion split");
 };
 
 template <class P, class TIO, int NB, int NT, class Ops>
-SF_HD void convert_group(Ops& ops, const TIO* u, const GroupPairs& gp, int tid, float* part, const float* psc) {
-  constexpr int V0 = P::N / P::R0, MB0 = P::MB(0), NE = 2 * P::G * P::L, STRIDE = NT * 8, NSTEP = NE / STRIDE;
-  static_assert(NE % STRIDE == 0 && NSTEP <= Energy<P>::SEG, "conversion steps");
+SF_HD void convert_group(Ops& ops, const TIO* u, const GroupPairs& gp, int tid, float* part, float scale) {
+  using EN = Energy<P, NT>;
+  constexpr int V0 = P::N / P::R0, MB0 = P::MB(0), TPS = EN::TPS, NSTEP = EN::NSTEP;
+  const int j = tid / TPS, tl = tid - j * TPS, g = j >> 1, plane = j & 1;   // this thread's sequence
+  const PairInfo pi = gp.get(g, P::L);
+  const long long soff = plane == 0 ? pi.off0 : pi.off1;
   uint32_t w[NB][8];
-  int mrow[NB], krow[NB];
-  float ss[NSTEP];
-  // step i: elements tid * 8 + i * STRIDE .. + 7 (all steps lie below NE: tid * 8 < STRIDE)
+  int nb[NB];
+  // step i: elements n = tl * 8 + i * 8 * TPS .. + 7 of the sequence
   auto issue = [&](int b, int i) {
-    const int e = tid * 8 + i * STRIDE;
-    const int j = e / P::L, n = e - j * P::L, g = j >> 1, plane = j & 1;
-    const PairInfo pi = gp.get(g, P::L);
-    const long long off = plane == 0 ? pi.off0 : pi.off1;
-    const int n0 = n / V0, vv = n - n0 * V0;
-    mrow[b] = g * V0 + vv;
-    krow[b] = plane * P::R0 + n0;
-    if (off >= 0) ops.ldraw(u + off + n, w[b]);
+    const int n = tl * 8 + i * 8 * TPS;
+    nb[b] = n;
+    if (soff >= 0) ops.ldraw(u + soff + n, w[b]);
     else {
       for (int q = 0; q < 8; q++) w[b][q] = 0u;   // zero bits read as 0.0 in both formats
     }
   };
-  auto finish = [&](int b, int i) -> float {
+  float e2 = 0.f;
+  auto finish = [&](int b) {
     float v[8];
     ops.unpack(u, w[b], v);
-    float e2 = 0.f;
     if (part) {
       for (int q = 0; q < 8; q++) e2 += v[q] * v[q];
     } else {
-      const float s = psc[(tid * 8 + i * STRIDE) / P::L];
-      for (int q = 0; q < 8; q++) v[q] *= s;
+      for (int q = 0; q < 8; q++) v[q] *= scale;
     }
+    const int n0 = nb[b] / V0, vv = nb[b] - n0 * V0;
     uint32_t hi[4], lo[4];
     for (int q = 0; q < 4; q++) hi[q] = ops.pack2(v[2 * q], v[2 * q + 1]);
     // K-row k + R0/2 (the lo plane) is R0/16 K-groups further: same swizzle phase, since R0/2 % 8 == 0
-    const uint32_t off = mn_off(mrow[b], krow[b], MB0), off_lo = off + (uint32_t)(P::R0 / 16) * MB0 * 1024u;
+    const uint32_t off = mn_off(g * V0 + vv, plane * P::R0 + n0, MB0), off_lo = off + (uint32_t)(P::R0 / 16) * MB0 * 1024u;
     ops.st16(off, hi[0], hi[1], hi[2], hi[3]);
     if constexpr (sizeof(TIO) == 4) {
       for (int q = 0; q < 4; q++)
@@ -145,18 +147,23 @@ SF_HD void convert_group(Ops& ops, const TIO* u, const GroupPairs& gp, int tid, 
     } else if constexpr (P::R0 == 16) {
       ops.st16(off_lo, 0u, 0u, 0u, 0u);   // bf16 converts exactly: its lo plane is zero
     }
-    return e2;
   };
+  // A rolled loop: the kernel's code must stay small (its instruction cache is a limit), so the steps are not
+  // unrolled beyond the NB loads kept in flight.
 #pragma unroll
   for (int b = 0; b < NB; b++)
     if (b < NSTEP) issue(b, b);
+#pragma unroll 1
+  for (int i0 = 0; i0 < NSTEP; i0 += NB) {
 #pragma unroll
-  for (int i = 0; i < NSTEP; i++) {
-    ss[i] = finish(i % NB, i);
-    if (i + NB < NSTEP) issue(i % NB, i + NB);
+    for (int b = 0; b < NB; b++) {
+      if (i0 + b >= NSTEP) break;
+      finish(b);
+      if (i0 + b + NB < NSTEP) issue(b, i0 + b + NB);
+    }
   }
-  // the step energies of the SEG lanes that share a run of one sequence, summed once after the loads
-  if (part) ops.template energy_store<NSTEP, Energy<P>::SEG>(part, ss, tid, STRIDE);
+  // the sequence's energy over the SEG lanes of this warp that share it, one slot per warp of the sequence
+  if (part) ops.energy_store(part, j * EN::SPS + tl / EN::SEG, e2, EN::SEG);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -177,6 +184,15 @@ SF_HD void convert_group(Ops& ops, const TIO* u, const GroupPairs& gp, int tid, 
 // sum of squares underflows fp32 (|u| below ~1e-19) counts as all-zero; the reference's fp16 storage
 // flushes such values to zero as well.
 // ---------------------------------------------------------------------------------------------
+SF_HD float exp2i(int f) {   // 2^f exactly, |f| <= 126
+  union {
+    uint32_t u;
+    float x;
+  } c;
+  c.u = (uint32_t)(f + 127) << 23;
+  return c.x;
+}
+
 SF_HD int round_half_log2(float r) {   // round(log2(r) / 2), |result| <= 100
   float f = 0.5f * log2f(r);
   f = f > 100.f ? 100.f : (f < -100.f ? -100.f : f);
@@ -200,28 +216,50 @@ SF_HD void pair_exponents(float E0, float E1, int L, int* f0, int* f1) {
   *f1 = f[1] > 120 ? 120 : f[1];
 }
 
-// Scales of a group's 2G rows from the energy slots of its conversion: psc (input) and osc (output; 0 for an
-// all-zero row).  Returns whether any row is scaled.  (The kernel computes the same per lane in parallel.)
-template <class P>
-SF_HD bool pair_scales(const float* part, float* psc, float* osc) {
-  using EN = Energy<P>;
-  bool redo = false;
+// Energies of pair g's two rows from the group's energy slots.
+template <class P, int NT>
+SF_HD void pair_energies(const float* en, int g, float* E0, float* E1) {
+  using EN = Energy<P, NT>;
+  float e[2] = {0.f, 0.f};
+  for (int p = 0; p < 2; p++)
+    for (int i = 0; i < EN::SPS; i++) e[p] += en[(2 * g + p) * EN::SPS + i];
+  *E0 = e[0];
+  *E1 = e[1];
+}
+
+// Input scale of row p (0, 1) of pair g.
+template <class P, int NT>
+SF_HD float row_in_scale(const float* en, int g, int p) {
+  float E0, E1;
+  int f0, f1;
+  pair_energies<P, NT>(en, g, &E0, &E1);
+  pair_exponents(E0, E1, P::L, &f0, &f1);
+  return exp2i(p ? f1 : f0);
+}
+
+// Output scales of pair g's rows: the inverse powers of two, or 0 for an all-zero row.
+template <class P, int NT>
+SF_HD void pair_out_scales(const float* en, int g, float* o0, float* o1) {
+  float E0, E1;
+  int f0, f1;
+  pair_energies<P, NT>(en, g, &E0, &E1);
+  pair_exponents(E0, E1, P::L, &f0, &f1);
+  *o0 = E0 == 0.f ? 0.f : exp2i(-f0);
+  *o1 = E1 == 0.f ? 0.f : exp2i(-f1);
+}
+
+// Whether any row of the group is scaled (the kernel asks this per warp, lanes in parallel).
+template <class P, int NT>
+SF_HD bool group_rescaled(const float* en) {
+  bool any = false;
   for (int g = 0; g < P::G; g++) {
-    float E[2];
-    for (int p = 0; p < 2; p++) {
-      float s = 0.f;
-      for (int i = 0; i < EN::SPS; i++) s += part[(2 * g + p) * EN::SPS + i];
-      E[p] = s;
-    }
-    int f[2];
-    pair_exponents(E[0], E[1], P::L, &f[0], &f[1]);
-    for (int p = 0; p < 2; p++) {
-      psc[2 * g + p] = ldexpf(1.f, f[p]);
-      osc[2 * g + p] = E[p] == 0.f ? 0.f : ldexpf(1.f, -f[p]);
-      redo = redo || f[p] != 0;
-    }
+    float E0, E1;
+    int f0, f1;
+    pair_energies<P, NT>(en, g, &E0, &E1);
+    pair_exponents(E0, E1, P::L, &f0, &f1);
+    any = any || f0 != 0 || f1 != 0;
   }
-  return redo;
+  return any;
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -292,7 +330,7 @@ struct EpiArgs {
   int B, H, cta;        // cta: the group index (pairs cta*G .. cta*G + G - 1)
   const uint8_t* kst;   // spectrum rows of channels khf, khf+1, ... staged by the loader warp, or null
   int khf;
-  const float* osc;     // output multiplier of each of the group's 2G sequences (pair_scales)
+  const float* en;      // the group's energy slots (its rows' output scales follow from them, pair_scales)
 };
 
 // 1/sqrt(R): the per-stage scale of a radix-R digit (the reference's 1/sqrt(R) per stage, total 1/N).
@@ -420,7 +458,10 @@ SF_HD void epi_finish(Ops& ops, const EpiArgs& ea, const GroupPairs& gp, const E
 
   if constexpr (OUT) {
     // each row's scale undoes its input scaling (pair_scales): a power of two, or 0 for an all-zero row
-    const float s0 = SC * ea.osc[2 * g], s1 = SC * ea.osc[2 * g + 1];
+    float s0, s1;
+    pair_out_scales<P, Shape<P, (int)sizeof(TIO)>::TWARPS * 32>(ea.en, g, &s0, &s1);
+    s0 *= SC;
+    s1 *= SC;
     if constexpr (S == 2) {
       const PairInfo pi = gp.get(g, P::L);
       TIO* y = (TIO*)ea.y;
