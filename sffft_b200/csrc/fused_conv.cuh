@@ -310,16 +310,32 @@ __device__ __forceinline__ void epi_sid(DevOps& ops, const EpiArgs& ea, const Gr
 
 template <class P, class TIO, bool ACC16>
 __device__ void epi_any(int sid, DevOps& ops, const EpiArgs& ea, const GroupPairs& gp, int q, int wi, int lane) {
-  switch (sid) {
-    case 0: epi_sid<P, TIO, ACC16, 0>(ops, ea, gp, q, wi, lane); break;
-    case 1: epi_sid<P, TIO, ACC16, 1>(ops, ea, gp, q, wi, lane); break;
-    case 2: epi_sid<P, TIO, ACC16, 2>(ops, ea, gp, q, wi, lane); break;
-    case 3: epi_sid<P, TIO, ACC16, 3>(ops, ea, gp, q, wi, lane); break;
-    default:
-      if constexpr (P::S == 3) {
-        if (sid == 4) epi_sid<P, TIO, ACC16, 4>(ops, ea, gp, q, wi, lane);
-        else epi_sid<P, TIO, ACC16, 5>(ops, ea, gp, q, wi, lane);
-      }
+  if constexpr (!shared_twiddle<P, TIO>()) {
+    switch (sid) {
+      case 0: epi_sid<P, TIO, ACC16, 0>(ops, ea, gp, q, wi, lane); break;
+      case 1: epi_sid<P, TIO, ACC16, 1>(ops, ea, gp, q, wi, lane); break;
+      case 2: epi_sid<P, TIO, ACC16, 2>(ops, ea, gp, q, wi, lane); break;
+      case 3: epi_sid<P, TIO, ACC16, 3>(ops, ea, gp, q, wi, lane); break;
+      default:
+        if constexpr (P::S == 3) {
+          if (sid == 4) epi_sid<P, TIO, ACC16, 4>(ops, ea, gp, q, wi, lane);
+          else epi_sid<P, TIO, ACC16, 5>(ops, ea, gp, q, wi, lane);
+        }
+    }
+  } else if (sid == 2) {
+    epi_sid<P, TIO, ACC16, 2>(ops, ea, gp, q, wi, lane);
+  } else if (sid == 5) {
+    epi_sid<P, TIO, ACC16, 5>(ops, ea, gp, q, wi, lane);
+  } else {
+    // the four twiddle stages share one copy of the epilogue; the stage only selects its constants
+    TwParams tp;
+    switch (sid) {
+      case 0: tp = tw_params<P, 0>(); break;
+      case 1: tp = tw_params<P, 1>(); break;
+      case 3: tp = tw_params<P, (P::S == 3 ? 3 : 0)>(); break;
+      default: tp = tw_params<P, (P::S == 3 ? 4 : 0)>(); break;
+    }
+    twiddle_stage<P, TIO, ACC16>(ops, ea, tp, wi, q, lane);
   }
 }
 

@@ -569,12 +569,125 @@ SF_HD void epi_spec_shared(Ops& ops, const EpiArgs& ea, const GroupPairs& gp, in
   }
 }
 
+// ---------------------------------------------------------------------------------------------
+// Twiddle stages of 3-stage plans (every stage except the spectrum stage S - 1 and the output stage 2S - 1)
+// through one runtime-parameterized epilogue (see shared_twiddle): their four index maps differ only in
+// constants, so one copy of the code serves all of them (the kernel's warps hop between stages, and one copy
+// per stage costs instruction-cache misses).
+// With the pair-row index rr = hi * D + lo (lo < D):
+//   twiddle exponent of column col: (a1 hi + a2 lo) col + c hi lo
+//   next operand: M row g * MG + mh hi + ml lo + column, K row kh hi + kl lo
+// ---------------------------------------------------------------------------------------------
+struct TwParams {
+  int R, T, c_shift, rpp_shift, d_shift;   // radix, tiles, log2(16-column chunks), log2(rows per pair), log2(D)
+  int a1, a2, c, MG, mh, ml, kh, kl;
+  int MBn;                           // M blocks of the next stage's operand
+  uint32_t imoff;                    // byte distance of the next operand's imaginary K rows
+  float sc;                          // 1/sqrt(R)
+};
+
+SF_HD constexpr int ilog2(int v) { return v <= 1 ? 0 : 1 + ilog2(v / 2); }
+
+template <class P, int SID>
+SF_HD constexpr TwParams tw_params() {
+  constexpr int S = P::S, R = P::rad(SID), N = P::N;
+  TwParams t{};
+  t.R = R;
+  t.T = P::tiles(SID);
+  t.c_shift = ilog2(R / 16);
+  t.rpp_shift = ilog2(N / R);
+  t.MBn = P::MB(SID + 1);
+  t.imoff = (uint32_t)(P::rad(SID + 1) / 8) * (uint32_t)P::MB(SID + 1) * 1024u;
+  t.sc = stage_scale(R);
+  if (SID == 0 && S == 2) {             // rr = n1: exponent rr k0, operand (g R0 + k0, n1)
+    t.d_shift = 0; t.a1 = 1; t.MG = P::R0; t.kh = 1;
+  } else if (SID == 0) {                // rr = n1 R2 + n2: exponent rr k0, operand (g R0 R2 + n2 R0 + k0, n1)
+    t.d_shift = ilog2(P::R2); t.a1 = P::R2; t.a2 = 1; t.MG = P::R0 * P::R2; t.ml = P::R0; t.kh = 1;
+  } else if (SID == 1 && S == 3) {      // rr = n2 R0 + k0: exponent R0 n2 k1, operand (g R0 R1 + k0 R1 + k1, n2)
+    t.d_shift = ilog2(P::R0); t.a1 = P::R0; t.MG = P::R0 * P::R1; t.ml = P::R1; t.kh = 1;
+  } else if (SID == S && S == 2) {      // rr = k0: exponent -k0 k1, operand (g R1 + n1, k0)
+    t.d_shift = 0; t.a1 = -1; t.MG = P::R1; t.kh = 1;
+  } else if (SID == S) {                // rr = k0 R1 + k1: exponent -R0 k1 k2, operand (g R0 R2 + k0 R2 + n2, k1)
+    t.d_shift = ilog2(P::R1); t.a2 = -P::R0; t.MG = P::R0 * P::R2; t.mh = P::R2; t.kl = 1;
+  } else {                              // SID S + 1, rr = k0 R2 + n2: exponent -k0 (R2 n1 + n2), operand (g R1 R2 + n2 R1 + n1, k0)
+    t.d_shift = ilog2(P::R2); t.a1 = -P::R2; t.c = -1; t.MG = P::R1 * P::R2; t.ml = P::R1; t.kh = 1;
+  }
+  return t;
+}
+
+// NU units of a thread (units u0, u0 + ustride, ...) of a twiddle stage: TMEM loads of all of them first, then
+// the twiddle, rounding and the next stage's operand.
+template <class P, class TIO, bool ACC16, int NU, class Ops>
+SF_HD void twiddle_units(Ops& ops, const EpiArgs& ea, const TwParams& tp, int u0, int ustride, int q, int lane) {
+  uint32_t rre[NU][16], rim[NU][16];
+  int c0[NU], ta[NU], tb[NU], m0[NU], kre[NU];
+  for (int i = 0; i < NU; i++) {
+    const int u = u0 + i * ustride, t = u >> tp.c_shift, c = u - (t << tp.c_shift);
+    const int r = t * 128 + q * 32 + lane, g = r >> tp.rpp_shift, rr = r - (g << tp.rpp_shift);
+    const int hi = rr >> tp.d_shift, lo = rr - (hi << tp.d_shift);
+    c0[i] = 16 * c;
+    ta[i] = tp.a1 * hi + tp.a2 * lo;
+    tb[i] = tp.c * hi * lo;
+    m0[i] = g * tp.MG + tp.mh * hi + tp.ml * lo;
+    kre[i] = tp.kh * hi + tp.kl * lo;
+    const uint32_t taddr = ea.tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(t * 2 * tp.R + c0[i]);
+    ops.tmem_ld16(taddr, rre[i]);
+    ops.tmem_ld16(taddr + (uint32_t)tp.R, rim[i]);
+  }
+  ops.tmem_wait();
+  for (int i = 0; i < NU; i++) {
+    float a[16], b[16];
+    for (int j = 0; j < 16; j++) { a[j] = ops.acc_val(rre[i][j]); b[j] = ops.acc_val(rim[i][j]); }
+    float t0r, t0i, t8r, t8i, wr, wi;
+    ops.tw(ta[i] * c0[i] + tb[i], &t0r, &t0i);
+    ops.tw(ta[i] * (c0[i] + 8) + tb[i], &t8r, &t8i);
+    ops.tw(ta[i], &wr, &wi);
+    uint32_t pr[8], pim[8];
+    ops.twiddle16(a, b, t0r * tp.sc, t0i * tp.sc, t8r * tp.sc, t8i * tp.sc, wr, wi, pr, pim);
+    uint32_t o0, o1;
+    mn_off2(m0[i] + c0[i], kre[i], tp.MBn, &o0, &o1);
+    ops.st16(o0, pr[0], pr[1], pr[2], pr[3]);
+    ops.st16(o1, pr[4], pr[5], pr[6], pr[7]);
+    ops.st16(o0 + tp.imoff, pim[0], pim[1], pim[2], pim[3]);
+    ops.st16(o1 + tp.imoff, pim[4], pim[5], pim[6], pim[7]);
+  }
+}
+
+// Whether a plan's twiddle stages share one runtime-parameterized epilogue: 3-stage plans with one warp per
+// lane quarter in a team (several teams per CTA, each at a different stage); measured on B200: L = 4096
+// (32x16x16, four teams) 5 % faster, the 3-stage plans with two or four warps per quarter 1-3 % slower, the
+// 2-stage plans (two twiddle stages) unchanged or slower.
+template <class P, class TIO>
+SF_HD constexpr bool shared_twiddle() {
+  return P::S == 3 && Shape<P, (int)sizeof(TIO)>::NWQ == 1;
+}
+
+// A thread's share of a twiddle stage (see epi_warp for the unit order).
+template <class P, class TIO, bool ACC16, class Ops>
+SF_HD void twiddle_stage(Ops& ops, const EpiArgs& ea, const TwParams& tp, int wi, int q, int lane) {
+  constexpr int NWQ = Shape<P, (int)sizeof(TIO)>::NWQ;
+  constexpr int NU = (NWQ == 2 && P::W == 4) ? 2 : 1;
+  const int U = tp.T << tp.c_shift;
+  int u = wi;
+  if constexpr (NU == 2) {
+#pragma unroll 1
+    for (; u + NWQ < U; u += 2 * NWQ) twiddle_units<P, TIO, ACC16, 2>(ops, ea, tp, u, NWQ, q, lane);
+  }
+#pragma unroll 1
+  for (; u < U; u += NWQ) twiddle_units<P, TIO, ACC16, 1>(ops, ea, tp, u, NWQ, q, lane);
+}
+
 // The units of stage SID that one thread handles: its warp covers TMEM lane quarter q (warp % 4) and,
 // being warp wi of the team's NWQ warps on that quarter, units wi, wi + NWQ, ...  With two warps per
 // quarter on a 4-warp plan (registers to spare), units are taken in pairs so that two units' TMEM loads
 // are in flight together.
 template <class P, class TIO, bool ACC16, int SID, class Ops>
 SF_HD void epi_warp(Ops& ops, const EpiArgs& ea, const GroupPairs& gp, int wi, int q, int lane) {
+  if constexpr (shared_twiddle<P, TIO>() && SID != P::S - 1 && SID != 2 * P::S - 1) {
+    constexpr TwParams tp = tw_params<P, SID>();
+    twiddle_stage<P, TIO, ACC16>(ops, ea, tp, wi, q, lane);
+    return;
+  }
   constexpr int NWQ = Shape<P, (int)sizeof(TIO)>::NWQ;
   constexpr int C = epi_chunks<P, SID>(), U = P::tiles(SID) * C;
   constexpr bool SPEC = SID == P::S - 1;
