@@ -35,6 +35,7 @@ struct sffft_plan {
   int kio;              // I/O type of the fused kernel launches (fp32 for composite plans)
   cudaMemPool_t pool;   // composite plans: pool of the per-call workspaces (keeps its memory until destroy)
   int io, acc, kernel_mode, device, occupancy, smem_launch, sms;
+  int smem_small[2];     // launch shared memory of the 1- and 2-slot variants (0: not compiled for this plan)
   uint4* btab;   // cached DFT-matrix image (device), null in legacy mode
   int* status;   // device status word
 };
@@ -182,12 +183,24 @@ int sffft_plan_create(sffft_plan_t* out, int L, int io, int acc, const char* con
   const void* fn = e->func[kio][acc];
   if ((ce = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_launch)) != cudaSuccess)
     return cuda_fail(ce);
+  // the small-launch variants (fewer, wider teams) run launches with at most one or two groups per SM
+  int smem_small[2] = {0, 0};
+  for (int v = 0; v < 2; v++) {
+    if (!e->func_small[v][kio][acc]) continue;
+    int sm_v = e->smem_small[v][kio] < half ? half : e->smem_small[v][kio];
+    if (sm_v > (int)prop.sharedMemPerBlockOptin) sm_v = (int)prop.sharedMemPerBlockOptin;
+    if ((ce = cudaFuncSetAttribute(e->func_small[v][kio][acc], cudaFuncAttributeMaxDynamicSharedMemorySize, sm_v)) !=
+        cudaSuccess)
+      return cuda_fail(ce);
+    smem_small[v] = sm_v;
+  }
   const int occ = 1;
 
   sffft_plan* p = new sffft_plan();
   p->e = e; p->blocks = blocks; p->L = L; p->kio = kio;
   p->io = io; p->acc = acc; p->kernel_mode = kernel_mode; p->device = device;
   p->occupancy = occ; p->smem_launch = smem_launch; p->sms = prop.multiProcessorCount;
+  p->smem_small[0] = smem_small[0]; p->smem_small[1] = smem_small[1];
   p->btab = nullptr; p->status = nullptr; p->pool = nullptr;
   if ((ce = cudaMalloc(&p->status, sizeof(int))) != cudaSuccess || (ce = cudaMemset(p->status, 0, sizeof(int))) != cudaSuccess) {
     cudaFree(p->status);
@@ -385,7 +398,13 @@ static int conv_launch(sffft_plan_t p, const void* u, const void* Kf, void* y, i
 #ifdef SFFFT_TRACE
   prm.trace = g_trace;
 #endif
-  const cudaError_t ce = e->launch[p->kio][p->acc](prm, grid, p->smem_launch, stream);
+  // one or two groups per SM: the variant with as many (wider) teams as there are groups shortens each group's
+  // chain; otherwise the plan's own 4-slot kernel
+  const long long per_cta = (groups + p->sms - 1) / p->sms;
+  const int v = per_cta <= 1 ? 0 : (per_cta <= 2 ? 1 : -1);
+  const cudaError_t ce = (v >= 0 && p->smem_small[v])
+                             ? e->launch_small[v][p->kio][p->acc](prm, grid, p->smem_small[v], stream)
+                             : e->launch[p->kio][p->acc](prm, grid, p->smem_launch, stream);
   return ce == cudaSuccess ? SFFFT_OK : cuda_fail(ce);
 }
 

@@ -265,6 +265,20 @@ int run_plan(const void* u, const float* Kf, void* y, int B, int H) {
   return 0;
 }
 
+// A small-launch variant (fewer, wider teams) where its team splits the conversion evenly, else 2 (unknown).
+template <class Pl>
+int run_variant(int io, int acc, const void* u, const float* Kf, void* y, int B, int H) {
+  constexpr int NT = Shape<Pl, 4>::TWARPS * 32, NSQ = 2 * Pl::G;
+  if constexpr (NT % NSQ == 0 && Pl::L % (8 * (NT / NSQ)) == 0) {
+    if (io == 0 && acc == 0) return run_plan<Pl, float, false>(u, Kf, y, B, H);
+    if (io == 0 && acc == 1) return run_plan<Pl, float, true>(u, Kf, y, B, H);
+    if (io == 1 && acc == 0) return run_plan<Pl, uint16_t, false>(u, Kf, y, B, H);
+    return run_plan<Pl, uint16_t, true>(u, Kf, y, B, H);
+  } else {
+    return 2;
+  }
+}
+
 }  // namespace emu
 }  // namespace sffft
 
@@ -285,6 +299,18 @@ int sffft_emu_conv(const char* config, int io, int acc, const void* u, const flo
   }
   SFFFT_CATALOG(SF_EMU_CASE)
 #undef SF_EMU_CASE
+  // the small-launch variants of the default plans (1 or 2 slots, wider teams): "<name>@1", "<name>@2"
+#define SF_EMU_SMALL(R0, R1, R2, G, W, NAME)                                                                \
+  for (int v = 1; v <= 2; v++) {                                                                             \
+    if (std::string(config) != std::string(NAME) + "@" + std::to_string(v)) continue;                       \
+    if (v == 1) rc = emu::run_variant<Plan<R0, R1, R2, G, W, 1>>(io, acc, u, Kf, y, B, H);                  \
+    else rc = emu::run_variant<Plan<R0, R1, R2, G, W, 2>>(io, acc, u, Kf, y, B, H);                         \
+  }
+  SF_EMU_SMALL(16, 16, 1, 8, 8, "16x16/w8") SF_EMU_SMALL(32, 16, 1, 8, 8, "32x16/w8")
+  SF_EMU_SMALL(32, 32, 1, 4, 8, "32x32/w8") SF_EMU_SMALL(64, 32, 1, 4, 8, "64x32/w8")
+  SF_EMU_SMALL(64, 64, 1, 2, 8, "64x64/w8") SF_EMU_SMALL(32, 16, 16, 1, 8, "32x16x16/w8")
+  SF_EMU_SMALL(32, 32, 16, 1, 8, "32x32x16/w8")
+#undef SF_EMU_SMALL
   } catch (const std::exception&) {
     return 3;
   }

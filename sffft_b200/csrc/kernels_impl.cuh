@@ -36,7 +36,51 @@ ConvEntry make_entry(const char* name) {
   e.func[1][0] = (const void*)&fused_conv_kernel<P, __nv_bfloat16, false>;
   e.func[1][1] = (const void*)&fused_conv_kernel<P, __nv_bfloat16, true>;
   e.build_bmat = &hostmath::build_bmat_image<P>;
+  for (int v = 0; v < 2; v++)
+    for (int io = 0; io < 2; io++) {
+      e.smem_small[v][io] = 0;
+      for (int a = 0; a < 2; a++) {
+        e.launch_small[v][io][a] = nullptr;
+        e.func_small[v][io][a] = nullptr;
+      }
+    }
   return e;
+}
+
+// Adds the v-slot variant (v = 1 or 2) of plan P to its entry, where its team splits the conversion evenly (a
+// team of 16 warps has more threads than the 8-element runs of the smallest groups).
+template <class P, int V>
+void add_small_variant(ConvEntry& e) {
+  using PV = Plan<P::R0, P::R1, P::R2, P::G, P::W, V>;
+  constexpr int NT = Shape<PV, 4>::TWARPS * 32, NSQ = 2 * P::G;
+  if constexpr (NT % NSQ == 0 && P::L % (8 * (NT / NSQ)) == 0) {
+    const int i = V == 1 ? 0 : 1;
+    e.smem_small[i][0] = Shape<PV, 4>::SMEM;
+    e.smem_small[i][1] = Shape<PV, 2>::SMEM;
+    e.launch_small[i][0][0] = &launch_conv<PV, float, false>;
+    e.launch_small[i][0][1] = &launch_conv<PV, float, true>;
+    e.launch_small[i][1][0] = &launch_conv<PV, __nv_bfloat16, false>;
+    e.launch_small[i][1][1] = &launch_conv<PV, __nv_bfloat16, true>;
+    e.func_small[i][0][0] = (const void*)&fused_conv_kernel<PV, float, false>;
+    e.func_small[i][0][1] = (const void*)&fused_conv_kernel<PV, float, true>;
+    e.func_small[i][1][0] = (const void*)&fused_conv_kernel<PV, __nv_bfloat16, false>;
+    e.func_small[i][1][1] = (const void*)&fused_conv_kernel<PV, __nv_bfloat16, true>;
+  }
+}
+
+template <class P>
+void add_small_variants(ConvEntry& e) {
+  add_small_variant<P, 1>(e);
+  add_small_variant<P, 2>(e);
+}
+
+// The plans with small-launch variants: the built-in default plan of each length up to 8192 (the 16384 plan
+// already has one slot).
+constexpr bool small_variants(int R0, int R1, int R2, int W) {
+  return W == 8 && ((R0 == 16 && R1 == 16 && R2 == 1) || (R0 == 32 && R1 == 16 && R2 == 1) ||
+                    (R0 == 32 && R1 == 32 && R2 == 1) || (R0 == 64 && R1 == 32 && R2 == 1) ||
+                    (R0 == 64 && R1 == 64 && R2 == 1) || (R0 == 32 && R1 == 16 && R2 == 16) ||
+                    (R0 == 32 && R1 == 32 && R2 == 16));
 }
 
 template <int NMIN, int NMAX>
@@ -45,6 +89,7 @@ std::vector<ConvEntry> collect_entries() {
 #define SF_COLLECT(R0, R1, R2, G, W, NAME)                                              \
   if constexpr (R0 * R1 * R2 >= NMIN && R0 * R1 * R2 <= NMAX) {                        \
     v.push_back(make_entry<Plan<R0, R1, R2, G, W>>(NAME));                              \
+    if constexpr (small_variants(R0, R1, R2, W)) add_small_variants<Plan<R0, R1, R2, G, W>>(v.back()); \
   }
   SFFFT_CATALOG(SF_COLLECT)
 #undef SF_COLLECT

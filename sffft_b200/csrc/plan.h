@@ -71,9 +71,11 @@ SF_HD constexpr uint32_t make_idesc(int M, int N, bool d_f32, bool a_mn, bool b_
 // ---------------------------------------------------------------------------------------------
 // Plan
 // ---------------------------------------------------------------------------------------------
-template <int R0_, int R1_, int R2_, int G_, int W_>
+// MS_: the most group slots (and teams) per CTA.  The catalog plans use 4; small launches, with at most one
+// or two groups per SM, run variants with 1 or 2 slots whose teams are 4x or 2x wider (shorter chains).
+template <int R0_, int R1_, int R2_, int G_, int W_, int MS_ = 4>
 struct Plan {
-  static constexpr int R0 = R0_, R1 = R1_, R2 = R2_, G = G_, W = W_;
+  static constexpr int R0 = R0_, R1 = R1_, R2 = R2_, G = G_, W = W_, MS = MS_;
   static constexpr int S = R2_ > 1 ? 3 : 2;
   static constexpr int N = R0 * R1 * R2, L = N / 2, NT = 32 * W;
   static constexpr int RL = S == 3 ? R2 : R1;          // radix of the last (contiguous) digit
@@ -158,7 +160,8 @@ struct Shape {
   static constexpr bool fits(int ns) {
     return ns * P::TMEM_COLS <= 512 && P::BMAT_BYTES + ns * P::DATA_BYTES <= CAP;
   }
-  static constexpr int NSMAX = WC / 4 < SFFFT_MAX_SLOTS ? WC / 4 : SFFFT_MAX_SLOTS;
+  static constexpr int SLOTCAP = SFFFT_MAX_SLOTS < P::MS ? SFFFT_MAX_SLOTS : P::MS;
+  static constexpr int NSMAX = WC / 4 < SLOTCAP ? WC / 4 : SLOTCAP;
   static constexpr int NS = (NSMAX >= 4 && fits(4)) ? 4 : ((NSMAX >= 2 && fits(2)) ? 2 : 1);
   static constexpr int NSLOT = NS;
   static constexpr int TMAXW = WC / 4 < SFFFT_MAX_TEAMS ? WC / 4 : SFFFT_MAX_TEAMS;

@@ -14,6 +14,11 @@ struct ConvEntry {
   int smem_bytes[2], tmem_cols[2], slots[2], kslots[2];   // per I/O type (fp32, bf16)
   ConvLaunchFn launch[2][2];   // [io: 0 fp32, 1 bf16][acc: 0 fp32, 1 fp16]
   const void* func[2][2];      // kernel function pointers (attributes, occupancy)
+  // small-launch variants with 1 and 2 slots ([0]: 1 slot, [1]: 2 slots; null where not compiled), for launches
+  // with at most one or two groups per SM
+  ConvLaunchFn launch_small[2][2][2];
+  const void* func_small[2][2][2];
+  int smem_small[2][2];        // [variant][io]
   void (*build_bmat)(uint8_t* img);   // host builder of the cached DFT-matrix image
 };
 

@@ -12,7 +12,7 @@ TOL = {("fp32", "fp32"): 5e-4, ("bf16", "fp32"): 3e-3, ("fp32", "fp16"): 1e-3, (
 
 
 def radices(name):
-    return [int(x) for x in name.split("/")[0].split("x")]
+    return [int(x) for x in name.split("@")[0].split("/")[0].split("x")]
 
 
 def run_case(oracle, name, B, H, io="fp32", acc="fp32", seed=0):
@@ -101,3 +101,15 @@ def test_pairs_of_very_different_scale(oracle, name, io, acc):
     assert errs.shape == (len(PAIR_SCALES), 2)
     assert np.all(errs <= TOL[(io, acc)]), errs
     assert not y[4].any()
+
+
+SMALL_VARIANTS = [f"{n}@{v}" for n in ["16x16/w8", "32x16/w8", "32x32/w8", "64x32/w8", "64x64/w8", "32x16x16/w8"]
+                  for v in (1, 2) if not (n == "16x16/w8" and v == 1)]
+
+
+@pytest.mark.parametrize("name", SMALL_VARIANTS)
+def test_small_launch_variants(oracle, name):
+    # the 1- and 2-slot variants of the default plans (wider teams), used for launches with at most one or two
+    # groups per SM
+    assert run_case(oracle, name, 4, 3) <= TOL[("fp32", "fp32")]
+    assert run_case(oracle, name, 2, 1, io="bf16", acc="fp16") <= TOL[("bf16", "fp16")]
