@@ -455,6 +455,8 @@ def main():
                        "vs_baseline_ref": "reference GB10 published ms/batch (README.md:29-35)" if pub else None},
             "roofline": {"bound": bound, "achieved": round(achieved, 2), "peak": peak, "unit": unit,
                          "frac": round(frac, 4), "traffic": traffic,
+                         "traffic_source": "ncu, one launch: dram__bytes_read.sum + lts__t_sectors_srcunit_tex_op_write.sum"
+                                           " x 32 B (stores = y's write-back) (profiles/traffic.json)" if traffic else None,
                          "peak_source": f"{src} (MEASURED_PEAKS.json)" if src == "measured" else src,
                          "algorithmic_bytes": alg_bytes, "algorithmic_flops": alg_flops, "t_roof_ms": round(t_roof, 5)},
             "e2e": {"value": round(e2e_step, 5), "unit": UNIT, "h2d_bytes_per_step": nbytes,
