@@ -42,7 +42,8 @@ L2_BYTES = 126e6
 NAMED_CONFIGS = {(1, 1, 128, "fp32", "fp32"): "configs[0]", (8, 768, 1024, "fp32", "fp32"): "configs[1]",
                  (8, 768, 4096, "bf16", "fp32"): "configs[2]", (8, 768, 8192, "bf16", "fp16"): "configs[3]",
                  (16, 1024, 16384, "fp32", "fp32"): "configs[4]"}
-SWEEP_EXTRA = [(8, 768, 4096, "bf16", "fp32"), (8, 768, 8192, "bf16", "fp16"), (16, 1024, 16384, "fp32", "fp32")]
+SWEEP_EXTRA = [(8, 768, 4096, "bf16", "fp32"), (8, 768, 8192, "bf16", "fp16"), (16, 1024, 16384, "fp32", "fp32"),
+               (8, 768, 65536, "fp32", "fp32")]   # the last: a composite plan (partitioned convolution, 4 blocks)
 
 
 def peaks():
@@ -327,7 +328,8 @@ def run_sweep(torch, sf, dev, local, steps, warmup):
         except Exception as exc:   # reported, not fatal: the sweep's fused numbers stand on their own
             cms = None
             print(f"cuFFT pipeline failed at L={L}: {exc}", file=sys.stderr)
-        out.append({"config": NAMED_CONFIGS.get((B, H, L, io, acc), "sweep"), "B": B, "H": H, "L": L, "io": io,
+        label = NAMED_CONFIGS.get((B, H, L, io, acc), "composite" if wl.plan.blocks > 1 else "sweep")
+        out.append({"config": label, "B": B, "H": H, "L": L, "io": io,
                     "acc": acc, "plan": wl.plan.config, "ms": round(ms, 5), "bound": bound,
                     "achieved": round(achieved, 2), "unit": unit, "frac": round(frac, 4),
                     "cufft_ms": round(cms, 5) if cms else None,

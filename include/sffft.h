@@ -33,6 +33,7 @@ extern "C" {
 #define SFFFT_ERR_NO_MATCH 6
 #define SFFFT_ERR_ALLOC 7
 #define SFFFT_ERR_SCRATCH_LIMIT 8 /* problem too large for sffft_conv_noalloc's fixed scratch */
+#define SFFFT_ERR_WORKSPACE 9     /* composite plan called without a large enough workspace */
 
 #define SFFFT_IO_FP32 0
 #define SFFFT_IO_BF16 1
@@ -56,12 +57,14 @@ typedef struct {
  * NULL / "" for the built-in B200 default for L.  Replaces the compile-time choice of fftconv<Plan<R0,R1,R2>,
  * W,TIO,TAcc,CACHED> plus its cudaFuncSetAttribute / occupancy setup (src/sffft.cu:243-245, 385-388).
  * Composite plans (no reference counterpart; the reference stops at L = 8192 and lists multi-pass plans
- * as missing, README.md:175): config "<P>x[<catalog name>]" runs L = P * Lb (P = 2..16) as a block
- * convolution on the catalog plan of length Lb, and the default for L = 32768 .. 262144 is
- * "<L/16384>x[<default for 16384>]".  For a composite plan Kf holds the P block spectra [P][H][2 Lb]
- * (the same H * 2L complex values), filter layouts other than causal are unsupported, and sffft_conv
- * takes a stream-ordered workspace of (P + P (P + 1) / 2) * B * H * Lb fp32 elements for the call from a
- * memory pool the plan owns (the pool keeps the largest workspace mapped until sffft_plan_destroy). */
+ * as missing, README.md:175): config "<P>x[<catalog name>]" runs L = P * Lb (P = 2..16) as a partitioned
+ * convolution on the catalog plan of length Lb (a forward transform per input block, then per output block
+ * the sum of block spectra times filter-segment spectra and one inverse transform; block plans: the default
+ * plan of each length up to 16384, and 16x16/w4), and the default for L = 32768 .. 262144 is
+ * "<L/16384>x[<default for 16384>]".  For a composite plan Kf holds the P filter-segment spectra
+ * [P][H][2 Lb] (the same H * 2L complex values), filter layouts other than causal are unsupported, and the
+ * convolution needs a caller-owned workspace (sffft_conv_workspace_bytes): passed to sffft_conv_ws, or
+ * attached to the plan for sffft_conv with sffft_plan_set_workspace. */
 int sffft_plan_create(sffft_plan_t* plan, int L, int io, int acc, const char* config, int kernel_mode, int device);
 int sffft_plan_destroy(sffft_plan_t plan);
 int sffft_plan_info(sffft_plan_t plan, sffft_plan_info_t* info);
@@ -99,6 +102,19 @@ int sffft_irfft(sffft_plan_t plan, const void* X, int B, float* x, void* work, v
  * fftconv<P,W,TIO,TAcc,CACHED><<<B*H, 32*W, smem>>>(u, Kf, tw, dft, y, B, H) (src/sffft.cu:243-280,
  * 389-390); the unused twiddle table and the DFT table are owned by the plan. */
 int sffft_conv(sffft_plan_t plan, const void* u, const void* Kf, void* y, int B, int H, void* stream);
+
+/* Workspace of a composite plan's convolution of a B x H batch, in bytes: the forward spectra of every
+ * input block (ceil(B/2) * H * L * 16 bytes) and the row energies; 0 for single-pass plans. */
+int sffft_conv_workspace_bytes(sffft_plan_t plan, int B, int H, size_t* bytes);
+/* sffft_conv with a caller-owned device workspace (256-byte aligned, at least sffft_conv_workspace_bytes;
+ * NULL for single-pass plans).  A composite call is three launches in stream order (row energies, forward
+ * transforms, spectrum sums with inverse transforms); the workspace must not be shared by calls that can
+ * overlap.  Returns SFFFT_ERR_WORKSPACE when a composite plan gets no workspace or too small a one. */
+int sffft_conv_ws(sffft_plan_t plan, const void* u, const void* Kf, void* y, int B, int H, void* work,
+                  size_t work_bytes, void* stream);
+/* Attaches a caller-owned workspace (256-byte aligned; NULL detaches) that sffft_conv uses for composite
+ * plans, which otherwise return SFFFT_ERR_WORKSPACE.  The plan does not free it. */
+int sffft_plan_set_workspace(sffft_plan_t plan, void* work, size_t bytes);
 
 /* Waits for the plan's device and returns (and clears) the device-side status word: SFFFT_OK, or
  * SFFFT_ERR_TIMEOUT when a kernel barrier wait gave up.  No reference counterpart (the reference has no

@@ -19,7 +19,8 @@ LIB_PATH = os.path.join(_HERE, "lib", "libsffft.so")
 EMU_PATH = os.path.join(_HERE, "lib", "libsffft_emu.so")
 CLI_PATH = os.path.join(_HERE, "bin", "sffft")
 
-OK, ERR_INVALID_ARGUMENT, ERR_UNSUPPORTED, ERR_CUDA, ERR_DEVICE, ERR_TIMEOUT, ERR_NO_MATCH, ERR_ALLOC = range(8)
+(OK, ERR_INVALID_ARGUMENT, ERR_UNSUPPORTED, ERR_CUDA, ERR_DEVICE, ERR_TIMEOUT, ERR_NO_MATCH, ERR_ALLOC,
+ ERR_SCRATCH_LIMIT, ERR_WORKSPACE) = range(10)
 IO = {"fp32": 0, "bf16": 1}
 ACC = {"fp32": 0, "fp16": 1}
 KERNEL = {"legacy": 0, "cached": 1}
@@ -58,6 +59,9 @@ def _declare(lib):
         "sffft_rfft": (I, [P, V, I, I, V, V, V]),
         "sffft_irfft": (I, [P, V, I, V, V, V]),
         "sffft_conv": (I, [P, V, V, V, I, I, V]),
+        "sffft_conv_workspace_bytes": (I, [P, I, I, ctypes.POINTER(ctypes.c_size_t)]),
+        "sffft_conv_ws": (I, [P, V, V, V, I, I, V, ctypes.c_size_t, V]),
+        "sffft_plan_set_workspace": (I, [P, V, ctypes.c_size_t]),
         "sffft_plan_check": (I, [P]),
         "sffft_catalog_count": (I, []),
         "sffft_catalog_entry": (I, [I, ctypes.POINTER(I), ctypes.c_char_p, I]),
@@ -198,6 +202,7 @@ class Plan:
         # digits of the length-N transform; a composite plan's last digit spans its blocks
         self.radices = [r for r in (inf.R0, inf.R1, inf.R2) if r > 1]
         self.radices[-1] *= self.blocks
+        self._ws = None   # composite plans: the workspace of conv (a device byte tensor, grown on demand)
 
     def filter_spectrum(self, k, Kf=None, stream=None, layout="causal"):
         """Kf [H][N] complex fp32 (as float32 [H, N, 2]) in digit order from the filter k.
@@ -256,20 +261,44 @@ class Plan:
         _check(lib().sffft_irfft(self._h, _ptr(X), rows, _ptr(x), _ptr(work), _stream(stream)), "irfft")
         return x
 
-    def conv(self, u, Kf, y=None, stream=None):
-        """y = causal_conv(u, k) for u [B][H][L] with the spectrum Kf of k."""
+    def workspace_bytes(self, B: int, H: int) -> int:
+        """Device workspace of a B x H convolution (sffft_conv_workspace_bytes): 0 for single-pass plans."""
+        need = ctypes.c_size_t()
+        _check(lib().sffft_conv_workspace_bytes(self._h, B, H, ctypes.byref(need)), "conv_workspace_bytes")
+        return need.value
+
+    def _work(self, B, H, work):
+        need = self.workspace_bytes(B, H)
+        if need == 0:
+            return None, 0
+        if work is not None:
+            nbytes = work.numel() * work.element_size()
+            if nbytes < need:
+                raise ValueError(f"workspace of {need} bytes needed, got {nbytes}")
+            return work.data_ptr(), nbytes
+        import torch
+        if self._ws is None or self._ws.numel() < need:
+            self._ws = None
+            self._ws = torch.empty(need, dtype=torch.uint8, device=torch.device("cuda", self.device))
+        return self._ws.data_ptr(), self._ws.numel()
+
+    def conv(self, u, Kf, y=None, stream=None, work=None):
+        """y = causal_conv(u, k) for u [B][H][L] with the spectrum Kf of k.  Composite plans use `work` (a device
+        tensor of at least workspace_bytes(B, H) bytes) or a workspace the plan keeps for its calls."""
         import torch
         B, H, L = u.shape
         if L != self.L:
             raise ValueError(f"plan is for L={self.L}, got {L}")
         if y is None:
             y = torch.empty_like(u)
-        _check(lib().sffft_conv(self._h, _ptr(u), _ptr(Kf), _ptr(y), B, H, _stream(stream)), "conv")
+        wp, wn = self._work(B, H, work)
+        _check(lib().sffft_conv_ws(self._h, _ptr(u), _ptr(Kf), _ptr(y), B, H, wp, wn, _stream(stream)), "conv")
         return y
 
     def conv_ptr(self, u_ptr: int, Kf_ptr: int, y_ptr: int, B: int, H: int, stream=None) -> int:
         """Raw-pointer form; returns the status instead of raising (for tight timing loops)."""
-        return lib().sffft_conv(self._h, u_ptr, Kf_ptr, y_ptr, B, H, _stream(stream))
+        wp, wn = self._work(B, H, None) if self.blocks > 1 else (None, 0)
+        return lib().sffft_conv_ws(self._h, u_ptr, Kf_ptr, y_ptr, B, H, wp, wn, _stream(stream))
 
     def check(self):
         """Synchronise and raise if a kernel reported a device-side error."""
@@ -398,10 +427,7 @@ def umma_probe(a_kind: int, a_slice: int, b_pitch: int, b_slice: int, A, Bm, acc
     return D
 
 
-def emu_conv(config: str, u, Kf, io: str = "fp32", acc: str = "fp32"):
-    """CPU emulation of the fused kernel (same stage code, emulated tcgen05); numpy in and out.
-    Test infrastructure for checking layouts without a GPU."""
-    import numpy as np
+def _emu_lib():
     global _emu
     if _emu is None:
         if not os.path.exists(EMU_PATH):
@@ -409,11 +435,38 @@ def emu_conv(config: str, u, Kf, io: str = "fp32", acc: str = "fp32"):
         _emu = ctypes.CDLL(EMU_PATH)
         _emu.sffft_emu_conv.argtypes = [ctypes.c_char_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
                                         ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int]
+        _emu.sffft_emu_conv_composite.argtypes = [ctypes.c_char_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                                  ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
+                                                  ctypes.c_int]
+    return _emu
+
+
+def emu_conv_composite(config: str, P: int, u, Kf, io: str = "fp32", acc: str = "fp32"):
+    """CPU emulation of the composite plan "<P>x[<config>]" (row energies, forward and inverse launches of the
+    partitioned convolution); Kf: the P filter-segment spectra [P][H][N] (float32 pairs).  Test infrastructure."""
+    import numpy as np
     B, H, L = u.shape
     u = np.ascontiguousarray(u)
     Kf = np.ascontiguousarray(Kf, dtype=np.float32)
     y = np.zeros_like(u)
-    rc = _emu.sffft_emu_conv(config.encode(), IO[io], ACC[acc], u.ctypes.data, Kf.ctypes.data, y.ctypes.data, B, H)
+    rc = _emu_lib().sffft_emu_conv_composite(config.encode(), P, IO[io], ACC[acc], u.ctypes.data, Kf.ctypes.data,
+                                             y.ctypes.data, B, H)
+    if rc == 3:
+        raise RuntimeError(f"emulated kernel accessed memory out of range ({P}x[{config}])")
+    if rc:
+        raise ValueError(f"no partitioned-convolution kernels for {config}")
+    return y
+
+
+def emu_conv(config: str, u, Kf, io: str = "fp32", acc: str = "fp32"):
+    """CPU emulation of the fused kernel (same stage code, emulated tcgen05); numpy in and out.
+    Test infrastructure for checking layouts without a GPU."""
+    import numpy as np
+    B, H, L = u.shape
+    u = np.ascontiguousarray(u)
+    Kf = np.ascontiguousarray(Kf, dtype=np.float32)
+    y = np.zeros_like(u)
+    rc = _emu_lib().sffft_emu_conv(config.encode(), IO[io], ACC[acc], u.ctypes.data, Kf.ctypes.data, y.ctypes.data, B, H)
     if rc == 3:
         raise RuntimeError(f"emulated kernel accessed shared memory or TMEM out of range ({config})")
     if rc:

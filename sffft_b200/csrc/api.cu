@@ -30,10 +30,12 @@ int wait_timeout_probe(int limit_us);
 using namespace sffft;
 
 struct sffft_plan {
-  const ConvEntry* e;   // the fused kernel's plan (the block plan of a composite plan)
-  int blocks, L;        // composite plans: L = blocks * e->L (blocks = 1: the plan itself)
-  int kio;              // I/O type of the fused kernel launches (fp32 for composite plans)
-  cudaMemPool_t pool;   // composite plans: pool of the per-call workspaces (keeps its memory until destroy)
+  const ConvEntry* e;    // the fused kernel's plan (the block plan of a composite plan)
+  int blocks, L;         // composite plans: L = blocks * e->L (blocks = 1: the plan itself)
+  int kio;               // I/O type of the fused kernel launches
+  const BlockEntry* be;  // composite plans: the partitioned-convolution kernels of the block plan
+  void* work;            // composite plans: workspace attached by sffft_plan_set_workspace (caller-owned)
+  size_t work_bytes;
   int io, acc, kernel_mode, device, occupancy, smem_launch, sms;
   int smem_small[2];     // launch shared memory of the 1- and 2-slot variants (0: not compiled for this plan)
   uint4* btab;   // cached DFT-matrix image (device), null in legacy mode
@@ -51,6 +53,21 @@ extern "C" void sffft_debug_set_trace(void* buf) { g_trace = (unsigned long long
 static int cuda_fail(cudaError_t e) {
   g_last_cuda = (int)e;
   return SFFFT_ERR_CUDA;
+}
+
+static const BlockEntry* block_entry(const char* name) {
+  static const std::vector<const BlockEntry*> all = [] {
+    std::vector<const BlockEntry*> v;
+    const BlockEntry* p;
+    int n = block_entries_2stage(&p);
+    for (int i = 0; i < n; i++) v.push_back(p + i);
+    n = block_entries_3stage(&p);
+    for (int i = 0; i < n; i++) v.push_back(p + i);
+    return v;
+  }();
+  for (const BlockEntry* b : all)
+    if (std::strcmp(b->name, name) == 0) return b;
+  return nullptr;
 }
 
 static const std::vector<const ConvEntry*>& catalog() {
@@ -71,8 +88,9 @@ static const std::vector<const ConvEntry*>& catalog() {
 // Built-in B200 default per length: the fastest catalog entry of the plan the benchmark configurations name for
 // that length (B = 8, H = 768, fp32 and bf16 I/O, timed on one B200); the CLI's empirical selector can
 // override it from its own measurements.
-// Composite plans: lengths above the largest single-kernel plan run as block convolutions of up to
-// kMaxBlocks blocks (the work grows as blocks * (blocks + 1) / 2 block convolutions).
+// Composite plans: lengths above the largest single-kernel plan run as partitioned convolutions of up to
+// kMaxBlocks blocks (a forward transform per input block, a spectrum sum and an inverse transform per output
+// block; the sums read blocks * (blocks + 1) / 2 block spectra).
 constexpr int kMaxBlockL = 16384, kMaxBlocks = 16;
 
 static const char* default_for(int L) {
@@ -109,6 +127,7 @@ const char* sffft_status_string(int s) {
     case SFFFT_ERR_NO_MATCH: return "no candidate meets the error budget";
     case SFFFT_ERR_ALLOC: return "device allocation failed";
     case SFFFT_ERR_SCRATCH_LIMIT: return "problem exceeds the fixed scratch of the allocation-free entry point";
+    case SFFFT_ERR_WORKSPACE: return "composite plan needs a workspace of sffft_conv_workspace_bytes";
     default: return "unknown status";
   }
 }
@@ -161,6 +180,8 @@ int sffft_plan_create(sffft_plan_t* out, int L, int io, int acc, const char* con
   for (const ConvEntry* c : catalog())
     if (want == c->name) e = c;
   if (!e || (long long)e->L * blocks != L) return SFFFT_ERR_UNSUPPORTED;
+  const BlockEntry* be = blocks > 1 ? block_entry(e->name) : nullptr;
+  if (blocks > 1 && !be) return SFFFT_ERR_UNSUPPORTED;   // block plan without partitioned-convolution kernels
 
   int ndev = 0;
   cudaError_t ce = cudaGetDeviceCount(&ndev);
@@ -169,8 +190,7 @@ int sffft_plan_create(sffft_plan_t* out, int L, int io, int acc, const char* con
   if ((ce = cudaSetDevice(device)) != cudaSuccess) return cuda_fail(ce);
   cudaDeviceProp prop;
   if ((ce = cudaGetDeviceProperties(&prop, device)) != cudaSuccess) return cuda_fail(ce);
-  // a composite plan runs its blocks through the block plan's fp32-I/O kernel (fp32 partial sums)
-  const int kio = blocks > 1 ? SFFFT_IO_FP32 : io;
+  const int kio = io;
   const int need = e->smem_bytes[kio];
   if (prop.major != 10 || prop.minor != 0 || (int)prop.sharedMemPerBlockOptin < need) return SFFFT_ERR_DEVICE;
 
@@ -183,6 +203,10 @@ int sffft_plan_create(sffft_plan_t* out, int L, int io, int acc, const char* con
   const void* fn = e->func[kio][acc];
   if ((ce = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_launch)) != cudaSuccess)
     return cuda_fail(ce);
+  for (int m = 0; be && m < 2; m++)   // the forward and inverse kernels have the block plan's shared memory
+    if ((ce = cudaFuncSetAttribute(be->func[m][kio][acc], cudaFuncAttributeMaxDynamicSharedMemorySize, smem_launch)) !=
+        cudaSuccess)
+      return cuda_fail(ce);
   // the small-launch variants (fewer, wider teams) run launches with at most one or two groups per SM
   int smem_small[2] = {0, 0};
   for (int v = 0; v < 2; v++) {
@@ -201,35 +225,18 @@ int sffft_plan_create(sffft_plan_t* out, int L, int io, int acc, const char* con
   p->io = io; p->acc = acc; p->kernel_mode = kernel_mode; p->device = device;
   p->occupancy = occ; p->smem_launch = smem_launch; p->sms = prop.multiProcessorCount;
   p->smem_small[0] = smem_small[0]; p->smem_small[1] = smem_small[1];
-  p->btab = nullptr; p->status = nullptr; p->pool = nullptr;
+  p->btab = nullptr; p->status = nullptr; p->be = be; p->work = nullptr; p->work_bytes = 0;
   if ((ce = cudaMalloc(&p->status, sizeof(int))) != cudaSuccess || (ce = cudaMemset(p->status, 0, sizeof(int))) != cudaSuccess) {
     cudaFree(p->status);
     delete p;
     return cuda_fail(ce);
   }
-  if (blocks > 1) {
-    // A pool of its own that never trims: a composite call's workspace (gigabytes at L >= 32768) is then
-    // mapped once, not again after every synchronisation as the default pool would do.
-    cudaMemPoolProps props = {};
-    props.allocType = cudaMemAllocationTypePinned;
-    props.location.type = cudaMemLocationTypeDevice;
-    props.location.id = device;
-    uint64_t keep = ~0ull;
-    if ((ce = cudaMemPoolCreate(&p->pool, &props)) != cudaSuccess ||
-        (ce = cudaMemPoolSetAttribute(p->pool, cudaMemPoolAttrReleaseThreshold, &keep)) != cudaSuccess) {
-      if (p->pool) cudaMemPoolDestroy(p->pool);
-      cudaFree(p->status);
-      delete p;
-      return cuda_fail(ce);
-    }
-  }
   if (kernel_mode == SFFFT_KERNEL_CACHED) {
-    std::vector<uint8_t> img(e->bmat_bytes, 0);
-    e->build_bmat(img.data());
-    if ((ce = cudaMalloc(&p->btab, e->bmat_bytes)) != cudaSuccess ||
-        (ce = cudaMemcpy(p->btab, img.data(), e->bmat_bytes, cudaMemcpyHostToDevice)) != cudaSuccess) {
+    std::vector<uint8_t> img(e->bmat_bytes[kio], 0);
+    e->build_bmat[kio](img.data());
+    if ((ce = cudaMalloc(&p->btab, e->bmat_bytes[kio])) != cudaSuccess ||
+        (ce = cudaMemcpy(p->btab, img.data(), e->bmat_bytes[kio], cudaMemcpyHostToDevice)) != cudaSuccess) {
       cudaFree(p->btab); cudaFree(p->status);
-      if (p->pool) cudaMemPoolDestroy(p->pool);
       delete p;
       return cuda_fail(ce);
     }
@@ -245,10 +252,6 @@ int sffft_plan_destroy(sffft_plan_t p) {
   cudaSetDevice(p->device);
   cudaFree(p->btab);
   cudaFree(p->status);
-  if (p->pool) {
-    cudaDeviceSynchronize();   // workspaces of calls still in flight return to the pool first
-    cudaMemPoolDestroy(p->pool);
-  }
   cudaSetDevice(prev);
   delete p;
   return SFFFT_OK;
@@ -294,15 +297,14 @@ int sffft_filter_spectrum_ex(sffft_plan_t p, const void* k, int k_dtype, int lay
     const cudaError_t ce = launch_spectrum((float2*)Kf, k, bf, layout, H, R, S, (cudaStream_t)stream, false, -1, 0);
     return ce == cudaSuccess ? SFFFT_OK : cuda_fail(ce);
   }
-  // composite: spectrum of lag d at Kf + d * H * Nb, [blocks][H][Nb]; lag 0 is the causal first block of
-  // k, lag d >= 1 the two-sided filter k[(d-1) Lb + 1 : (d+1) Lb] (rows of k have the full length L)
+  // composite: spectrum of filter segment d at Kf + d * H * Nb, [blocks][H][Nb]: kw_d[n] = k[d Lb + n] and
+  // kw_d[Lb + m] = k[(d - 1) Lb + m] for n, m < Lb (zero for d = 0), rows of k having the full length L
   if (layout != SFFFT_FILTER_CAUSAL) return SFFFT_ERR_UNSUPPORTED;
   const int Lb = p->e->L;
   for (int d = 0; d < p->blocks; d++) {
     float2* dst = (float2*)Kf + (size_t)d * H * p->e->N;
-    const cudaError_t ce = d == 0 ? launch_spectrum(dst, k, bf, SFFFT_FILTER_CAUSAL, H, R, S, (cudaStream_t)stream, false, p->L, 0)
-                                  : launch_spectrum(dst, k, bf, SFFFT_FILTER_TWO_SIDED, H, R, S, (cudaStream_t)stream, false,
-                                                    p->L, (long long)(d - 1) * Lb + 1);
+    const cudaError_t ce = launch_spectrum(dst, k, bf, kLayoutSegment, H, R, S, (cudaStream_t)stream, false, p->L,
+                                           (long long)(d - 1) * Lb);
     if (ce != cudaSuccess) return cuda_fail(ce);
   }
   return SFFFT_OK;
@@ -348,40 +350,70 @@ int sffft_irfft(sffft_plan_t p, const void* X, int B, float* x, void* work, void
 }
 
 static int conv_launch(sffft_plan_t p, const void* u, const void* Kf, void* y, int B, int H, cudaStream_t stream,
-                       unsigned long long wait_ns, int skip_arrive);
+                       unsigned long long wait_ns, int skip_arrive, int mode = 0, const BlockArgs* blk = nullptr);
+
+// Workspace of a composite plan's convolution of a B x H batch: the pair spectra of all input blocks
+// ([H * blocks][ceil(B/2)][N] complex fp32, *zbytes) and then the row energies ([B][H] fp32); 0 for a
+// single-pass plan.
+static size_t conv_ws_bytes(sffft_plan_t p, int B, int H, size_t* zbytes) {
+  *zbytes = 0;
+  if (p->blocks == 1) return 0;
+  *zbytes = (size_t)((B + 1) / 2) * (size_t)H * (size_t)p->blocks * (size_t)p->e->N * sizeof(float2);
+  return *zbytes + ((size_t)B * H * sizeof(float) + 255) / 256 * 256;
+}
+
+int sffft_conv_workspace_bytes(sffft_plan_t p, int B, int H, size_t* bytes) {
+  if (!p || !bytes || B < 1 || H < 1) return SFFFT_ERR_INVALID_ARGUMENT;
+  size_t z;
+  *bytes = conv_ws_bytes(p, B, H, &z);
+  return SFFFT_OK;
+}
+
+int sffft_plan_set_workspace(sffft_plan_t p, void* work, size_t bytes) {
+  if (!p || (work && ((uintptr_t)work & 255) != 0)) return SFFFT_ERR_INVALID_ARGUMENT;
+  p->work = work;
+  p->work_bytes = work ? bytes : 0;
+  return SFFFT_OK;
+}
 
 int sffft_conv(sffft_plan_t p, const void* u, const void* Kf, void* y, int B, int H, void* stream) {
+  if (!p) return SFFFT_ERR_INVALID_ARGUMENT;
+  return sffft_conv_ws(p, u, Kf, y, B, H, p->work, p->work_bytes, stream);
+}
+
+int sffft_conv_ws(sffft_plan_t p, const void* u, const void* Kf, void* y, int B, int H, void* work, size_t work_bytes,
+                  void* stream) {
   if (!p || !u || !Kf || !y || B < 1 || H < 1) return SFFFT_ERR_INVALID_ARGUMENT;
   if ((((uintptr_t)u | (uintptr_t)y | (uintptr_t)Kf) & 15) != 0) return SFFFT_ERR_INVALID_ARGUMENT;
   if (p->blocks == 1) return conv_launch(p, u, Kf, y, B, H, (cudaStream_t)stream, 0, 0);
 
-  // composite plan: u in block-major order, one fused launch per block lag, then the fp32 block sum
+  // composite plan: partitioned convolution over the [B][H * P][Lb] view of u and y (stages.h)
   const int P = p->blocks, Lb = p->e->L;
-  const bool bf = p->io == SFFFT_IO_BF16;
-  const long long blk = (long long)B * H * Lb;
-  if ((long long)P * B * H > std::numeric_limits<int>::max() / 2) return SFFFT_ERR_INVALID_ARGUMENT;
+  if ((long long)H * P > std::numeric_limits<int>::max() / 2 || (long long)B * H * P > std::numeric_limits<int>::max())
+    return SFFFT_ERR_INVALID_ARGUMENT;
+  size_t zbytes;
+  const size_t need = conv_ws_bytes(p, B, H, &zbytes);
+  if (!work || work_bytes < need) return SFFFT_ERR_WORKSPACE;
+  if (((uintptr_t)work & 255) != 0) return SFFFT_ERR_INVALID_ARGUMENT;
   int rc = use_device(p->device);
   if (rc) return rc;
   const cudaStream_t st = (cudaStream_t)stream;
-  float* work = nullptr;
-  const size_t elems = (size_t)blk * (size_t)(P + part_offset(P, P, 1));
-  cudaError_t ce = cudaMallocFromPoolAsync((void**)&work, elems * sizeof(float), p->pool, st);
+  BlockArgs blk;
+  blk.Z = (float*)work;
+  blk.En = (const float*)((char*)work + zbytes);
+  blk.lgP = 0;
+  while ((1 << blk.lgP) < P) blk.lgP++;
+  blk.Hb = H;
+  const cudaError_t ce = launch_row_energy(u, p->io == SFFFT_IO_BF16, (long long)B * H, p->L, Lb,
+                                           (float*)((char*)work + zbytes), st);
   if (ce != cudaSuccess) return cuda_fail(ce);
-  float* ub = work;                              // [P][B][H][Lb]
-  float* parts = work + (size_t)P * blk;         // lag d: [P - d][B][H][Lb] at part_offset(d)
-  ce = launch_block_gather(u, ub, bf, B, H, Lb, P, p->sms, st);
-  for (int d = 0; d < P && ce == cudaSuccess && rc == SFFFT_OK; d++)
-    rc = conv_launch(p, ub, (const char*)Kf + (size_t)d * H * p->e->N * 8, parts + part_offset(d, P, blk),
-                     (P - d) * B, H, st, 0, 0);
-  if (ce == cudaSuccess && rc == SFFFT_OK) ce = launch_block_sum(parts, y, bf, B, H, Lb, P, p->sms, st);
-  const cudaError_t cf = cudaFreeAsync(work, st);
-  if (rc) return rc;
-  if (ce == cudaSuccess) ce = cf;
-  return ce == cudaSuccess ? SFFFT_OK : cuda_fail(ce);
+  rc = conv_launch(p, u, nullptr, nullptr, B, H * P, st, 0, 0, 1, &blk);
+  if (!rc) rc = conv_launch(p, nullptr, Kf, y, B, H * P, st, 0, 0, 2, &blk);
+  return rc;
 }
 
 static int conv_launch(sffft_plan_t p, const void* u, const void* Kf, void* y, int B, int H, cudaStream_t stream,
-                       unsigned long long wait_ns = 0, int skip_arrive = 0) {
+                       unsigned long long wait_ns, int skip_arrive, int mode, const BlockArgs* blk) {
   const ConvEntry* e = p->e;
   const long long pairs = (long long)((B + 1) / 2) * H;
   const long long groups = (pairs + e->G - 1) / e->G;
@@ -395,16 +427,21 @@ static int conv_launch(sffft_plan_t p, const void* u, const void* Kf, void* y, i
   prm.ngroups = (int)groups;
   prm.wait_ns = wait_ns;
   prm.debug_skip_arrive = skip_arrive;
+  prm.blk = blk ? *blk : BlockArgs{nullptr, nullptr, 0, 0};
 #ifdef SFFFT_TRACE
   prm.trace = g_trace;
 #endif
-  // one or two groups per SM: the variant with as many (wider) teams as there are groups shortens each group's
-  // chain; otherwise the plan's own 4-slot kernel
-  const long long per_cta = (groups + p->sms - 1) / p->sms;
-  const int v = per_cta <= 1 ? 0 : (per_cta <= 2 ? 1 : -1);
-  const cudaError_t ce = (v >= 0 && p->smem_small[v])
-                             ? e->launch_small[v][p->kio][p->acc](prm, grid, p->smem_small[v], stream)
-                             : e->launch[p->kio][p->acc](prm, grid, p->smem_launch, stream);
+  cudaError_t ce;
+  if (mode > 0) {
+    ce = p->be->launch[mode - 1][p->kio][p->acc](prm, grid, p->smem_launch, stream);
+  } else {
+    // one or two groups per SM: the variant with as many (wider) teams as there are groups shortens each
+    // group's chain; otherwise the plan's own 4-slot kernel
+    const long long per_cta = (groups + p->sms - 1) / p->sms;
+    const int v = per_cta <= 1 ? 0 : (per_cta <= 2 ? 1 : -1);
+    ce = (v >= 0 && p->smem_small[v]) ? e->launch_small[v][p->kio][p->acc](prm, grid, p->smem_small[v], stream)
+                                      : e->launch[p->kio][p->acc](prm, grid, p->smem_launch, stream);
+  }
   return ce == cudaSuccess ? SFFFT_OK : cuda_fail(ce);
 }
 

@@ -108,6 +108,11 @@ struct HostOps {
     float f; std::memcpy(&f, &w, 4); return f;
   }
   void ldK(const float* p, float (&k)[4]) { for (int e = 0; e < 4; e++) k[e] = p[e]; }
+  void check_z(const float* p) const {
+    if (p < z_lo || p + 4 > z_hi) throw std::out_of_range("pair spectrum access outside the workspace");
+  }
+  void ldZ(const float* p, float (&z)[4]) { check_z(p); for (int e = 0; e < 4; e++) z[e] = p[e]; }
+  void stZ(float* p, const float* v) { check_z(p); for (int e = 0; e < 4; e++) p[e] = v[e]; }
   const uint8_t* kst_lo = nullptr;   // staged spectrum region of the current group
   const uint8_t* kst_hi = nullptr;
   void ldsK(const void* p, float (&k)[4]) {
@@ -149,6 +154,8 @@ struct HostOps {
     for (int i = 0; i < 4; i++) v[i] = w[i ^ (int)rot];
   }
   int n_tw;
+  const float* z_lo = nullptr;   // composite plans: the pair-spectrum workspace (reads and writes stay inside)
+  const float* z_hi = nullptr;
   void tw(int e, float* re, float* im) {
     e &= (n_tw - 1);
     const double a = -2.0 * M_PI * (double)e / (double)n_tw;
@@ -188,8 +195,11 @@ struct HostOps {
   }
 };
 
-template <int SID, class P, class TIO, bool ACC16>
-void run_stage_emu(HostOps& ops, const EpiArgs& ea, const GroupPairs& gp, uint32_t data_s, uint32_t bmat_s) {
+// Stages SID .. of one group: up to 2S - 1, or (MODE 1, a composite plan's forward launch) up to S - 1, whose
+// epilogue stores the pair spectra.
+template <int SID, int MODE, class P, class TIO, bool ACC16>
+void run_stage_emu(HostOps& ops, const EpiArgs& ea, const BlockArgs& ba, const GroupPairs& gp, uint32_t data_s,
+                   uint32_t bmat_s) {
   issue_stage<P, ACC16, SID, sizeof(TIO) == 4>(ops, ea.tmem, data_s, bmat_s);
   // every compute warp's share of the stage, in the kernel's unit order (lane quarter q, warp wi of NWQ)
   constexpr int NWQ = Shape<P, (int)sizeof(TIO)>::NWQ;
@@ -197,18 +207,22 @@ void run_stage_emu(HostOps& ops, const EpiArgs& ea, const GroupPairs& gp, uint32
     for (int q = 0; q < 4; q++)
       for (int lane = 0; lane < 32; lane++) {
         ops.cur_lane = lane;
-        epi_warp<P, TIO, ACC16, SID>(ops, ea, gp, wi, q, lane);
+        if constexpr (MODE == 1 && SID == P::S - 1) spec_store_units<P, TIO>(ops, ea, ba, gp, wi, q, lane);
+        else epi_warp<P, TIO, ACC16, SID>(ops, ea, gp, wi, q, lane);
       }
   if constexpr (SID == 2 * P::S - 1 && P::S == 3)
     for (int tid = 0; tid < 64; tid++) copy_out_staged<P, TIO>(ops, ea, gp, tid, 64);
-  if constexpr (SID + 1 < 2 * P::S) run_stage_emu<SID + 1, P, TIO, ACC16>(ops, ea, gp, data_s, bmat_s);
+  constexpr int LAST = MODE == 1 ? P::S - 1 : 2 * P::S - 1;
+  if constexpr (SID < LAST) run_stage_emu<SID + 1, MODE, P, TIO, ACC16>(ops, ea, ba, gp, data_s, bmat_s);
 }
 
 // Emulates the persistent kernel's per-group flow: the team's conversion of the group's input (read
 // directly from u, with the kernel's thread count and load batching), then the 2S stages, cycling through
 // the kernel's data / TMEM slots.
-template <class P, class TIO, bool ACC16>
-int run_plan(const void* u, const float* Kf, void* y, int B, int H) {
+// MODE 1 / 2: a composite plan's forward / inverse launch over the [B][H][Lb] view (H = channels x blocks), with
+// the block arguments ba (pair spectra, row energies).
+template <class P, class TIO, bool ACC16, int MODE = 0>
+int run_plan(const void* u, const float* Kf, void* y, int B, int H, const BlockArgs* ba = nullptr) {
   using SH = Shape<P, (int)sizeof(TIO)>;
   const int PB = (B + 1) / 2;
   const long long pairs = (long long)PB * H;
@@ -222,20 +236,45 @@ int run_plan(const void* u, const float* Kf, void* y, int B, int H) {
     const int slot = group % SH::NSLOT;
     const uint32_t dbase = (uint32_t)(SH::DATA_OFF + slot * P::DATA_BYTES);
     HostOps ops{&smem, dbase, &tmem, 0, ACC16, SH::TMEM_ALLOC, (size_t)P::DATA_BYTES, nullptr, nullptr, nullptr, nullptr, P::N};
-    ops.in_lo = (const uint8_t*)u;
-    ops.in_hi = (const uint8_t*)u + (size_t)B * H * P::L * sizeof(TIO);
+    if (u) {
+      ops.in_lo = (const uint8_t*)u;
+      ops.in_hi = (const uint8_t*)u + (size_t)B * H * P::L * sizeof(TIO);
+    }
+    const BlockArgs bz = ba ? *ba : BlockArgs{nullptr, nullptr, 0, 0};
+    if (ba) {
+      ops.z_lo = ba->Z;
+      ops.z_hi = ba->Z + 2 * (size_t)((B + 1) / 2) * H * P::N;
+    }
     const GroupPairs gp = group_pairs(group, P::G, B, H);
     std::memset(smem.data() + dbase, 0xFF, P::DATA_BYTES);   // poison: stale data must never be read
-    // the two conversion passes of the kernel: energies, then (where a row needs it) scaled input
     constexpr int NT = SH::TWARPS * 32;
     std::vector<float> part(Energy<P, NT>::SLOTS, 0.f);
-    for (int tid = 0; tid < NT; tid++) convert_group<P, TIO, SH::NB, NT>(ops, uu, gp, tid, part.data(), 1.f);
-    if (group_rescaled<P, NT>(part.data()))
-      for (int tid = 0; tid < NT; tid++) {
-        const int j = tid / Energy<P, NT>::TPS;
-        convert_group<P, TIO, SH::NB, NT>(ops, uu, gp, tid, nullptr, row_in_scale<P, NT>(part.data(), j >> 1, j & 1));
-      }
     EpiArgs ea{(uint32_t)(slot * P::TMEM_COLS), Kf, y, B, H, group, nullptr, 0, part.data()};
+    if constexpr (MODE == 0) {
+      // the two conversion passes of the kernel: energies, then (where a row needs it) scaled input
+      for (int tid = 0; tid < NT; tid++) convert_group<P, TIO, SH::NB, NT>(ops, uu, gp, tid, part.data(), 1.f);
+      if (group_rescaled<P, NT>(part.data()))
+        for (int tid = 0; tid < NT; tid++) {
+          const int j = tid / Energy<P, NT>::TPS;
+          convert_group<P, TIO, SH::NB, NT>(ops, uu, gp, tid, nullptr, row_in_scale<P, NT>(part.data(), j >> 1, j & 1));
+        }
+    } else {
+      fill_energies<P, NT>(part.data(), bz, gp, 0, 1);
+      if constexpr (MODE == 1) {
+        for (int tid = 0; tid < NT; tid++) {
+          const int j = tid / Energy<P, NT>::TPS;
+          convert_group<P, TIO, SH::NB, NT>(ops, uu, gp, tid, nullptr, row_in_scale<P, NT>(part.data(), j >> 1, j & 1));
+        }
+        run_stage_emu<0, 1, P, TIO, ACC16>(ops, ea, bz, gp, dbase, 0u);
+      } else {
+        constexpr int NWQ = SH::NWQ;
+        for (int wi = 0; wi < NWQ; wi++)
+          for (int q = 0; q < 4; q++)
+            for (int lane = 0; lane < 32; lane++) spec_accumulate_units<P, TIO>(ops, ea, bz, gp, wi, q, lane);
+        run_stage_emu<P::S, 2, P, TIO, ACC16>(ops, ea, bz, gp, dbase, 0u);
+      }
+      continue;
+    }
     // the loader warp's staging of the group's spectrum rows (same swizzle as the device)
     if constexpr (SH::KSLOT > 0) {
       const int hf = gp.get(0, P::L).h;
@@ -260,8 +299,39 @@ int run_plan(const void* u, const float* Kf, void* y, int B, int H) {
         ops.kst_hi = kst.data() + (size_t)(hl - hf + 1) * SH::KROW;
       }
     }
-    run_stage_emu<0, P, TIO, ACC16>(ops, ea, gp, dbase, 0u);
+    run_stage_emu<0, 0, P, TIO, ACC16>(ops, ea, bz, gp, dbase, 0u);
   }
+  return 0;
+}
+
+// A composite plan "<P>x[<block plan Pl>]": the row energies of the partitioned convolution (fp32 sums over the
+// whole row, times Lb / L), then the forward and the inverse launch over the [B][H * P][Lb] view.
+template <class Pl, class TIO, bool ACC16>
+int run_composite(int P, const void* u, const float* Kf, void* y, int B, int H) {
+  const int L = P * Pl::L;
+  std::vector<float> En((size_t)B * H);
+  for (size_t r = 0; r < En.size(); r++) {
+    float s = 0.f;
+    for (int n = 0; n < L; n++) {
+      float v;
+      if constexpr (sizeof(TIO) == 4) v = ((const float*)u)[r * L + n];
+      else {
+        const uint32_t w = (uint32_t)((const uint16_t*)u)[r * L + n] << 16;
+        std::memcpy(&v, &w, 4);
+      }
+      s += v * v;
+    }
+    En[r] = s * ((float)Pl::L / (float)L);
+  }
+  std::vector<float> Z(2 * (size_t)((B + 1) / 2) * H * P * Pl::N, 0.f);
+  BlockArgs ba;
+  ba.Z = Z.data();
+  ba.En = En.data();
+  ba.lgP = 0;
+  while ((1 << ba.lgP) < P) ba.lgP++;
+  ba.Hb = H;
+  run_plan<Pl, TIO, ACC16, 1>(u, nullptr, nullptr, B, H * P, &ba);
+  run_plan<Pl, TIO, ACC16, 2>(nullptr, Kf, y, B, H * P, &ba);
   return 0;
 }
 
@@ -272,8 +342,8 @@ int run_variant(int io, int acc, const void* u, const float* Kf, void* y, int B,
   if constexpr (NT % NSQ == 0 && Pl::L % (8 * (NT / NSQ)) == 0) {
     if (io == 0 && acc == 0) return run_plan<Pl, float, false>(u, Kf, y, B, H);
     if (io == 0 && acc == 1) return run_plan<Pl, float, true>(u, Kf, y, B, H);
-    if (io == 1 && acc == 0) return run_plan<Pl, uint16_t, false>(u, Kf, y, B, H);
-    return run_plan<Pl, uint16_t, true>(u, Kf, y, B, H);
+    if (io == 1 && acc == 0) return run_plan<IoPlan<Pl, 2>, uint16_t, false>(u, Kf, y, B, H);
+    return run_plan<IoPlan<Pl, 2>, uint16_t, true>(u, Kf, y, B, H);
   } else {
     return 2;
   }
@@ -283,6 +353,32 @@ int run_variant(int io, int acc, const void* u, const float* Kf, void* y, int B,
 }  // namespace sffft
 
 extern "C" {
+// Emulated partitioned convolution of the composite plan "<P>x[<config>]" (config: a block plan with the
+// partitioned-convolution kernels); Kf holds the P filter-segment spectra [P][H][N].  Returns as sffft_emu_conv.
+int sffft_emu_conv_composite(const char* config, int P, int io, int acc, const void* u, const float* Kf, void* y, int B,
+                             int H) {
+  using namespace sffft;
+  int rc = 2;
+  if (P < 2 || (P & (P - 1))) return 2;
+  try {
+#define SF_EMU_COMPOSITE(R0, R1, R2, G, W, NAME)                                                        \
+  if constexpr (block_mode_plans(R0, R1, R2, W)) {                                                     \
+    if (std::string(config) == NAME) {                                                                  \
+      using Pl = Plan<R0, R1, R2, G, W>;                                                                \
+      if (io == 0 && acc == 0) rc = emu::run_composite<Pl, float, false>(P, u, Kf, y, B, H);            \
+      else if (io == 0 && acc == 1) rc = emu::run_composite<Pl, float, true>(P, u, Kf, y, B, H);        \
+      else if (io == 1 && acc == 0) rc = emu::run_composite<IoPlan<Pl, 2>, uint16_t, false>(P, u, Kf, y, B, H);    \
+      else rc = emu::run_composite<IoPlan<Pl, 2>, uint16_t, true>(P, u, Kf, y, B, H);                              \
+    }                                                                                                   \
+  }
+  SFFFT_CATALOG(SF_EMU_COMPOSITE)
+#undef SF_EMU_COMPOSITE
+  } catch (const std::exception&) {
+    return 3;
+  }
+  return rc;
+}
+
 // Runs the emulated fused kernel for catalog entry `config` ("64x32/w4" ...).  io: 0 fp32, 1 bf16 (u,y as
 // uint16 bf16 bits).  acc: 0 fp32, 1 fp16.  Returns 0 on success, nonzero for an unknown config.
 int sffft_emu_conv(const char* config, int io, int acc, const void* u, const float* Kf, void* y, int B, int H) {
@@ -294,8 +390,8 @@ int sffft_emu_conv(const char* config, int io, int acc, const void* u, const flo
     using Pl = Plan<R0, R1, R2, G, W>;                                                                \
     if (io == 0 && acc == 0) rc = emu::run_plan<Pl, float, false>(u, Kf, y, B, H);                    \
     else if (io == 0 && acc == 1) rc = emu::run_plan<Pl, float, true>(u, Kf, y, B, H);                \
-    else if (io == 1 && acc == 0) rc = emu::run_plan<Pl, uint16_t, false>(u, Kf, y, B, H);            \
-    else rc = emu::run_plan<Pl, uint16_t, true>(u, Kf, y, B, H);                                      \
+    else if (io == 1 && acc == 0) rc = emu::run_plan<IoPlan<Pl, 2>, uint16_t, false>(u, Kf, y, B, H);            \
+    else rc = emu::run_plan<IoPlan<Pl, 2>, uint16_t, true>(u, Kf, y, B, H);                                      \
   }
   SFFFT_CATALOG(SF_EMU_CASE)
 #undef SF_EMU_CASE

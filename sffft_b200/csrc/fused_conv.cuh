@@ -85,6 +85,14 @@ struct DevOps {
     const float4 v = __ldg(reinterpret_cast<const float4*>(p));
     k[0] = v.x; k[1] = v.y; k[2] = v.z; k[3] = v.w;
   }
+  // pair spectra of composite plans: written by the forward launch, read (only) by the inverse launch
+  __device__ __forceinline__ void ldZ(const float* p, float (&z)[4]) {
+    const float4 v = __ldg(reinterpret_cast<const float4*>(p));
+    z[0] = v.x; z[1] = v.y; z[2] = v.z; z[3] = v.w;
+  }
+  __device__ __forceinline__ void stZ(float* p, const float* v) {
+    *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+  }
   // eight input values from global memory (read-only for the whole launch)
   // u is read once (after the L2 prefetch) and y written once: both use the streaming (evict-first) cache
   // policy so they do not displace the spectrum rows that several groups of a channel share (measured 3 %
@@ -210,6 +218,7 @@ struct ConvParams {
   int debug_skip_arrive;        // test hook of sffft_debug_conv_timeout: g + 1 makes the first warp of the
                                 // team converting group g skip its arrival, so that a barrier never completes
                                 // and the bounded waits run out (0 in every regular launch)
+  BlockArgs blk;                // composite plans' forward / inverse launches (kernel MODE 1 / 2) only
 #ifdef SFFFT_TRACE
   unsigned long long* trace;   // debug builds only: [grid][kTraceRoles][kTraceLen] SM clock stamps
 #endif
@@ -376,10 +385,17 @@ __device__ __noinline__ void convert_scaled(DevOps ops, const TIO* u, GroupPairs
   convert_group<P, TIO, NB, NT>(ops, u, gp, tid, nullptr, row_in_scale<P, NT>(en, j >> 1, j & 1));
 }
 
-template <class P, class TIO, bool ACC16>
+// MODE 0: the convolution in one launch.  Composite plans run a partitioned convolution in two launches over
+// the blocks of their rows (BlockArgs): MODE 1 converts the input blocks and runs the forward stages, storing
+// the pair spectra; MODE 2 sums the spectra times the filter's block spectra and runs the inverse stages.
+template <class P, class TIO, bool ACC16, int MODE = 0>
 __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kernel(ConvParams prm) {
   using SH = Shape<P, sizeof(TIO)>;
-  constexpr int S2 = 2 * P::S, TPG = SH::TPG, NS = SH::NS;
+  constexpr int S2 = 2 * P::S, NS = SH::NS;
+  constexpr int NSTG = MODE == 0 ? S2 : P::S;   // stages a launch runs per group
+  constexpr int SID0 = MODE == 2 ? P::S : 0;    // its first stage
+  constexpr int TPG = NSTG + 1;                 // tasks per group: conversion (or spectrum sums) + epilogues
+  static_assert(MODE == 0 || TPG < SH::TPG, "modes");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* bmat = sm;
@@ -444,8 +460,9 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
   if (warp == 0) {
     // ---------------- L2 prefetcher ----------------
     // Brings each group's 2G input sequences (one bulk prefetch per sequence, one lane each) and spectrum
-    // rows into L2, at most PD groups ahead of the conversions, so a team's direct loads hit L2.
-    for (int gi = 0; gi < ni; gi++) {
+    // rows into L2, at most PD groups ahead of the conversions, so a team's direct loads hit L2.  (The inverse
+    // launch of a composite plan reads pair and filter spectra shared by many groups: no prefetch.)
+    for (int gi = 0; gi < (MODE == 2 ? 0 : ni); gi++) {
       if (gi >= SH::PD && !wait_stamp_all(conv_done, gi - SH::PD + 1, abort_flag)) break;
       if (lane == 0) SFFFT_STAMP(0, 3 * gi);
       const int group = (int)blockIdx.x + gi * (int)gridDim.x;
@@ -455,7 +472,7 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
         const long long off = (lane & 1) ? pi.off1 : pi.off0;
         if (off >= 0) prefetch_l2(u + off, (uint32_t)SH::SEQB);
       }
-      if (lane == 0) {
+      if (MODE == 0 && lane == 0) {
         const PairInfo a = gp.get(0, P::L), b = gp.get(P::G - 1, P::L);
         if (a.h >= 0) prefetch_l2(prm.Kf + 2ll * a.h * P::N, P::N * 8);
         if (b.h >= 0 && b.h != a.h) prefetch_l2(prm.Kf + 2ll * b.h * P::N, P::N * 8);
@@ -475,7 +492,7 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
       for (int s = 0; s < NS; s++) {
         done[s] = 0;
         ncommit[s] = 0;
-        total[s] = (s < ni ? (ni - s + NS - 1) / NS : 0) * S2;
+        total[s] = (s < ni ? (ni - s + NS - 1) / NS : 0) * NSTG;
         left += total[s];
       }
       int nmma = 0;
@@ -494,7 +511,7 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
             // arrival)
             const bool again = rep[s] != 0;
             if (again) rep[s] = 0;
-            issue_any<P, ACC16, sizeof(TIO) == 4>((again ? done[s] - 1 : done[s]) % S2, ops,
+            issue_any<P, ACC16, sizeof(TIO) == 4>(SID0 + (again ? done[s] - 1 : done[s]) % NSTG, ops,
                                 tmem + (uint32_t)(s * P::TMEM_COLS),
                                 smem_u32(sm + SH::DATA_OFF + s * P::DATA_BYTES), smem_u32(bmat));
             mma_commit(mma_done + s);
@@ -531,7 +548,7 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
     // Copies each group's spectrum rows (coalesced 16-byte loads) into a staging slot in the swizzled
     // order the spectrum epilogue reads; a group whose pairs span more than KC channels is marked -1 and
     // its epilogue reads Kf from global memory instead.
-    if constexpr (SH::KSLOT > 0) {
+    if constexpr (SH::KSLOT > 0 && MODE == 0) {
       constexpr int NPIECE = SH::KROW / 16, PPR = P::RL / 2;   // 16-byte pieces per row of the last digit
       for (int gi = 0; gi < ni; gi++) {
         const int ks = gi % SH::KSLOT, use = gi / SH::KSLOT;
@@ -612,7 +629,20 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
           // convert the group's input, measuring each row's energy for the MMA warp, which derives the rows'
           // scales while the stage-0 MMAs run (pair_scales)
           float* en = energies + (s * 2 + ((gi / NS) & 1)) * SH::EN_STRIDE;
-          convert_group<P, TIO, SH::NB, TWT>(ops, u, gp, ttid, en, 1.f);
+          if constexpr (MODE == 0) {
+            convert_group<P, TIO, SH::NB, TWT>(ops, u, gp, ttid, en, 1.f);
+          } else {
+            // composite: the rows' scales follow from their energies over the whole row (every warp writes
+            // the same values into the slots it then reads)
+            fill_energies<P, TWT>(en, prm.blk, gp, lane, 32);
+            __syncwarp();
+            if constexpr (MODE == 1) {
+              convert_scaled<P, TIO, SH::NB, TWT>(ops, u, gp, ttid, en);
+            } else {
+              const EpiArgs ea{0u, prm.Kf, prm.y, prm.B, prm.H, group, nullptr, 0, en};
+              spec_accumulate_units<P, TIO>(ops, ea, prm.blk, gp, wi, q, lane);
+            }
+          }
           if (lane == 0 && wt == 0) SFFFT_STAMP(2 + team, 3 * ntask + 1);
           fence_async_smem();
           tc_fence_before();
@@ -620,14 +650,14 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
           if (lane == 0 && wt == 0) atomicAdd((int*)conv_done, 1);
           if (lane == 0 && wt == 0) SFFFT_STAMP(2 + team, 3 * ntask + 2);
         } else {
-          const int sid = j - 1;
+          const int sid = SID0 + j - 1;
           if (!wait_phase_all(mma_done + s, (md_bits >> l) & 1u, abort_flag)) { ok = false; break; }
           md_bits ^= 1u << l;
           // stage 0 ran after every warp of the team had converted the group (each arrived on a_ready after
           // storing its energy slots), so every warp now derives the same row scales into its own copy; a group
           // with a row to rescale (rare) is converted again with them and stage 0 repeated
           float* en = energies + (s * 2 + ((gi / NS) & 1)) * SH::EN_STRIDE;
-          if (sid == 0 && group_rescaled_warp<P, TWT>(en, lane)) {
+          if (MODE == 0 && sid == 0 && group_rescaled_warp<P, TWT>(en, lane)) {
             tc_fence_after();
             convert_scaled<P, TIO, SH::NB, TWT>(ops, u, gp, ttid, en);
             if (lane == 0 && wt == 0) rep[s] = 1;
@@ -640,7 +670,7 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
           if (lane == 0 && wt == 0) SFFFT_STAMP(2 + team, 3 * ntask + 1);
           tc_fence_after();
           EpiArgs ea{tmem + (uint32_t)(s * P::TMEM_COLS), prm.Kf, prm.y, prm.B, prm.H, group, nullptr, 0, en};
-          const bool kst = SH::KSLOT > 0 && sid == P::S - 1;
+          const bool kst = MODE == 0 && SH::KSLOT > 0 && sid == P::S - 1;
           constexpr int KS = SH::KSLOT > 0 ? SH::KSLOT : 1;
           const int ks = gi % KS;
           if (kst) {
@@ -652,7 +682,8 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
             const int hf = kinfo[ks];
             if (hf >= 0) { ea.kst = kstage + ks * SH::KC * SH::KROW; ea.khf = hf; }
           }
-          epi_any<P, TIO, ACC16>(sid, ops, ea, gp, q, wi, lane);
+          if (MODE == 1 && sid == P::S - 1) spec_store_units<P, TIO>(ops, ea, prm.blk, gp, wi, q, lane);
+          else epi_any<P, TIO, ACC16>(sid, ops, ea, gp, q, wi, lane);
           if (kst) warp_arrive(k_empty + ks, lane);
           tc_fence_before();
           if (P::S == 3 && sid == S2 - 1) {
@@ -661,7 +692,7 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
             copy_out_staged<P, TIO>(ops, ea, gp, ttid, TWT);
             if (!team_sync(team_done + team, ts_phase, lane, abort_flag)) { ok = false; break; }
           }
-          if (sid < S2 - 1) {
+          if (j < TPG - 1) {
             fence_async_smem();
             warp_arrive(a_ready + s, lane);
           }

@@ -9,9 +9,9 @@
 
 namespace sffft {
 
-template <class P, class TIO, bool ACC16>
+template <class P, class TIO, bool ACC16, int MODE = 0>
 cudaError_t launch_conv(const ConvParams& prm, int grid, int smem_bytes, cudaStream_t st) {
-  fused_conv_kernel<P, TIO, ACC16><<<grid, Shape<P, sizeof(TIO)>::NT, smem_bytes, st>>>(prm);
+  fused_conv_kernel<P, TIO, ACC16, MODE><<<grid, Shape<P, sizeof(TIO)>::NT, smem_bytes, st>>>(prm);
   return cudaGetLastError();
 }
 
@@ -20,22 +20,25 @@ ConvEntry make_entry(const char* name) {
   ConvEntry e;
   e.name = name;
   e.R0 = P::R0; e.R1 = P::R1; e.R2 = P::R2; e.G = P::G; e.W = P::W; e.N = P::N; e.L = P::L;
+  using PB = IoPlan<P, 2>;   // the bf16-I/O kernels' plan
   using S4 = Shape<P, 4>;
-  using S2 = Shape<P, 2>;
-  e.threads = S4::NT; e.bmat_bytes = P::BMAT_BYTES;
+  using S2 = Shape<PB, 2>;
+  e.threads = S4::NT;
+  e.bmat_bytes[0] = P::BMAT_BYTES; e.bmat_bytes[1] = PB::BMAT_BYTES;
   e.smem_bytes[0] = S4::SMEM; e.smem_bytes[1] = S2::SMEM;
   e.tmem_cols[0] = S4::TMEM_ALLOC; e.tmem_cols[1] = S2::TMEM_ALLOC;
   e.slots[0] = S4::NSLOT; e.slots[1] = S2::NSLOT;
   e.kslots[0] = S4::KSLOT; e.kslots[1] = S2::KSLOT;
   e.launch[0][0] = &launch_conv<P, float, false>;
   e.launch[0][1] = &launch_conv<P, float, true>;
-  e.launch[1][0] = &launch_conv<P, __nv_bfloat16, false>;
-  e.launch[1][1] = &launch_conv<P, __nv_bfloat16, true>;
+  e.launch[1][0] = &launch_conv<PB, __nv_bfloat16, false>;
+  e.launch[1][1] = &launch_conv<PB, __nv_bfloat16, true>;
   e.func[0][0] = (const void*)&fused_conv_kernel<P, float, false>;
   e.func[0][1] = (const void*)&fused_conv_kernel<P, float, true>;
-  e.func[1][0] = (const void*)&fused_conv_kernel<P, __nv_bfloat16, false>;
-  e.func[1][1] = (const void*)&fused_conv_kernel<P, __nv_bfloat16, true>;
-  e.build_bmat = &hostmath::build_bmat_image<P>;
+  e.func[1][0] = (const void*)&fused_conv_kernel<PB, __nv_bfloat16, false>;
+  e.func[1][1] = (const void*)&fused_conv_kernel<PB, __nv_bfloat16, true>;
+  e.build_bmat[0] = &hostmath::build_bmat_image<P>;
+  e.build_bmat[1] = &hostmath::build_bmat_image<PB>;
   for (int v = 0; v < 2; v++)
     for (int io = 0; io < 2; io++) {
       e.smem_small[v][io] = 0;
@@ -52,19 +55,20 @@ ConvEntry make_entry(const char* name) {
 template <class P, int V>
 void add_small_variant(ConvEntry& e) {
   using PV = Plan<P::R0, P::R1, P::R2, P::G, P::W, V>;
+  using PVB = IoPlan<PV, 2>;
   constexpr int NT = Shape<PV, 4>::TWARPS * 32, NSQ = 2 * P::G;
   if constexpr (NT % NSQ == 0 && P::L % (8 * (NT / NSQ)) == 0) {
     const int i = V == 1 ? 0 : 1;
     e.smem_small[i][0] = Shape<PV, 4>::SMEM;
-    e.smem_small[i][1] = Shape<PV, 2>::SMEM;
+    e.smem_small[i][1] = Shape<PVB, 2>::SMEM;
     e.launch_small[i][0][0] = &launch_conv<PV, float, false>;
     e.launch_small[i][0][1] = &launch_conv<PV, float, true>;
-    e.launch_small[i][1][0] = &launch_conv<PV, __nv_bfloat16, false>;
-    e.launch_small[i][1][1] = &launch_conv<PV, __nv_bfloat16, true>;
+    e.launch_small[i][1][0] = &launch_conv<PVB, __nv_bfloat16, false>;
+    e.launch_small[i][1][1] = &launch_conv<PVB, __nv_bfloat16, true>;
     e.func_small[i][0][0] = (const void*)&fused_conv_kernel<PV, float, false>;
     e.func_small[i][0][1] = (const void*)&fused_conv_kernel<PV, float, true>;
-    e.func_small[i][1][0] = (const void*)&fused_conv_kernel<PV, __nv_bfloat16, false>;
-    e.func_small[i][1][1] = (const void*)&fused_conv_kernel<PV, __nv_bfloat16, true>;
+    e.func_small[i][1][0] = (const void*)&fused_conv_kernel<PVB, __nv_bfloat16, false>;
+    e.func_small[i][1][1] = (const void*)&fused_conv_kernel<PVB, __nv_bfloat16, true>;
   }
 }
 
@@ -74,13 +78,41 @@ void add_small_variants(ConvEntry& e) {
   add_small_variant<P, 2>(e);
 }
 
-// The plans with small-launch variants: the built-in default plan of each length up to 8192 (the 16384 plan
-// already has one slot).
-constexpr bool small_variants(int R0, int R1, int R2, int W) {
-  return W == 8 && ((R0 == 16 && R1 == 16 && R2 == 1) || (R0 == 32 && R1 == 16 && R2 == 1) ||
-                    (R0 == 32 && R1 == 32 && R2 == 1) || (R0 == 64 && R1 == 32 && R2 == 1) ||
-                    (R0 == 64 && R1 == 64 && R2 == 1) || (R0 == 32 && R1 == 16 && R2 == 16) ||
-                    (R0 == 32 && R1 == 32 && R2 == 16));
+template <class P>
+BlockEntry make_block_entry(const char* name) {
+  using PB = IoPlan<P, 2>;
+  BlockEntry e;
+  e.name = name;
+  e.smem_bytes[0] = Shape<P, 4>::SMEM;
+  e.smem_bytes[1] = Shape<PB, 2>::SMEM;
+  e.launch[0][0][0] = &launch_conv<P, float, false, 1>;
+  e.launch[0][0][1] = &launch_conv<P, float, true, 1>;
+  e.launch[0][1][0] = &launch_conv<PB, __nv_bfloat16, false, 1>;
+  e.launch[0][1][1] = &launch_conv<PB, __nv_bfloat16, true, 1>;
+  e.launch[1][0][0] = &launch_conv<P, float, false, 2>;
+  e.launch[1][0][1] = &launch_conv<P, float, true, 2>;
+  e.launch[1][1][0] = &launch_conv<PB, __nv_bfloat16, false, 2>;
+  e.launch[1][1][1] = &launch_conv<PB, __nv_bfloat16, true, 2>;
+  e.func[0][0][0] = (const void*)&fused_conv_kernel<P, float, false, 1>;
+  e.func[0][0][1] = (const void*)&fused_conv_kernel<P, float, true, 1>;
+  e.func[0][1][0] = (const void*)&fused_conv_kernel<PB, __nv_bfloat16, false, 1>;
+  e.func[0][1][1] = (const void*)&fused_conv_kernel<PB, __nv_bfloat16, true, 1>;
+  e.func[1][0][0] = (const void*)&fused_conv_kernel<P, float, false, 2>;
+  e.func[1][0][1] = (const void*)&fused_conv_kernel<P, float, true, 2>;
+  e.func[1][1][0] = (const void*)&fused_conv_kernel<PB, __nv_bfloat16, false, 2>;
+  e.func[1][1][1] = (const void*)&fused_conv_kernel<PB, __nv_bfloat16, true, 2>;
+  return e;
+}
+
+template <int STAGES>
+std::vector<BlockEntry> collect_block_entries() {
+  std::vector<BlockEntry> v;
+#define SF_COLLECT_BLK(R0, R1, R2, G, W, NAME)                                                    \
+  if constexpr ((R2 > 1 ? 3 : 2) == STAGES && block_mode_plans(R0, R1, R2, W))                   \
+    v.push_back(make_block_entry<Plan<R0, R1, R2, G, W>>(NAME));
+  SFFFT_CATALOG(SF_COLLECT_BLK)
+#undef SF_COLLECT_BLK
+  return v;
 }
 
 template <int NMIN, int NMAX>

@@ -30,6 +30,8 @@ struct sffft_pipe {
   sffft_plan_t plan;
   int B, H, L, N, sio, nb, hc, device;   // chunk: nb batch rows (even) x hc channels
   int hp;                    // channels per batch row of the host arrays (H, or more for a channel slice)
+  void* work;                // composite plans: the workspace of one chunk's convolution (the kernels of all
+  size_t work_bytes;         // chunks run in order on one stream, so one is enough)
   void* u_stage[kStreams];   // device staging [nb][hc][L] per slot
   void* y_stage[kStreams];
   cudaStream_t s[kStreams];  // one per stage
@@ -41,6 +43,9 @@ static void pipe_free(sffft_pipe* q) {
   for (int i = 0; i < kStreams; i++) {
     if (q->u_stage[i]) cudaFree(q->u_stage[i]);
     if (q->y_stage[i]) cudaFree(q->y_stage[i]);
+  }
+  if (q->work) cudaFree(q->work);
+  for (int i = 0; i < kStreams; i++) {
     if (q->s[i]) cudaStreamDestroy(q->s[i]);
     if (q->done[i]) cudaEventDestroy(q->done[i]);
     if (q->up[i]) cudaEventDestroy(q->up[i]);
@@ -81,7 +86,9 @@ int sffft_pipe_create_slice(sffft_pipe_t* pipe, sffft_plan_t plan, int B, int H,
   }
   if (q->nb > B) q->nb = B;
   const size_t bytes = (size_t)q->nb * q->hc * q->L * q->sio;
-  bool ok = cudaEventCreateWithFlags(&q->start, cudaEventDisableTiming) == cudaSuccess;
+  bool ok = sffft_conv_workspace_bytes(plan, q->nb, q->hc, &q->work_bytes) == SFFFT_OK &&
+            (q->work_bytes == 0 || cudaMalloc(&q->work, q->work_bytes) == cudaSuccess) &&
+            cudaEventCreateWithFlags(&q->start, cudaEventDisableTiming) == cudaSuccess;
   for (int i = 0; i < kStreams && ok; i++) {
     ok = cudaMalloc(&q->u_stage[i], bytes) == cudaSuccess && cudaMalloc(&q->y_stage[i], bytes) == cudaSuccess &&
          cudaStreamCreateWithFlags(&q->s[i], cudaStreamNonBlocking) == cudaSuccess &&
@@ -137,7 +144,8 @@ extern "C" int sffft_conv_host(sffft_pipe_t q, const void* u_host, const void* K
       if (ce == cudaSuccess) ce = cudaStreamWaitEvent(sk, q->up[k], 0);
       if (ce == cudaSuccess) ce = cudaStreamWaitEvent(sk, q->down[k], 0);
       if (ce != cudaSuccess) break;
-      rc = sffft_conv(q->plan, q->u_stage[k], (const char*)Kf + (size_t)h0 * q->N * 8, q->y_stage[k], bn, hn, sk);
+      rc = sffft_conv_ws(q->plan, q->u_stage[k], (const char*)Kf + (size_t)h0 * q->N * 8, q->y_stage[k], bn, hn,
+                         q->work, q->work_bytes, sk);
       if (rc) break;
       ce = cudaEventRecord(q->conv[k], sk);
       // download after the kernel

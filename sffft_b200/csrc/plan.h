@@ -73,13 +73,14 @@ SF_HD constexpr uint32_t make_idesc(int M, int N, bool d_f32, bool a_mn, bool b_
 // ---------------------------------------------------------------------------------------------
 // MS_: the most group slots (and teams) per CTA.  The catalog plans use 4; small launches, with at most one
 // or two groups per SM, run variants with 1 or 2 slots whose teams are 4x or 2x wider (shorter chains).
-template <int R0_, int R1_, int R2_, int G_, int W_, int MS_ = 4>
+// SPLIT_: three-stage plans hold their DFT matrices as fp16 hi + lo (IoPlan clears it for bf16 I/O).
+template <int R0_, int R1_, int R2_, int G_, int W_, int MS_ = 4, bool SPLIT_ = true>
 struct Plan {
   static constexpr int R0 = R0_, R1 = R1_, R2 = R2_, G = G_, W = W_, MS = MS_;
   static constexpr int S = R2_ > 1 ? 3 : 2;
   static constexpr int N = R0 * R1 * R2, L = N / 2, NT = 32 * W;
   static constexpr int RL = S == 3 ? R2 : R1;          // radix of the last (contiguous) digit
-  static constexpr bool FSPLIT = S == 3;                // DFT matrices as fp16 hi + lo (accuracy)
+  static constexpr bool FSPLIT = S == 3 && SPLIT_;      // DFT matrices as fp16 hi + lo (accuracy)
   static constexpr int NSET = FSPLIT ? 2 : 1;
 
   SF_HD static constexpr int R(int j) { return j == 0 ? R0 : (j == 1 ? R1 : R2); }
@@ -125,6 +126,21 @@ struct Plan {
                 (R2 == 1 || R2 == 16 || R2 == 32 || R2 == 64), "radices must be 16/32/64");
   static_assert(W == 4 || W == 8, "4 or 8 warps");
 };
+
+// The plan a kernel with I/O element size SIO runs.  The hi + lo split of three-stage plans' DFT matrices keeps
+// fp32 I/O within its tolerance (relative L2 3.5e-4 with it, 4.3-5.0e-4 without, against 5e-4); bf16 I/O is
+// rounded to bf16 at the output, which the split does not change (1.69e-3 with, 1.71e-3 without at L = 4096,
+// against 3e-3), so its kernels run one fp16 set: half the MMAs of every stage and half the matrix bytes.
+template <class P, int SIO>
+struct IoPlanT {
+  using type = P;
+};
+template <int R0, int R1, int R2, int G, int W, int MS>
+struct IoPlanT<Plan<R0, R1, R2, G, W, MS, true>, 2> {
+  using type = Plan<R0, R1, R2, G, W, MS, (R2 == 1)>;   // two-stage plans: the same type (no split either way)
+};
+template <class P, int SIO>
+using IoPlan = typename IoPlanT<P, SIO>::type;
 
 // Resources of the persistent kernel for plan P and I/O element size SIO:
 //   1 L2-prefetch warp (a few groups ahead of the conversions), 1 MMA warp, 1 spectrum-loader warp, and

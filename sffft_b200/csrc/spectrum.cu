@@ -43,6 +43,7 @@ __device__ __forceinline__ float k_to_float(__nv_bfloat16 v) { return __bfloat16
 enum { kSrcInPlace = 0, kSrcReal = 1, kSrcHermitian = 2 };
 constexpr int kLayoutFull = 3;
 
+
 template <class TK, int SRC>
 __global__ void __launch_bounds__(256) spectrum_stage_kernel(float2* __restrict__ Kf, const TK* __restrict__ k, SpecStage st) {
   extern __shared__ float2 sbuf[];
@@ -80,10 +81,13 @@ __global__ void __launch_bounds__(256) spectrum_stage_kernel(float2* __restrict_
         col = p & (L - 1);
       } else if (st.layout == kLayoutFull) {
         col = p;
+      } else if (st.layout == kLayoutSegment) {
+        col = p < L ? L + p : p - L;
       } else {
         col = p < L ? p : -1;
       }
-      val = make_float2(col >= 0 ? k_to_float(k[h * st.kpitch + st.koff + col]) : 0.f, 0.f);
+      const long long ix = st.koff + col;
+      val = make_float2(col >= 0 && ix >= 0 ? k_to_float(k[h * st.kpitch + ix]) : 0.f, 0.f);
     } else {
       val = Kh[p];
     }

@@ -1,8 +1,13 @@
-// Host launchers of the digit-stage kernels (spectrum.cu) and of the block-convolution kernels (blocks.cu).
+// Host launchers of the digit-stage kernels (spectrum.cu) and of the composite plans' row energies (blocks.cu).
 #pragma once
 #include <cuda_runtime.h>
 
 namespace sffft {
+
+// Filter layout of a composite plan's segment d of block length L (launch_spectrum with koff = (d - 1) * L,
+// negative for d = 0): kw[n] = k[koff + L + n] = k[d L + n] for n < L and kw[L + m] = k[koff + m] for m < L,
+// zero where the index is negative (segment 0 is the causal first block).
+constexpr int kLayoutSegment = 4;
 
 // Filter spectrum (or forward DFT) of H rows in digit order for radices R[0..S-1]; see spectrum.cu.
 cudaError_t launch_spectrum(float2* Kf, const void* k, bool k_bf16, int layout, int H, const int* R, int S,
@@ -13,11 +18,7 @@ cudaError_t launch_rfft(const void* x, bool x_bf16, int rows, float2* X, float2*
 cudaError_t launch_irfft(const float2* X, int rows, float* x, float2* W, const int* R, int S, int sms,
                          cudaStream_t stream);
 
-// Block convolution of composite plans; see blocks.cu.
-__host__ __device__ long long part_offset(int d, int P, long long blk);
-cudaError_t launch_block_gather(const void* u, float* ub, bool bf16, int B, int H, int Lb, int P, int sms,
-                                cudaStream_t stream);
-cudaError_t launch_block_sum(const float* parts, void* y, bool bf16, int B, int H, int Lb, int P, int sms,
-                             cudaStream_t stream);
+// Row energies of composite plans (sum of squares over each row of L values, times Lb / L); see blocks.cu.
+cudaError_t launch_row_energy(const void* u, bool bf16, long long rows, int L, int Lb, float* E, cudaStream_t stream);
 
 }  // namespace sffft

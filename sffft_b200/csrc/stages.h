@@ -31,6 +31,7 @@ namespace sffft {
 struct PairInfo {
   long long off0, off1;   // element offsets of the two sequences in u / y, or -1 when absent
   int h;                  // channel (spectrum row), -1 when the pair slot is empty
+  int j;                  // batch pair: rows 2j, 2j + 1
 };
 
 // Pair bookkeeping of one group with 32-bit arithmetic: one division per group, then pair g is found
@@ -46,6 +47,7 @@ struct GroupPairs {
       if (j >= PB) { const int d = j / PB; j -= d * PB; h += d; }
     }
     PairInfo pi;
+    pi.j = j;
     if (h >= H) { pi.off0 = pi.off1 = -1; pi.h = -1; return pi; }
     pi.h = h;
     pi.off0 = (long long)(2 * j * H + h) * L;
@@ -66,9 +68,11 @@ SF_HD PairInfo pair_info(int cta, int g, int G, int B, int H, int L) {
   const int PB = (B + 1) / 2;
   const long long gp = (long long)cta * G + g;
   PairInfo pi;
+  pi.j = 0;
   if (gp >= (long long)PB * H) { pi.off0 = pi.off1 = -1; pi.h = -1; return pi; }
   const int h = (int)(gp / PB), j = (int)(gp % PB);
   pi.h = h;
+  pi.j = j;
   pi.off0 = ((long long)(2 * j) * H + h) * L;
   pi.off1 = (2 * j + 1 < B) ? ((long long)(2 * j + 1) * H + h) * L : -1;
   return pi;
@@ -717,6 +721,123 @@ SF_HD void copy_out_staged(Ops& ops, const EpiArgs& ea, const GroupPairs& gp, in
     const uint32_t w = out_stage_word(e);            // e % 4 == 0: the 4 words share one XOR value
     ops.ld4_staged((w & ~3u) * 4, (w ^ (uint32_t)e) & 3u, v);
     if (off >= 0) ops.store4(y + off + n, v);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Partitioned convolution of composite plans (L = P * Lb, blocks of the block plan's length Lb = P::L)
+//
+// The caller's [B][Hb][L] arrays are read as [B][Hb * P][Lb]: row (b, h) block q is "channel" h' = h * P + q of
+// length Lb, so the kernel's pairs, groups and offsets apply unchanged.  With U_q the spectrum of input block q
+// (zero-padded to N = 2 Lb) and K'_d the spectrum of the filter segment kw_d[n] = k[d Lb + n] (n < Lb),
+// kw_d[Lb + m] = k[(d - 1) Lb + m] (m < Lb, zero for d = 0), output block p is the first Lb outputs of the
+// inverse transform of W_p = sum_{q <= p} U_q K'_{p - q}: K'_d = K_d + (-1)^f K_{d-1} folds the second half of
+// block p - 1's linear convolution (a shift by N / 2 is a sign flip of the odd frequencies) into block p.
+//   forward launch:  conversion and stages 0 .. S-1 of every (pair, block); the last forward stage stores the
+//                    pair's spectrum (x its 1/sqrt(R) stage scale) to Z [Hb * P][PB][N] (complex fp32, digit
+//                    order) instead of multiplying it by a filter spectrum;
+//   inverse launch:  the operand of stage S from sum_q Z_q K'_{p-q} (the spectrum multiply of the single-pass
+//                    kernel, extended over the blocks), then stages S .. 2S-1 and the outputs of block p.
+// Both launches scale each row by the power of two that its energy over the whole row gives (pair_scales), so
+// that every block of a row carries the same scale and the sum over blocks stays consistent; the energies come
+// from a separate pass over u, normalised to Lb values.
+// ---------------------------------------------------------------------------------------------
+struct BlockArgs {
+  float* Z;           // [Hb * P][PB][N] complex pair spectra of the input blocks
+  const float* En;    // [B * Hb] row energies (sum of squares over the row x Lb / L)
+  int lgP;            // log2 of the block count P
+  int Hb;             // channels of the caller's arrays
+};
+
+// The group's energy slots from the row energies (slot 0 of each sequence holds its row's energy, the others
+// zero), lanes i0, i0 + istep, ... of the caller; absent sequences have energy 0.
+template <class P, int NT>
+SF_HD void fill_energies(float* en, const BlockArgs& ba, const GroupPairs& gp, int i0, int istep) {
+  using EN = Energy<P, NT>;
+  constexpr int LGL = ilog2(P::L);
+  for (int i = i0; i < EN::SLOTS; i += istep) {
+    const int seq = i / EN::SPS, slot = i - seq * EN::SPS;
+    float e = 0.f;
+    if (slot == 0) {
+      const PairInfo pi = gp.get(seq >> 1, P::L);
+      const long long off = (seq & 1) ? pi.off1 : pi.off0;
+      if (off >= 0) e = ba.En[off >> (LGL + ba.lgP)];
+    }
+    en[i] = e;
+  }
+}
+
+// Forward launch, after the last forward stage: the pair spectra of the group's units to Z.
+template <class P, class TIO, class Ops>
+SF_HD void spec_store_units(Ops& ops, const EpiArgs& ea, const BlockArgs& ba, const GroupPairs& gp, int wi, int q,
+                            int lane) {
+  constexpr int SID = P::S - 1, C = epi_chunks<P, SID>(), R = P::rad(SID), U = P::tiles(SID) * C, N = P::N;
+  constexpr int NWQ = Shape<P, (int)sizeof(TIO)>::NWQ;
+  constexpr float SC = stage_scale(R);
+#pragma unroll 1
+  for (int u = wi; u < U; u += NWQ) {
+    const int t = u / C, c = u - t * C;
+    const EpiIdx x = epi_idx<P, SID>(ea.tmem, t, c, q, lane);
+    uint32_t rre[16], rim[16];
+    ops.tmem_ld16(x.taddr, rre);
+    ops.tmem_ld16(x.taddr + (uint32_t)R, rim);
+    ops.tmem_wait();
+    const PairInfo pi = gp.get(x.g, P::L);
+    if (pi.h < 0) continue;
+    float* zp = ba.Z + 2 * (((long long)pi.h * gp.PB + pi.j) * N + (long long)x.rr * R + x.c0);
+    for (int j = 0; j < 16; j += 2) {
+      const float v[4] = {ops.acc_val(rre[j]) * SC, ops.acc_val(rim[j]) * SC, ops.acc_val(rre[j + 1]) * SC,
+                          ops.acc_val(rim[j + 1]) * SC};
+      ops.stZ(zp + 2 * j, v);
+    }
+  }
+}
+
+// Inverse launch, in place of the conversion: the A operand of stage S (the layout the spectrum stage's
+// epilogue writes) from sum_{q <= p} Z_q K'_{p - q} of each unit's 16 values, accumulated in fp32 in two runs
+// of eight.
+template <class P, class TIO, class Ops>
+SF_HD void spec_accumulate_units(Ops& ops, const EpiArgs& ea, const BlockArgs& ba, const GroupPairs& gp, int wi, int q,
+                                 int lane) {
+  constexpr int SID = P::S - 1, C = epi_chunks<P, SID>(), R = P::rad(SID), U = P::tiles(SID) * C, N = P::N;
+  constexpr int NWQ = Shape<P, (int)sizeof(TIO)>::NWQ, RWS = P::rows(SID + 1);
+#pragma unroll 1
+  for (int u = wi; u < U; u += NWQ) {
+    const int t = u / C, c = u - t * C;
+    const EpiIdx x = epi_idx<P, SID>(0u, t, c, q, lane);
+    const PairInfo pi = gp.get(x.g, P::L);
+    const int hb = pi.h >> ba.lgP, pb = pi.h - (hb << ba.lgP);
+#pragma unroll 1
+    for (int half = 0; half < 2; half++) {
+      float ar[8], ai[8];
+      for (int e = 0; e < 8; e++) ar[e] = ai[e] = 0.f;
+      const long long pos = (long long)x.rr * R + x.c0 + 8 * half;
+      if (pi.h >= 0) {
+#pragma unroll 1
+        for (int qq = 0; qq <= pb; qq++) {
+          const float* zp = ba.Z + 2 * ((((long long)(hb << ba.lgP) + qq) * gp.PB + pi.j) * N + pos);
+          const float* kp = ea.Kf + 2 * (((long long)(pb - qq) * ba.Hb + hb) * N + pos);
+          float z[16], k[16];
+          for (int e = 0; e < 4; e++) {
+            float z4[4], k4[4];
+            ops.ldZ(zp + 4 * e, z4);
+            ops.ldK(kp + 4 * e, k4);
+            for (int i = 0; i < 4; i++) { z[4 * e + i] = z4[i]; k[4 * e + i] = k4[i]; }
+          }
+          for (int e = 0; e < 8; e++) {
+            ar[e] += z[2 * e] * k[2 * e] - z[2 * e + 1] * k[2 * e + 1];
+            ai[e] += z[2 * e] * k[2 * e + 1] + z[2 * e + 1] * k[2 * e];
+          }
+        }
+      }
+      uint32_t pr[4], pim[4];
+      for (int p = 0; p < 4; p++) {
+        pr[p] = ops.pack2(ar[2 * p], ar[2 * p + 1]);
+        pim[p] = ops.pack2(ai[2 * p], ai[2 * p + 1]);
+      }
+      ops.st16(kmaj_data_off(x.r, x.c0 + 8 * half, R, RWS), pr[0], pr[1], pr[2], pr[3]);
+      ops.st16(kmaj_data_off(x.r, R + x.c0 + 8 * half, R, RWS), pim[0], pim[1], pim[2], pim[3]);
+    }
   }
 }
 

@@ -101,6 +101,23 @@ def spectrum_digit_order(k, radices):
     return Kc[:, digit_order(radices)]
 
 
+def segment_spectra_digit_order(k, P, radices):
+    """Filter-segment spectra of a composite plan of P blocks, complex128 [P, H, N] in digit order (N = 2 Lb, Lb =
+    L / P): segment d is kw_d[n] = k[d Lb + n] and kw_d[Lb + m] = k[(d - 1) Lb + m] (zero for d = 0), whose
+    spectrum is K_d + (-1)^f K_(d-1), the block-d term of the partitioned convolution."""
+    k = np.asarray(k, np.float64)
+    H, L = k.shape
+    Lb = L // P
+    out = []
+    for d in range(P):
+        kw = np.zeros((H, 2 * Lb))
+        kw[:, :Lb] = k[:, d * Lb:(d + 1) * Lb]
+        if d > 0:
+            kw[:, Lb:] = k[:, (d - 1) * Lb:d * Lb]
+        out.append(np.fft.fft(kw, axis=1)[:, digit_order(radices)])
+    return np.stack(out)
+
+
 def to_bf16(x):
     """Round-to-nearest-even fp32 -> bf16, returned as fp32 values."""
     x = np.ascontiguousarray(x, np.float32)

@@ -78,6 +78,9 @@ def test_plan_create_rejects_bad_arguments():
 def test_null_handles_are_rejected():
     lib = sf.lib()
     assert lib.sffft_conv(None, 16, 16, 16, 1, 1, None) == sf.ERR_INVALID_ARGUMENT
+    assert lib.sffft_conv_ws(None, 16, 16, 16, 1, 1, 256, 1 << 20, None) == sf.ERR_INVALID_ARGUMENT
+    assert lib.sffft_conv_workspace_bytes(None, 1, 1, ctypes.byref(ctypes.c_size_t())) == sf.ERR_INVALID_ARGUMENT
+    assert lib.sffft_plan_set_workspace(None, None, 0) == sf.ERR_INVALID_ARGUMENT
     assert lib.sffft_filter_spectrum(None, 16, 0, 1, 16, None) == sf.ERR_INVALID_ARGUMENT
     assert lib.sffft_filter_spectrum_ex(None, 16, 0, 1, 1, 16, None) == sf.ERR_INVALID_ARGUMENT
     assert lib.sffft_rfft(None, 16, 0, 1, 16, 16, None) == sf.ERR_INVALID_ARGUMENT

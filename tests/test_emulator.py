@@ -6,7 +6,8 @@ import pytest
 
 import sffft_b200 as sf
 from tests.conftest import rel_l2
-from tests.oracle_py import bf16_bits, bf16_from_bits, spectrum_digit_order, to_bf16
+from tests.oracle_py import (bf16_bits, bf16_from_bits, per_row_rel_l2, scaled_pair_inputs, segment_spectra_digit_order,
+                             spectrum_digit_order, to_bf16)
 
 TOL = {("fp32", "fp32"): 5e-4, ("bf16", "fp32"): 3e-3, ("fp32", "fp16"): 1e-3, ("bf16", "fp16"): 4e-3}
 
@@ -113,3 +114,42 @@ def test_small_launch_variants(oracle, name):
     # groups per SM
     assert run_case(oracle, name, 4, 3) <= TOL[("fp32", "fp32")]
     assert run_case(oracle, name, 2, 1, io="bf16", acc="fp16") <= TOL[("bf16", "fp16")]
+
+
+# Composite plans' partitioned convolution (row energies, forward launch storing pair spectra, inverse launch
+# summing them against the filter-segment spectra), every sequence against the fp64 oracle.
+@pytest.mark.parametrize("name,P,B,H,io,acc", [("16x16/w4", 2, 3, 2, "fp32", "fp32"), ("16x16/w4", 4, 2, 1, "bf16", "fp32"),
+                                               ("32x16/w8", 2, 3, 1, "fp32", "fp16"),
+                                               ("32x16x16/w8", 2, 2, 1, "fp32", "fp32")])
+def test_composite_partitioned_convolution(oracle, name, P, B, H, io, acc):
+    R = radices(name)
+    L = P * int(np.prod(R)) // 2
+    u, k = oracle.gen_profile(B, H, L, decay=4.0, sqrt_norm=True, seed=P + B)
+    if io == "bf16":
+        u, k = to_bf16(u), to_bf16(k)
+    Kc = segment_spectra_digit_order(k, P, R)
+    Kf = np.stack([Kc.real, Kc.imag], -1).astype(np.float32)
+    if io == "bf16":
+        y = bf16_from_bits(sf.emu_conv_composite(name, P, bf16_bits(u), Kf, io=io, acc=acc)).reshape(u.shape)
+    else:
+        y = sf.emu_conv_composite(name, P, u, Kf, io=io, acc=acc)
+    assert rel_l2(y, oracle.direct_conv(u, k)) <= TOL[(io, acc)]
+
+
+def test_composite_pairs_of_very_different_scale(oracle):
+    # rows scaled 1, 1e-3, 1e-4, 0, 1e-5 ... next to their partners: each row's scale comes from its energy over
+    # the whole row, shared by its blocks, so every row keeps its own relative accuracy
+    P, name = 2, "16x16/w4"
+    L = P * 128
+    u, k = scaled_pair_inputs(oracle, 1, L, "fp32", seed=11)
+    Kc = segment_spectra_digit_order(k, P, radices(name))
+    Kf = np.stack([Kc.real, Kc.imag], -1).astype(np.float32)
+    y = sf.emu_conv_composite(name, P, u, Kf)
+    errs = per_row_rel_l2(y, oracle.direct_conv(u, k))
+    assert np.all(errs <= TOL[("fp32", "fp32")]), errs
+
+
+def test_composite_without_block_kernels_is_rejected():
+    u = np.zeros((2, 1, 512), np.float32)
+    with pytest.raises(ValueError):
+        sf.emu_conv_composite("32x32/w4", 2, u, np.zeros((2, 1, 1024, 2), np.float32))

@@ -1,5 +1,6 @@
-"""Composite plans: lengths past the largest single-kernel plan as block convolutions on a catalog plan
-(sffft_plan_create with "<P>x[<plan>]", the default for L > 16384).
+"""Composite plans: lengths past the largest single-kernel plan as partitioned convolutions on a block plan
+(sffft_plan_create with "<P>x[<plan>]", the default for L > 16384): one forward launch over every input block,
+one inverse launch summing the block spectra against the filter-segment spectra, in a caller-owned workspace.
 
 The reference stops at L = 8192 and lists multi-pass plans as missing (README.md:175), so parity is with
 the oracle's fp64 direct causal convolution (the reference's own check, src/sffft.cu:376-378), at the
@@ -12,7 +13,7 @@ import torch
 
 import sffft_b200 as sf
 from tests.conftest import rel_l2
-from tests.oracle_py import to_bf16
+from tests.oracle_py import per_row_rel_l2, scaled_pair_inputs, to_bf16
 
 pytestmark = pytest.mark.gpu
 TOL = {("fp32", "fp32"): 5e-4, ("bf16", "fp32"): 3e-3, ("bf16", "fp16"): 4e-3}
@@ -55,8 +56,8 @@ def test_default_long_plans(oracle, cuda_device, L, io):
     ref = oracle.direct_conv_seqs(u, k, seqs)
     err = rel_l2(y.reshape(B * H, L)[seqs], ref)
     assert err <= TOL[(io, "fp32")], f"L={L} {io}: {err:.3e}"
-    # linearity at full length: y(2u) / 2 == y(u) up to the rounding of subnormal fp16 intermediates, which
-    # the partial sums of the blocks carry separately (bound: a fifth of the parity tolerance)
+    # linearity at full length: y(2u) / 2 == y(u) (the rows' power-of-two scales absorb the factor; bound: a
+    # fifth of the parity tolerance)
     dt = torch.bfloat16 if io == "bf16" else torch.float32
     y2 = plan.conv((2 * torch.from_numpy(u).to(cuda_device)).to(dt), Kf).float().cpu().numpy()
     plan.check()
@@ -97,3 +98,48 @@ def test_composite_rejects_other_filter_layouts(cuda_device):
     with pytest.raises(sf.SffftError):
         sf.Plan(384, config="3x[16x16/w4]")          # block counts are powers of two
     plan.close()
+
+
+def test_composite_workspace_contract(cuda_device):
+    L, B, H = 256, 3, 4
+    plan = sf.Plan(L, config="2x[16x16/w4]")
+    need = plan.workspace_bytes(B, H)
+    # pair spectra of every input block (ceil(B/2) * H * L complex fp32 pairs) and the row energies
+    assert need == 2 * H * L * 2 * 8 + 256
+    assert sf.Plan(1024).workspace_bytes(B, H) == 0
+    rng = np.random.default_rng(9)
+    u = torch.from_numpy(rng.standard_normal((B, H, L)).astype(np.float32)).to(cuda_device)
+    k = torch.from_numpy((rng.standard_normal((H, L)) / np.sqrt(L)).astype(np.float32)).to(cuda_device)
+    Kf = plan.filter_spectrum(k)
+    y_ref = plan.conv(u, Kf)
+    lib = sf.lib()
+    y = torch.empty_like(u)
+    args = (plan._h, u.data_ptr(), Kf.data_ptr(), y.data_ptr(), B, H)
+    assert lib.sffft_conv(*args, None) == sf.ERR_WORKSPACE            # nothing attached
+    work = torch.empty(need, dtype=torch.uint8, device=cuda_device)
+    assert lib.sffft_conv_ws(*args, work.data_ptr(), need - 1, None) == sf.ERR_WORKSPACE
+    assert lib.sffft_conv_ws(*args, work.data_ptr() + 16, need, None) == sf.ERR_INVALID_ARGUMENT   # alignment
+    assert lib.sffft_plan_set_workspace(plan._h, work.data_ptr() + 16, need) == sf.ERR_INVALID_ARGUMENT
+    assert lib.sffft_plan_set_workspace(plan._h, work.data_ptr(), need) == sf.OK
+    assert lib.sffft_conv(*args, None) == sf.OK
+    plan.check()
+    assert torch.equal(y, y_ref)
+    y.zero_()
+    assert lib.sffft_conv_ws(*args, work.data_ptr(), need, None) == sf.OK
+    plan.check()
+    assert torch.equal(y, y_ref)
+    assert lib.sffft_plan_set_workspace(plan._h, None, 0) == sf.OK
+    assert lib.sffft_conv(*args, None) == sf.ERR_WORKSPACE
+    plan.close()
+
+
+def test_composite_pairs_of_very_different_scale(oracle, cuda_device):
+    # every row keeps its own relative accuracy next to a partner 1e3-1e5 times larger, or all zero: its scale
+    # comes from its energy over the whole row and is shared by its blocks
+    L, config = 512, "4x[16x16/w8]"
+    plan = sf.Plan(L, config=config)
+    u, k = scaled_pair_inputs(oracle, 2, L, "fp32", seed=4)
+    y, _ = run(plan, u, k, cuda_device)
+    plan.close()
+    errs = per_row_rel_l2(y, oracle.direct_conv(u, k))
+    assert np.all(errs <= TOL[("fp32", "fp32")]), errs
