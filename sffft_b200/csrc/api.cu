@@ -9,6 +9,7 @@
 #include <vector>
 
 #include "../../include/sffft.h"
+#include "calibration.h"
 #include "fused_conv.cuh"
 #include "registry.h"
 #include "spectrum.h"
@@ -85,26 +86,18 @@ static const std::vector<const ConvEntry*>& catalog() {
   return all;
 }
 
-// Built-in B200 default per length: the fastest catalog entry of the plan the benchmark configurations name for
-// that length (B = 8, H = 768, fp32 and bf16 I/O, timed on one B200); the CLI's empirical selector can
-// override it from its own measurements.
+// Built-in B200 default per length: the calibrated plan of calibration.h (measured on one B200 by
+// `python -m sffft_b200.calibrate`, chosen by make_calibration.py); the CLI's empirical selector can override it
+// from its own measurements.
 // Composite plans: lengths above the largest single-kernel plan run as partitioned convolutions of up to
 // kMaxBlocks blocks (a forward transform per input block, a spectrum sum and an inverse transform per output
 // block; the sums read blocks * (blocks + 1) / 2 block spectra).
 constexpr int kMaxBlockL = 16384, kMaxBlocks = 16;
 
 static const char* default_for(int L) {
-  switch (L) {
-    case 128: return "16x16/w8";
-    case 256: return "32x16/w8";
-    case 512: return "32x32/w8";
-    case 1024: return "64x32/w8";
-    case 2048: return "64x64/w8";
-    case 4096: return "32x16x16/w8";
-    case 8192: return "32x32x16/w8";
-    case 16384: return "32x32x32/w8";
-    default: return nullptr;
-  }
+  for (const CalibratedPlan& c : kCalibratedPlans)
+    if (c.L == L) return c.name;
+  return nullptr;
 }
 
 static int copy_name(const char* s, char* out, int cap) {

@@ -7,6 +7,8 @@
 // 128 KiB of fp16 data plus 20 KiB of split DFT matrices fits B200's 227 KiB per-block shared memory.
 #pragma once
 
+#include "calibration.h"
+
 #define SFFFT_CATALOG(X)                                                                              \
   X(16, 16, 1, 8, 4, "16x16/w4") X(16, 16, 1, 8, 8, "16x16/w8")                                       \
   X(32, 16, 1, 8, 4, "32x16/w4") X(16, 32, 1, 8, 4, "16x32/w4") X(32, 16, 1, 8, 8, "32x16/w8")        \
@@ -23,18 +25,14 @@
   X(32, 32, 16, 1, 8, "32x32x16/w8") X(16, 32, 32, 1, 8, "16x32x32/w8") X(16, 16, 64, 1, 8, "16x16x64/w8") \
   X(32, 32, 32, 1, 4, "32x32x32/w4") X(32, 32, 32, 1, 8, "32x32x32/w8")
 
-// The plans with small-launch variants: the built-in default plan of each length up to 8192 (the 16384 plan
-// already has one slot).
+// The plans with small-launch variants: the calibrated default plan of each length up to 8192 (calibration.h; the
+// 16384 plan already has one slot).
 constexpr bool small_variants(int R0, int R1, int R2, int W) {
-  return W == 8 && ((R0 == 16 && R1 == 16 && R2 == 1) || (R0 == 32 && R1 == 16 && R2 == 1) ||
-                    (R0 == 32 && R1 == 32 && R2 == 1) || (R0 == 64 && R1 == 32 && R2 == 1) ||
-                    (R0 == 64 && R1 == 64 && R2 == 1) || (R0 == 32 && R1 == 16 && R2 == 16) ||
-                    (R0 == 32 && R1 == 32 && R2 == 16));
+  return calibrated_default(R0, R1, R2, W) && R0 * R1 * R2 <= 16384;
 }
 
-// The block plans of composite plans with the partitioned-convolution kernels: the default plan of each length
-// up to 8192, 16x16/w4, and 32x32x32/w8 (the default block of every composite length above 16384).
+// The block plans of composite plans with the partitioned-convolution kernels: the calibrated default of every
+// length (32x32x32/w8, the 16384 default, is the block of every default composite length) and 16x16/w4.
 constexpr bool block_mode_plans(int R0, int R1, int R2, int W) {
-  return small_variants(R0, R1, R2, W) || (R0 == 16 && R1 == 16 && R2 == 1 && W == 4) ||
-         (R0 == 32 && R1 == 32 && R2 == 32 && W == 8);
+  return calibrated_default(R0, R1, R2, W) || (R0 == 16 && R1 == 16 && R2 == 1 && W == 4);
 }
