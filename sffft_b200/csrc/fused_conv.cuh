@@ -408,7 +408,8 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
   volatile int* abort_flag = reinterpret_cast<volatile int*>(k_empty + 3);
   int* kinfo = reinterpret_cast<int*>(k_empty + 4);   // [2] first staged channel, or -1
   uint64_t* team_done = k_empty + 5;           // [NTEAM] a team's warps staged their outputs / copied them out
-  volatile int* kstamp = reinterpret_cast<volatile int*>(team_done + SH::NTEAM);   // [2] group being staged
+  uint64_t* bmat_full = team_done + SH::NTEAM; // the cached DFT matrices have arrived (bulk copy)
+  volatile int* kstamp = reinterpret_cast<volatile int*>(bmat_full + 1);   // [2] group being staged
   volatile int* conv_done = kstamp + 2;        // groups whose input has been converted
   volatile int* rep = conv_done + 1;           // [NS] the slot's next MMA request repeats stage 0
   uint8_t* kstage = sm + SH::K_OFF;
@@ -425,18 +426,18 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
     for (int s = 0; s < NS; s++) { mbar_init(a_ready + s, SH::TWARPS); mbar_init(mma_done + s, 1); }
     for (int l = 0; l < 2; l++) { mbar_init(k_full + l, 32); mbar_init(k_empty + l, SH::TWARPS); }
     for (int t = 0; t < SH::NTEAM; t++) mbar_init(team_done + t, SH::TWARPS);
+    mbar_init(bmat_full, 1);
     kstamp[0] = kstamp[1] = -1;
     *conv_done = 0;
     for (int q = 0; q < NS; q++) rep[q] = 0;
     *abort_flag = 0;
     s_wait_ns = prm.wait_ns ? prm.wait_ns : kWaitLimitNs;
     fence_mbar_init();
+    // the cached DFT matrices arrive by bulk copy while the teams convert their first groups; the MMA warp waits
+    // for them before its first issue
+    if (prm.btab) bulk_load_smem(bmat, prm.btab, P::BMAT_BYTES, bmat_full);
   }
-  if (prm.btab) {
-    const uint4* src = prm.btab;
-    uint4* dst = reinterpret_cast<uint4*>(bmat);
-    for (int i = tid; i < P::BMAT_BYTES / 16; i += SH::NT) dst[i] = __ldg(src + i);
-  } else {
+  if (!prm.btab) {
     BmatEmitDev emit{bmat};
     for_each_bmat_entry<P>(emit, tid, SH::NT);
   }
@@ -483,7 +484,7 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
     // ---------------- MMA issuer ----------------
     // Slot s holds this CTA's groups s, s + NS, ...; each group needs its 2S stages in order.  The issuer
     // scans the slots and issues the next stage of any slot whose operand is ready.
-    if (lane == 0) {
+    if (lane == 0 && (!prm.btab || wait_phase(bmat_full, 0u, abort_flag))) {
       DevOps ops{sm, ACC16, nullptr, nullptr, P::N};
       int done[NS], total[NS], ncommit[NS];
       uint32_t ar_bits = 0;
@@ -703,6 +704,9 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
     }
   }
 
+  // no bulk copy may still be writing shared memory when the CTA exits (it lands within microseconds; the MMA
+  // warp normally waited for it long before)
+  if (tid == 0 && prm.btab) mbar_wait_bounded(bmat_full, 0u, s_wait_ns);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();

@@ -216,9 +216,9 @@ struct Shape {
   static constexpr int TMEM_ALLOC = pow2ceil(cmax(32, NS * P::TMEM_COLS));
   static constexpr int TPG = 2 * P::S + 1;                          // tasks per group: convert + 2S epilogues
   // 8-byte words from BAR_OFF: a_ready[NS], mma_done[NS], k_full[2], k_empty[2], TMEM base, abort flag,
-  // first staged channel per spectrum slot[2], team_done[NTEAM], then ints: spectrum slot stamps[2], the
-  // count of converted groups and the stage-repeat flags[NS]
-  static constexpr int NBARW = 2 * NS + 4 + 3 + NTEAM + (3 + NS + 1) / 2;
+  // first staged channel per spectrum slot[2], team_done[NTEAM], bmat_full, then ints: spectrum slot stamps[2],
+  // the count of converted groups and the stage-repeat flags[NS]
+  static constexpr int NBARW = 2 * NS + 4 + 3 + NTEAM + 1 + (3 + NS + 1) / 2;
   static_assert(NBARW <= 64, "barrier area");
   static_assert(NS % NTEAM == 0 && WC % (4 * NTEAM) == 0, "teams");
   static_assert(SMEM <= 227 * 1024, "shared memory");

@@ -85,6 +85,20 @@ __device__ __forceinline__ uint64_t global_ns() {
   return t;
 }
 
+// Copies `bytes` (a multiple of 16, both addresses 16-byte aligned) from global memory into this CTA's shared
+// memory with bulk copies of at most 32 KB, completing on `bar` (initialised with one arrival, which this call
+// makes together with the expected byte count).  Plain bulk copies of this GPU's own memory, no multicast.
+__device__ __forceinline__ void bulk_load_smem(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+  for (uint32_t off = 0; off < bytes; off += 32768u) {
+    const uint32_t n = bytes - off < 32768u ? bytes - off : 32768u;
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(static_cast<char*>(dst) + off)),
+                 "l"(static_cast<const char*>(src) + off), "r"(n), "r"(smem_u32(bar))
+                 : "memory");
+  }
+}
+
 // Waits for the given phase parity; gives up after `limit_ns` nanoseconds and reports false.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
