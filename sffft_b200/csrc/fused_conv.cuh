@@ -420,6 +420,9 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int ni = (int)blockIdx.x < prm.ngroups ? (prm.ngroups - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x : 0;
 
+  // the next kernel of the stream may start its own prologue as soon as SMs free up (it waits for this grid to
+  // complete before touching global memory)
+  if (tid == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   if (warp == 1) { tmem_alloc(tmem_slot, SH::TMEM_ALLOC); tmem_relinquish(); }
   if (tid == 0) {
     // consumer barriers count one arrival per warp of the consuming team
@@ -451,6 +454,9 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
     sincospif(-2.0f * (float)e / (float)P::N, &sn, &cs);
     tw_lo[i] = make_float2(cs, sn);
   }
+  // everything above touched only shared memory, TMEM and the plan's constant DFT-matrix image; u, Kf, y and the
+  // status word may be produced or consumed by the stream's previous kernel, which must have completed first
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   fence_async_smem();
   tc_fence_before();
   __syncthreads();

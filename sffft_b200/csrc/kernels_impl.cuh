@@ -9,10 +9,22 @@
 
 namespace sffft {
 
+// Launched as a programmatic dependent of the stream's previous kernel: the kernel's prologue (barriers, TMEM,
+// DFT matrices, twiddle table) may run while that kernel's last CTAs finish; it waits for that kernel to complete
+// (griddepcontrol.wait) before it touches anything in global memory the previous work may have produced.
 template <class P, class TIO, bool ACC16, int MODE = 0>
 cudaError_t launch_conv(const ConvParams& prm, int grid, int smem_bytes, cudaStream_t st) {
-  fused_conv_kernel<P, TIO, ACC16, MODE><<<grid, Shape<P, sizeof(TIO)>::NT, smem_bytes, st>>>(prm);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3((unsigned)Shape<P, sizeof(TIO)>::NT);
+  cfg.dynamicSmemBytes = (size_t)smem_bytes;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, fused_conv_kernel<P, TIO, ACC16, MODE>, prm);
 }
 
 template <class P>
