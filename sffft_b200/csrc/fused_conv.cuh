@@ -454,37 +454,48 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
     sincospif(-2.0f * (float)e / (float)P::N, &sn, &cs);
     tw_lo[i] = make_float2(cs, sn);
   }
-  // everything above touched only shared memory, TMEM and the plan's constant DFT-matrix image; u, Kf, y and the
-  // status word may be produced or consumed by the stream's previous kernel, which must have completed first
+  const TIO* u = reinterpret_cast<const TIO*>(prm.u);
+  // L2 prefetch of group gi's input sequences and spectrum rows by warp 0 (one bulk prefetch per sequence).  A
+  // prefetch only moves lines into L2, the point of coherence, so it may be issued before the previous kernel has
+  // finished writing them: the loads that use the data come after the dependency wait below.
+  auto prefetch_group = [&](int gi) {
+    const int group = (int)blockIdx.x + gi * (int)gridDim.x;
+    const GroupPairs gp = group_pairs(group, P::G, prm.B, prm.H);
+    if (lane < 2 * P::G) {
+      const PairInfo pi = gp.get(lane >> 1, P::L);
+      const long long off = (lane & 1) ? pi.off1 : pi.off0;
+      if (off >= 0) prefetch_l2(u + off, (uint32_t)SH::SEQB);
+    }
+    if (MODE == 0 && lane == 0) {
+      const PairInfo a = gp.get(0, P::L), b = gp.get(P::G - 1, P::L);
+      if (a.h >= 0) prefetch_l2(prm.Kf + 2ll * a.h * P::N, P::N * 8);
+      if (b.h >= 0 && b.h != a.h) prefetch_l2(prm.Kf + 2ll * b.h * P::N, P::N * 8);
+    }
+  };
+  // the first PD groups' prefetches overlap the previous kernel's tail
+  const int npre = MODE == 2 ? 0 : (ni < SH::PD ? ni : SH::PD);
+  if (warp == 0)
+    for (int gi = 0; gi < npre; gi++) prefetch_group(gi);
+  // everything above touched only shared memory, TMEM and the plan's constant DFT-matrix image (and issued L2
+  // prefetches); u, Kf, y and the status word may be produced or consumed by the stream's previous kernel, which
+  // must have completed first
   asm volatile("griddepcontrol.wait;" ::: "memory");
   fence_async_smem();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const TIO* u = reinterpret_cast<const TIO*>(prm.u);
 
   if (warp == 0) {
     // ---------------- L2 prefetcher ----------------
     // Brings each group's 2G input sequences (one bulk prefetch per sequence, one lane each) and spectrum
     // rows into L2, at most PD groups ahead of the conversions, so a team's direct loads hit L2.  (The inverse
     // launch of a composite plan reads pair and filter spectra shared by many groups: no prefetch.)
-    for (int gi = 0; gi < (MODE == 2 ? 0 : ni); gi++) {
+    for (int gi = npre; gi < (MODE == 2 ? 0 : ni); gi++) {
       if (gi >= SH::PD && !wait_stamp_all(conv_done, gi - SH::PD + 1, abort_flag)) break;
       if (lane == 0) SFFFT_STAMP(0, 3 * gi);
-      const int group = (int)blockIdx.x + gi * (int)gridDim.x;
-      const GroupPairs gp = group_pairs(group, P::G, prm.B, prm.H);
-      if (lane < 2 * P::G) {
-        const PairInfo pi = gp.get(lane >> 1, P::L);
-        const long long off = (lane & 1) ? pi.off1 : pi.off0;
-        if (off >= 0) prefetch_l2(u + off, (uint32_t)SH::SEQB);
-      }
-      if (MODE == 0 && lane == 0) {
-        const PairInfo a = gp.get(0, P::L), b = gp.get(P::G - 1, P::L);
-        if (a.h >= 0) prefetch_l2(prm.Kf + 2ll * a.h * P::N, P::N * 8);
-        if (b.h >= 0 && b.h != a.h) prefetch_l2(prm.Kf + 2ll * b.h * P::N, P::N * 8);
-        SFFFT_STAMP(0, 3 * gi + 1);
-      }
+      prefetch_group(gi);
+      if (lane == 0) SFFFT_STAMP(0, 3 * gi + 1);
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
