@@ -1,7 +1,7 @@
 """The host-buffer pipeline (sffft_pipe_create / sffft_conv_host): channel chunks of a batch in pinned host
 memory are uploaded, convolved and downloaded on three streams.  Per-pair results do not depend on how
 pairs are grouped, so the output must equal sffft_conv on the whole device batch bit for bit, for chunk
-counts that divide H and ones that leave a short last chunk, odd B, both I/O types."""
+counts that divide H and ones that leave a short last chunk, the default chunking, odd B, both I/O types."""
 import pytest
 import torch
 
@@ -10,7 +10,7 @@ import sffft_b200 as sf
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("L,B,H,io,chunks", [(1024, 8, 96, "fp32", 0), (1024, 5, 37, "fp32", 4),
+@pytest.mark.parametrize("L,B,H,io,chunks", [(1024, 8, 96, "fp32", 0), (512, 7, 37, "bf16", 0), (1024, 5, 37, "fp32", 4),
                                              (128, 3, 50, "bf16", 7), (4096, 2, 9, "bf16", 3),
                                              (256, 4, 3, "fp32", 8)])
 def test_host_pipe_equals_device_path(L, B, H, io, chunks):
