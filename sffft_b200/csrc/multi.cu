@@ -9,9 +9,15 @@
 //                          (one pitched copy per chunk: B rows of (h1 - h0) * L contiguous values), convolves
 //                          it and downloads its slice of y through a host pipe of its own, so the devices'
 //                          copies and kernels run concurrently; the call returns when every device is done.
+//                          Each device has a host thread of its own (started with the multi-device pipe), which
+//                          issues that device's copies and kernels and waits for them, so no device waits for
+//                          the host to finish issuing another device's work.
 #include <cuda_runtime.h>
 
+#include <condition_variable>
+#include <mutex>
 #include <new>
+#include <thread>
 #include <vector>
 
 #include "../../include/sffft.h"
@@ -40,7 +46,51 @@ struct sffft_multi {
   std::vector<int> h0, h1, dev;
   std::vector<sffft_pipe_t> pipes;
   std::vector<cudaStream_t> streams;   // per shard: the stream its pipe is ordered on
+  // one worker thread per shard; a call publishes its arguments, bumps `gen` and waits until `pending` is 0
+  std::vector<std::thread> workers;
+  std::mutex mu;
+  std::condition_variable go, done;
+  unsigned gen = 0;
+  int pending = 0;
+  bool quit = false;
+  const void* u_host = nullptr;
+  const void* const* Kf = nullptr;
+  void* y_host = nullptr;
+  std::vector<int> rc;                 // per shard: the status of the current call
 };
+
+namespace {
+
+// Shard g's part of one sffft_conv_host_multi call, on its worker thread: issue the shard's chunks on its device,
+// wait for them and read the device-side status.
+int run_shard(sffft_multi* m, int g) {
+  if (!m->Kf[g]) return SFFFT_ERR_INVALID_ARGUMENT;
+  if (cudaSetDevice(m->dev[g]) != cudaSuccess) return SFFFT_ERR_CUDA;
+  const size_t col = (size_t)m->L * m->sio;   // bytes of one channel row
+  int rc = sffft_conv_host(m->pipes[g], (const char*)m->u_host + (size_t)m->h0[g] * col, m->Kf[g],
+                           (char*)m->y_host + (size_t)m->h0[g] * col, m->streams[g]);
+  if (cudaStreamSynchronize(m->streams[g]) != cudaSuccess && !rc) rc = SFFFT_ERR_CUDA;
+  const int st = sffft_plan_check(m->plans[g]);   // device-side status of the shard's kernels
+  return rc ? rc : st;
+}
+
+void worker(sffft_multi* m, int g) {
+  unsigned seen = 0;
+  while (true) {
+    {
+      std::unique_lock<std::mutex> lk(m->mu);
+      m->go.wait(lk, [&] { return m->quit || m->gen != seen; });
+      if (m->quit) return;
+      seen = m->gen;
+    }
+    const int rc = run_shard(m, g);
+    std::lock_guard<std::mutex> lk(m->mu);
+    m->rc[g] = rc;
+    if (--m->pending == 0) m->done.notify_all();
+  }
+}
+
+}  // namespace
 
 extern "C" int sffft_conv_multi(const sffft_plan_t* plans, int G, const void* const* u, const void* const* Kf,
                                 void* const* y, int B, int H, void* const* streams) {
@@ -108,36 +158,41 @@ extern "C" int sffft_multi_pipe_create(sffft_multi_t* out, const sffft_plan_t* p
     sffft_multi_pipe_destroy(m);
     return rc;
   }
+  m->rc.assign(G, SFFFT_OK);
+  try {
+    for (int g = 0; g < G; g++) m->workers.emplace_back(worker, m, g);
+  } catch (...) {
+    sffft_multi_pipe_destroy(m);
+    return SFFFT_ERR_ALLOC;
+  }
   *out = m;
   return SFFFT_OK;
 }
 
 extern "C" int sffft_conv_host_multi(sffft_multi_t m, const void* u_host, const void* const* Kf, void* y_host) {
   if (!m || !u_host || !Kf || !y_host) return SFFFT_ERR_INVALID_ARGUMENT;
-  int prev = 0;
-  if (cudaGetDevice(&prev) != cudaSuccess) return SFFFT_ERR_CUDA;
-  // queue every device's chunks first (the calls return once queued), then wait for all of them
-  int rc = SFFFT_OK;
-  const size_t col = (size_t)m->L * m->sio;   // bytes of one channel row
-  for (int g = 0; g < m->G && rc == SFFFT_OK; g++) {
-    if (!Kf[g]) { rc = SFFFT_ERR_INVALID_ARGUMENT; break; }
-    rc = sffft_conv_host(m->pipes[g], (const char*)u_host + (size_t)m->h0[g] * col, Kf[g],
-                         (char*)y_host + (size_t)m->h0[g] * col, m->streams[g]);
-  }
-  for (int g = 0; g < m->G; g++) {
-    if (cudaSetDevice(m->dev[g]) != cudaSuccess || cudaStreamSynchronize(m->streams[g]) != cudaSuccess) {
-      if (!rc) rc = SFFFT_ERR_CUDA;
-      continue;
-    }
-    const int st = sffft_plan_check(m->plans[g]);   // device-side status of the shard's kernels
-    if (!rc) rc = st;
-  }
-  cudaSetDevice(prev);
-  return rc;
+  // every shard's worker issues and waits for its own device's work; the first error (in shard order) is returned
+  std::unique_lock<std::mutex> lk(m->mu);
+  m->u_host = u_host;
+  m->Kf = Kf;
+  m->y_host = y_host;
+  m->pending = m->G;
+  m->gen++;
+  m->go.notify_all();
+  m->done.wait(lk, [&] { return m->pending == 0; });
+  for (int g = 0; g < m->G; g++)
+    if (m->rc[g]) return m->rc[g];
+  return SFFFT_OK;
 }
 
 extern "C" int sffft_multi_pipe_destroy(sffft_multi_t m) {
   if (!m) return SFFFT_ERR_INVALID_ARGUMENT;
+  {
+    std::lock_guard<std::mutex> lk(m->mu);
+    m->quit = true;
+  }
+  m->go.notify_all();
+  for (std::thread& t : m->workers) t.join();
   int prev = 0;
   cudaGetDevice(&prev);
   for (size_t g = 0; g < m->pipes.size(); g++) {
