@@ -197,8 +197,11 @@ int sffft_pipe_destroy(sffft_pipe_t pipe);
  *   sffft_multi_pipe_create / sffft_conv_host_multi: one [B][H][L] batch in host memory (pinned for overlap);
  *     every device uploads its channel slice, convolves it with its spectrum rows Kf[g] ([h1 - h0][N] on that
  *     device) and downloads its slice of y_host, all devices concurrently, each through a host pipe of its own
- *     (as sffft_pipe_create with `chunks`); the call returns when every device has finished, with the first
- *     error or device-side status (SFFFT_ERR_TIMEOUT) of any shard. */
+ *     (as sffft_pipe_create with `chunks`) driven by a host thread of its own (started by
+ *     sffft_multi_pipe_create, joined by sffft_multi_pipe_destroy); the call returns when every device has
+ *     finished, with the first error or device-side status (SFFFT_ERR_TIMEOUT) of any shard.  Composite plans
+ *     in sffft_conv_multi use the workspace attached to each plan (sffft_plan_set_workspace); the pipes
+ *     allocate their own. */
 int sffft_conv_multi(const sffft_plan_t* plans, int G, const void* const* u, const void* const* Kf, void* const* y,
                      int B, int H, void* const* streams);
 typedef struct sffft_multi* sffft_multi_t;

@@ -147,7 +147,7 @@ int sffft_plan_create(sffft_plan_t* out, int L, int io, int acc, const char* con
   if ((io != SFFFT_IO_FP32 && io != SFFFT_IO_BF16) || (acc != SFFFT_ACC_FP32 && acc != SFFFT_ACC_FP16) ||
       (kernel_mode != SFFFT_KERNEL_LEGACY && kernel_mode != SFFFT_KERNEL_CACHED) || device < 0)
     return SFFFT_ERR_INVALID_ARGUMENT;
-  // A composite plan "<P>x[<block plan>]" runs lengths L = P * Lb as block convolutions on the block plan;
+  // A composite plan "<P>x[<block plan>]" runs lengths L = P * Lb as partitioned convolutions on the block plan;
   // lengths above the largest catalog plan get one by default.
   int blocks = 1;
   std::string want;
