@@ -98,3 +98,39 @@ def test_invalid_calls_fail_cleanly(cuda_device):
     with pytest.raises(sf.SffftError):
         sf.Plan(128, config="64x32/w4")
     plan.check()
+
+
+@pytest.mark.parametrize("L", [1024, 4096])
+def test_back_to_back_calls_on_one_stream(cuda_device, L):
+    # each fused launch may start its prologue while the stream's previous kernel finishes, but reads its input only
+    # after that kernel has completed: a chain y3 = conv(conv(conv(u))), with torch kernels in between that rewrite
+    # the next input, issued without synchronisation, equals the same calls made one at a time
+    B, H = 8, 96
+    g = torch.Generator(device=cuda_device).manual_seed(L)
+    u = torch.randn((B, H, L), device=cuda_device, generator=g)
+    k = torch.randn((H, L), device=cuda_device, generator=g) / L ** 0.5
+    plan = sf.Plan(L)
+    Kf = plan.filter_spectrum(k)
+    stream = torch.cuda.current_stream(cuda_device)
+    ys = [torch.empty_like(u) for _ in range(3)]
+    x = u
+    for i in range(3):
+        plan.conv(x, Kf, ys[i], stream=stream)
+        x = ys[i] * 0.5 + 1.0          # a torch kernel producing the next input on the same stream
+    torch.cuda.synchronize()
+    plan.check()
+    x = u
+    for i in range(3):
+        torch.cuda.synchronize()
+        y = plan.conv(x.clone(), Kf)
+        torch.cuda.synchronize()
+        assert torch.equal(y, ys[i])
+        x = y * 0.5 + 1.0
+    # fused launches straight after each other, the second reading the first's output
+    a, b = torch.empty_like(u), torch.empty_like(u)
+    plan.conv(u, Kf, a, stream=stream)
+    plan.conv(a, Kf, b, stream=stream)
+    torch.cuda.synchronize()
+    plan.check()
+    assert torch.equal(b, plan.conv(a.clone(), Kf))
+    plan.close()
