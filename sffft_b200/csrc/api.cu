@@ -401,8 +401,10 @@ int sffft_conv_ws(sffft_plan_t p, const void* u, const void* Kf, void* y, int B,
                                            (float*)((char*)work + zbytes), st);
   if (ce != cudaSuccess) return cuda_fail(ce);
   rc = conv_launch(p, u, nullptr, nullptr, B, H * P, st, 0, 0, 1, &blk);
-  if (!rc) rc = conv_launch(p, nullptr, Kf, y, B, H * P, st, 0, 0, 2, &blk);
-  return rc;
+  if (rc) return rc;
+  const cudaError_t cs = launch_spectrum_sum(blk.Z, (const float*)Kf, H, (B + 1) / 2, p->e->N, P, p->sms, st);
+  if (cs != cudaSuccess) return cuda_fail(cs);
+  return conv_launch(p, nullptr, Kf, y, B, H * P, st, 0, 0, 2, &blk);
 }
 
 static int conv_launch(sffft_plan_t p, const void* u, const void* Kf, void* y, int B, int H, cudaStream_t stream,

@@ -1,5 +1,5 @@
-// Row energies of composite plans (L = P * Lb above the largest single-pass length; the multi-pass plans the
-// reference lists as missing, README.md:175).
+// Row energies and spectrum sums of composite plans (L = P * Lb above the largest single-pass length; the
+// multi-pass plans the reference lists as missing, README.md:175).
 //
 // A composite plan's partitioned convolution (stages.h, "Partitioned convolution") scales each row by the power
 // of two that its energy gives, with one scale for all of a row's blocks, so the energy is taken over the whole
@@ -48,6 +48,57 @@ cudaError_t launch_row_energy(const void* u, bool bf16, long long rows, int L, i
     row_energy_kernel<__nv_bfloat16><<<(unsigned)rows, 256, 0, stream>>>((const __nv_bfloat16*)u, E, L, norm);
   else
     row_energy_kernel<float><<<(unsigned)rows, 256, 0, stream>>>((const float*)u, E, L, norm);
+  return cudaGetLastError();
+}
+
+// The spectrum sums of a composite plan's partitioned convolution, in place: for every pair (hb, j) and frequency
+// position f, W_p[f] = sum_{q <= p} Z_q[f] K'_{p-q}[f] overwrites Z_p[f] (Z [Hb * P][PB][N], K' [P][Hb][N], complex
+// fp32).  One thread per (hb, j, f) keeps the P values Z_q[f] and K'_d[f] in registers and writes the P sums, from
+// the last block down, so each sum reads only values not yet overwritten.  Consecutive threads take consecutive f,
+// so every load and store of a warp is one contiguous 256-byte run; the filter values are shared by the PB pairs of a
+// channel, which run in neighbouring CTAs (L2 hits).
+template <int NP>
+__global__ void __launch_bounds__(256) spectrum_sum_kernel(float2* __restrict__ Z, const float2* __restrict__ K, int Hb,
+                                                           int PB, int lgN) {
+  const int N = 1 << lgN;
+  const long long total = ((long long)Hb * PB) << lgN;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    const int row = (int)(i >> lgN);                // hb * PB + j (Hb * PB < 2^31)
+    const int f = (int)(i & (N - 1));
+    const int hb = row / PB, j = row - hb * PB;
+    float2 z[NP], k[NP];
+#pragma unroll
+    for (int q = 0; q < NP; q++) {
+      z[q] = Z[(((long long)hb * NP + q) * PB + j) * N + f];
+      k[q] = __ldg(K + ((long long)q * Hb + hb) * N + f);
+    }
+#pragma unroll
+    for (int p = NP - 1; p >= 0; p--) {
+      float re = 0.f, im = 0.f;
+#pragma unroll
+      for (int q = 0; q <= p; q++) {
+        const float2 a = z[q], b = k[p - q];
+        re += a.x * b.x - a.y * b.y;
+        im += a.x * b.y + a.y * b.x;
+      }
+      Z[(((long long)hb * NP + p) * PB + j) * N + f] = make_float2(re, im);
+    }
+  }
+}
+
+cudaError_t launch_spectrum_sum(float* Z, const float* K, int Hb, int PB, int N, int P, int sms, cudaStream_t stream) {
+  float2* z = reinterpret_cast<float2*>(Z);
+  const float2* k = reinterpret_cast<const float2*>(K);
+  const unsigned grid = (unsigned)sms * 8;
+  int lgN = 0;
+  while ((1 << lgN) < N) lgN++;
+  switch (P) {
+    case 2: spectrum_sum_kernel<2><<<grid, 256, 0, stream>>>(z, k, Hb, PB, lgN); break;
+    case 4: spectrum_sum_kernel<4><<<grid, 256, 0, stream>>>(z, k, Hb, PB, lgN); break;
+    case 8: spectrum_sum_kernel<8><<<grid, 256, 0, stream>>>(z, k, Hb, PB, lgN); break;
+    case 16: spectrum_sum_kernel<16><<<grid, 256, 0, stream>>>(z, k, Hb, PB, lgN); break;
+    default: return cudaErrorInvalidValue;
+  }
   return cudaGetLastError();
 }
 

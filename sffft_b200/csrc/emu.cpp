@@ -270,7 +270,7 @@ int run_plan(const void* u, const float* Kf, void* y, int B, int H, const BlockA
         constexpr int NWQ = SH::NWQ;
         for (int wi = 0; wi < NWQ; wi++)
           for (int q = 0; q < 4; q++)
-            for (int lane = 0; lane < 32; lane++) spec_accumulate_units<P, TIO>(ops, ea, bz, gp, wi, q, lane);
+            for (int lane = 0; lane < 32; lane++) spec_load_units<P, TIO>(ops, bz, gp, wi, q, lane);
         run_stage_emu<P::S, 2, P, TIO, ACC16>(ops, ea, bz, gp, dbase, 0u);
       }
       continue;
@@ -331,6 +331,25 @@ int run_composite(int P, const void* u, const float* Kf, void* y, int B, int H) 
   while ((1 << ba.lgP) < P) ba.lgP++;
   ba.Hb = H;
   run_plan<Pl, TIO, ACC16, 1>(u, nullptr, nullptr, B, H * P, &ba);
+  // the spectrum sums, in place (the device's spectrum_sum_kernel): Z_p <- sum_{q <= p} Z_q K'_{p-q}, fp32
+  const int PB = (B + 1) / 2, N = Pl::N;
+  std::vector<float> zq(2 * (size_t)P);
+  for (int hb = 0; hb < H; hb++)
+    for (int j = 0; j < PB; j++)
+      for (int f = 0; f < N; f++) {
+        auto zi = [&](int q) { return 2 * ((((size_t)hb * P + q) * PB + j) * N + f); };
+        for (int q = 0; q < P; q++) { zq[2 * q] = Z[zi(q)]; zq[2 * q + 1] = Z[zi(q) + 1]; }
+        for (int p = P - 1; p >= 0; p--) {
+          float re = 0.f, im = 0.f;
+          for (int q = 0; q <= p; q++) {
+            const float* kk = Kf + 2 * (((size_t)(p - q) * H + hb) * N + f);
+            re += zq[2 * q] * kk[0] - zq[2 * q + 1] * kk[1];
+            im += zq[2 * q] * kk[1] + zq[2 * q + 1] * kk[0];
+          }
+          Z[zi(p)] = re;
+          Z[zi(p) + 1] = im;
+        }
+      }
   run_plan<Pl, TIO, ACC16, 2>(nullptr, Kf, y, B, H * P, &ba);
   return 0;
 }

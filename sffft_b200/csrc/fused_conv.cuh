@@ -455,12 +455,22 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
     tw_lo[i] = make_float2(cs, sn);
   }
   const TIO* u = reinterpret_cast<const TIO*>(prm.u);
-  // L2 prefetch of group gi's input sequences and spectrum rows by warp 0 (one bulk prefetch per sequence).  A
-  // prefetch only moves lines into L2, the point of coherence, so it may be issued before the previous kernel has
-  // finished writing them: the loads that use the data come after the dependency wait below.
+  // L2 prefetch of group gi's input sequences and spectrum rows by warp 0 (one bulk prefetch per sequence; the
+  // inverse launch of a composite plan: each pair's summed spectrum row).  A prefetch only moves lines into L2, the
+  // point of coherence, so it may be issued before the previous kernel has finished writing them: the loads that
+  // use the data come after the dependency wait below.
   auto prefetch_group = [&](int gi) {
     const int group = (int)blockIdx.x + gi * (int)gridDim.x;
     const GroupPairs gp = group_pairs(group, P::G, prm.B, prm.H);
+    if constexpr (MODE == 2) {
+      if (lane < P::G) {
+        const PairInfo pi = gp.get(lane, P::L);
+        const int hb = pi.h >> prm.blk.lgP, pb = pi.h - (hb << prm.blk.lgP);
+        if (pi.h >= 0)
+          prefetch_l2(prm.blk.Z + 2 * ((((long long)(hb << prm.blk.lgP) + pb) * gp.PB + pi.j) * P::N), P::N * 8);
+      }
+      return;
+    }
     if (lane < 2 * P::G) {
       const PairInfo pi = gp.get(lane >> 1, P::L);
       const long long off = (lane & 1) ? pi.off1 : pi.off0;
@@ -473,7 +483,7 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
     }
   };
   // the first PD groups' prefetches overlap the previous kernel's tail
-  const int npre = MODE == 2 ? 0 : (ni < SH::PD ? ni : SH::PD);
+  const int npre = ni < SH::PD ? ni : SH::PD;
   if (warp == 0)
     for (int gi = 0; gi < npre; gi++) prefetch_group(gi);
   // everything above touched only shared memory, TMEM and the plan's constant DFT-matrix image (and issued L2
@@ -489,9 +499,8 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
   if (warp == 0) {
     // ---------------- L2 prefetcher ----------------
     // Brings each group's 2G input sequences (one bulk prefetch per sequence, one lane each) and spectrum
-    // rows into L2, at most PD groups ahead of the conversions, so a team's direct loads hit L2.  (The inverse
-    // launch of a composite plan reads pair and filter spectra shared by many groups: no prefetch.)
-    for (int gi = npre; gi < (MODE == 2 ? 0 : ni); gi++) {
+    // rows into L2, at most PD groups ahead of the conversions, so a team's direct loads hit L2.
+    for (int gi = npre; gi < ni; gi++) {
       if (gi >= SH::PD && !wait_stamp_all(conv_done, gi - SH::PD + 1, abort_flag)) break;
       if (lane == 0) SFFFT_STAMP(0, 3 * gi);
       prefetch_group(gi);
@@ -657,8 +666,7 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
             if constexpr (MODE == 1) {
               convert_scaled<P, TIO, SH::NB, TWT>(ops, u, gp, ttid, en);
             } else {
-              const EpiArgs ea{0u, prm.Kf, prm.y, prm.B, prm.H, group, nullptr, 0, en};
-              spec_accumulate_units<P, TIO>(ops, ea, prm.blk, gp, wi, q, lane);
+              spec_load_units<P, TIO>(ops, prm.blk, gp, wi, q, lane);
             }
           }
           if (lane == 0 && wt == 0) SFFFT_STAMP(2 + team, 3 * ntask + 1);

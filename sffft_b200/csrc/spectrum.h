@@ -1,4 +1,5 @@
-// Host launchers of the digit-stage kernels (spectrum.cu) and of the composite plans' row energies (blocks.cu).
+// Host launchers of the digit-stage kernels (spectrum.cu) and of the composite plans' row energies and spectrum
+// sums (blocks.cu).
 #pragma once
 #include <cuda_runtime.h>
 
@@ -20,5 +21,7 @@ cudaError_t launch_irfft(const float2* X, int rows, float* x, float2* W, const i
 
 // Row energies of composite plans (sum of squares over each row of L values, times Lb / L); see blocks.cu.
 cudaError_t launch_row_energy(const void* u, bool bf16, long long rows, int L, int Lb, float* E, cudaStream_t stream);
+// Spectrum sums of composite plans in place: Z_p <- sum_{q <= p} Z_q K'_{p-q} for P = 2, 4, 8 or 16; see blocks.cu.
+cudaError_t launch_spectrum_sum(float* Z, const float* K, int Hb, int PB, int N, int P, int sms, cudaStream_t stream);
 
 }  // namespace sffft

@@ -736,8 +736,9 @@ SF_HD void copy_out_staged(Ops& ops, const EpiArgs& ea, const GroupPairs& gp, in
 //   forward launch:  conversion and stages 0 .. S-1 of every (pair, block); the last forward stage stores the
 //                    pair's spectrum (x its 1/sqrt(R) stage scale) to Z [Hb * P][PB][N] (complex fp32, digit
 //                    order) instead of multiplying it by a filter spectrum;
-//   inverse launch:  the operand of stage S from sum_q Z_q K'_{p-q} (the spectrum multiply of the single-pass
-//                    kernel, extended over the blocks), then stages S .. 2S-1 and the outputs of block p.
+//   spectrum sums:   a streaming kernel (blocks.cu) replaces every pair's Z_p by W_p = sum_{q <= p} Z_q K'_{p-q}
+//                    in place (the spectrum multiply of the single-pass kernel, extended over the blocks);
+//   inverse launch:  the operand of stage S from W_p, then stages S .. 2S-1 and the outputs of block p.
 // Both launches scale each row by the power of two that its energy over the whole row gives (pair_scales), so
 // that every block of a row carries the same scale and the sum over blocks stays consistent; the energies come
 // from a separate pass over u, normalised to Lb values.
@@ -794,11 +795,10 @@ SF_HD void spec_store_units(Ops& ops, const EpiArgs& ea, const BlockArgs& ba, co
 }
 
 // Inverse launch, in place of the conversion: the A operand of stage S (the layout the spectrum stage's
-// epilogue writes) from sum_{q <= p} Z_q K'_{p - q} of each unit's 16 values, accumulated in fp32 in two runs
-// of eight.
+// epilogue writes) from each unit's 16 values of the summed spectrum W_p (held in Z's slot of block p), in two
+// runs of eight.
 template <class P, class TIO, class Ops>
-SF_HD void spec_accumulate_units(Ops& ops, const EpiArgs& ea, const BlockArgs& ba, const GroupPairs& gp, int wi, int q,
-                                 int lane) {
+SF_HD void spec_load_units(Ops& ops, const BlockArgs& ba, const GroupPairs& gp, int wi, int q, int lane) {
   constexpr int SID = P::S - 1, C = epi_chunks<P, SID>(), R = P::rad(SID), U = P::tiles(SID) * C, N = P::N;
   constexpr int NWQ = Shape<P, (int)sizeof(TIO)>::NWQ, RWS = P::rows(SID + 1);
 #pragma unroll 1
@@ -813,21 +813,11 @@ SF_HD void spec_accumulate_units(Ops& ops, const EpiArgs& ea, const BlockArgs& b
       for (int e = 0; e < 8; e++) ar[e] = ai[e] = 0.f;
       const long long pos = (long long)x.rr * R + x.c0 + 8 * half;
       if (pi.h >= 0) {
-#pragma unroll 1
-        for (int qq = 0; qq <= pb; qq++) {
-          const float* zp = ba.Z + 2 * ((((long long)(hb << ba.lgP) + qq) * gp.PB + pi.j) * N + pos);
-          const float* kp = ea.Kf + 2 * (((long long)(pb - qq) * ba.Hb + hb) * N + pos);
-          float z[16], k[16];
-          for (int e = 0; e < 4; e++) {
-            float z4[4], k4[4];
-            ops.ldZ(zp + 4 * e, z4);
-            ops.ldK(kp + 4 * e, k4);
-            for (int i = 0; i < 4; i++) { z[4 * e + i] = z4[i]; k[4 * e + i] = k4[i]; }
-          }
-          for (int e = 0; e < 8; e++) {
-            ar[e] += z[2 * e] * k[2 * e] - z[2 * e + 1] * k[2 * e + 1];
-            ai[e] += z[2 * e] * k[2 * e + 1] + z[2 * e + 1] * k[2 * e];
-          }
+        const float* zp = ba.Z + 2 * ((((long long)(hb << ba.lgP) + pb) * gp.PB + pi.j) * N + pos);
+        for (int e = 0; e < 4; e++) {
+          float z4[4];
+          ops.ldZ(zp + 4 * e, z4);
+          ar[2 * e] = z4[0]; ai[2 * e] = z4[1]; ar[2 * e + 1] = z4[2]; ai[2 * e + 1] = z4[3];
         }
       }
       uint32_t pr[4], pim[4];
