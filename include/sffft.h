@@ -107,9 +107,9 @@ int sffft_conv(sffft_plan_t plan, const void* u, const void* Kf, void* y, int B,
  * input block (ceil(B/2) * H * L * 16 bytes) and the row energies; 0 for single-pass plans. */
 int sffft_conv_workspace_bytes(sffft_plan_t plan, int B, int H, size_t* bytes);
 /* sffft_conv with a caller-owned device workspace (256-byte aligned, at least sffft_conv_workspace_bytes;
- * NULL for single-pass plans).  A composite call is three launches in stream order (row energies, forward
- * transforms, spectrum sums with inverse transforms); the workspace must not be shared by calls that can
- * overlap.  Returns SFFFT_ERR_WORKSPACE when a composite plan gets no workspace or too small a one. */
+ * NULL for single-pass plans).  A composite call is four launches in stream order (row energies, forward
+ * transforms, spectrum sums, inverse transforms); the workspace must not be shared by calls that can overlap.
+ * Returns SFFFT_ERR_WORKSPACE when a composite plan gets no workspace or too small a one. */
 int sffft_conv_ws(sffft_plan_t plan, const void* u, const void* Kf, void* y, int B, int H, void* work,
                   size_t work_bytes, void* stream);
 /* Attaches a caller-owned workspace (256-byte aligned; NULL detaches) that sffft_conv uses for composite

@@ -53,35 +53,35 @@ cudaError_t launch_row_energy(const void* u, bool bf16, long long rows, int L, i
 
 // The spectrum sums of a composite plan's partitioned convolution, in place: for every pair (hb, j) and frequency
 // position f, W_p[f] = sum_{q <= p} Z_q[f] K'_{p-q}[f] overwrites Z_p[f] (Z [Hb * P][PB][N], K' [P][Hb][N], complex
-// fp32).  One thread per (hb, j, f) keeps the P values Z_q[f] and K'_d[f] in registers and writes the P sums, from
-// the last block down, so each sum reads only values not yet overwritten.  Consecutive threads take consecutive f,
-// so every load and store of a warp is one contiguous 256-byte run; the filter values are shared by the PB pairs of a
-// channel, which run in neighbouring CTAs (L2 hits).
+// fp32).  One thread per (hb, f) keeps the channel's P filter values K'_d[f] in registers and, for each of the PB
+// pairs of the channel, the pair's P values Z_q[f], writing the P sums from the last block down, so each sum reads
+// only values not yet overwritten.  Consecutive threads take consecutive f, so every load and store of a warp is one
+// contiguous 256-byte run, and each filter value is read from memory once.
 template <int NP>
 __global__ void __launch_bounds__(256) spectrum_sum_kernel(float2* __restrict__ Z, const float2* __restrict__ K, int Hb,
                                                            int PB, int lgN) {
   const int N = 1 << lgN;
-  const long long total = ((long long)Hb * PB) << lgN;
+  const long long total = (long long)Hb << lgN;
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
-    const int row = (int)(i >> lgN);                // hb * PB + j (Hb * PB < 2^31)
-    const int f = (int)(i & (N - 1));
-    const int hb = row / PB, j = row - hb * PB;
-    float2 z[NP], k[NP];
+    const int hb = (int)(i >> lgN), f = (int)(i & (N - 1));
+    float2 k[NP];
 #pragma unroll
-    for (int q = 0; q < NP; q++) {
-      z[q] = Z[(((long long)hb * NP + q) * PB + j) * N + f];
-      k[q] = __ldg(K + ((long long)q * Hb + hb) * N + f);
-    }
+    for (int d = 0; d < NP; d++) k[d] = __ldg(K + ((long long)d * Hb + hb) * N + f);
+    for (int j = 0; j < PB; j++) {
+      float2 z[NP];
 #pragma unroll
-    for (int p = NP - 1; p >= 0; p--) {
-      float re = 0.f, im = 0.f;
+      for (int q = 0; q < NP; q++) z[q] = Z[(((long long)hb * NP + q) * PB + j) * N + f];
 #pragma unroll
-      for (int q = 0; q <= p; q++) {
-        const float2 a = z[q], b = k[p - q];
-        re += a.x * b.x - a.y * b.y;
-        im += a.x * b.y + a.y * b.x;
+      for (int p = NP - 1; p >= 0; p--) {
+        float re = 0.f, im = 0.f;
+#pragma unroll
+        for (int q = 0; q <= p; q++) {
+          const float2 a = z[q], b = k[p - q];
+          re += a.x * b.x - a.y * b.y;
+          im += a.x * b.y + a.y * b.x;
+        }
+        Z[(((long long)hb * NP + p) * PB + j) * N + f] = make_float2(re, im);
       }
-      Z[(((long long)hb * NP + p) * PB + j) * N + f] = make_float2(re, im);
     }
   }
 }
