@@ -98,9 +98,11 @@ int sffft_fft_workspace_bytes(sffft_plan_t plan, int B, size_t* bytes);
 int sffft_rfft(sffft_plan_t plan, const void* x, int x_dtype, int B, void* X, void* work, void* stream);
 int sffft_irfft(sffft_plan_t plan, const void* X, int B, float* x, void* work, void* stream);
 
-/* The fused convolution: one kernel launch per call.  Replaces the launch
- * fftconv<P,W,TIO,TAcc,CACHED><<<B*H, 32*W, smem>>>(u, Kf, tw, dft, y, B, H) (src/sffft.cu:243-280,
- * 389-390); the unused twiddle table and the DFT table are owned by the plan. */
+/* The fused convolution: one kernel launch per call (four for a composite plan, which needs a workspace: see
+ * sffft_conv_ws).  Replaces the launch fftconv<P,W,TIO,TAcc,CACHED><<<B*H, 32*W, smem>>>(u, Kf, tw, dft, y, B, H)
+ * (src/sffft.cu:243-280, 389-390); the unused twiddle table and the DFT table are owned by the plan.  The kernel
+ * is a programmatic dependent of the stream's previous kernel: its prologue may overlap that kernel's end, and it
+ * reads u and Kf only after that kernel has completed. */
 int sffft_conv(sffft_plan_t plan, const void* u, const void* Kf, void* y, int B, int H, void* stream);
 
 /* Workspace of a composite plan's convolution of a B x H batch, in bytes: the forward spectra of every
