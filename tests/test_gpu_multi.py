@@ -81,3 +81,35 @@ def test_invalid_multi_calls(cuda_device):
     assert lib.sffft_multi_pipe_create(ctypes.byref(h), hs, 2, 8, 1, 0) == sf.ERR_INVALID_ARGUMENT    # H < G
     with pytest.raises(sf.SffftError):
         sf.conv_multi(plans, [None, None], [None, None], [None, None], 8, 16)
+
+
+def test_composite_plans_over_devices(oracle, cuda_device):
+    # composite plans take their workspace from the caller: attached to each plan for sffft_conv_multi, allocated by
+    # each device's pipe for sffft_conv_host_multi; both equal one composite plan over the whole batch
+    L, B, H, G, config = 512, 4, 10, 2, "4x[16x16/w8]"
+    u, k = oracle.gen_profile(B, H, L, seed=6)
+    plans = [sf.Plan(L, config=config, device=d) for d in devices(G)]
+    us, Kfs, ys, works = [], [], [], []
+    for g, p in enumerate(plans):
+        h0, h1 = sf.shard_range(H, G, g)
+        dev = torch.device("cuda", p.device)
+        us.append(torch.from_numpy(np.ascontiguousarray(u[:, h0:h1])).to(dev))
+        Kfs.append(p.filter_spectrum(torch.from_numpy(np.ascontiguousarray(k[h0:h1])).to(dev)))
+        ys.append(torch.empty_like(us[-1]))
+        works.append(torch.empty(p.workspace_bytes(B, h1 - h0), dtype=torch.uint8, device=dev))
+        assert sf.lib().sffft_plan_set_workspace(p._h, works[-1].data_ptr(), works[-1].numel()) == sf.OK
+    sf.conv_multi(plans, us, Kfs, ys, B, H)
+    for p in plans:
+        p.check()
+    y = np.concatenate([t.cpu().numpy() for t in ys], axis=1)
+    whole = sf.Plan(L, config=config)
+    ref = whole.conv(torch.from_numpy(u).to(cuda_device), whole.filter_spectrum(torch.from_numpy(k).to(cuda_device)))
+    whole.check()
+    assert np.array_equal(y, ref.cpu().numpy())
+    assert rel_l2(y, oracle.direct_conv(u, k)) <= 5e-4
+    u_h = torch.from_numpy(u).pin_memory()
+    y_h = torch.zeros_like(u_h).pin_memory()
+    mp = sf.HostPipeMulti(plans, B, H)
+    mp.conv(u_h, Kfs, y_h)
+    mp.close()
+    assert np.array_equal(y_h.numpy(), y)
