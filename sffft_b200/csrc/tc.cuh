@@ -87,7 +87,7 @@ __device__ __forceinline__ uint64_t global_ns() {
 
 // Copies `bytes` (a multiple of 16, both addresses 16-byte aligned) from global memory into this CTA's shared
 // memory with bulk copies of at most 32 KB, completing on `bar` (initialised with one arrival, which this call
-// makes together with the expected byte count).  Plain bulk copies of this GPU's own memory, no multicast.
+// makes together with the expected byte count).  Plain bulk copies of this GPU's own memory into this CTA alone.
 __device__ __forceinline__ void bulk_load_smem(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
   for (uint32_t off = 0; off < bytes; off += 32768u) {
