@@ -55,19 +55,22 @@ __device__ __forceinline__ u64 mul2(u64 a, u64 b) {
   return d;
 }
 
+// Shared memory is addressed through 32-bit shared-window addresses (st.shared / ld.shared): generic pointers
+// would cost 64-bit address arithmetic and registers in every epilogue unit, and generic loads wait as
+// L1TEX accesses.
 struct DevOps {
-  uint8_t* sm;   // base of the data buffer the epilogue / conversion writes (generic pointer)
+  uint32_t sm;      // shared-window address of the data buffer the epilogue / conversion writes
   bool acc16;
-  const float2* tw_lo;   // w_N^e, e in [0, 64)
-  const float2* tw_hi;   // w_N^(64 h), h in [0, N/64)
-  int n_tw;              // transform size N
+  uint32_t tw_lo;   // shared-window address of w_N^e, e in [0, 64) (float2 each)
+  uint32_t tw_hi;   // of w_N^(64 h), h in [0, N/64)
+  int n_tw;         // transform size N
   __device__ __forceinline__ void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
     mma_f16_ss(d, a, b, idesc, acc);
   }
   __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) { sffft::tmem_ld16(taddr, r); }
   __device__ __forceinline__ void tmem_wait() { tmem_wait_ld(); }
   __device__ __forceinline__ void st16(uint32_t off, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
-    *reinterpret_cast<uint4*>(sm + off) = make_uint4(a, b, c, d);
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(sm + off), "r"(a), "r"(b), "r"(c), "r"(d));
   }
   __device__ __forceinline__ void sincospi(float x, float* s, float* c) { sincospif(x, s, c); }
   __device__ __forceinline__ uint32_t pack2(float lo, float hi) const {
@@ -78,8 +81,9 @@ struct DevOps {
   __device__ __forceinline__ float hi16f(uint32_t w) { return __half2float(__ushort_as_half((unsigned short)(w >> 16))); }
   __device__ __forceinline__ float acc_val(uint32_t w) { return acc16 ? lo16f(w) : __uint_as_float(w); }
   __device__ __forceinline__ void ldsK(const void* p, float (&k)[4]) {
-    const float4 v = *reinterpret_cast<const float4*>(p);
-    k[0] = v.x; k[1] = v.y; k[2] = v.z; k[3] = v.w;
+    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(k[0]), "=f"(k[1]), "=f"(k[2]), "=f"(k[3])
+                 : "r"((uint32_t)__cvta_generic_to_shared(p)));
   }
   __device__ __forceinline__ void ldK(const float* p, float (&k)[4]) {
     const float4 v = __ldg(reinterpret_cast<const float4*>(p));
@@ -132,18 +136,22 @@ struct DevOps {
       if (m < seg) ss += __shfl_xor_sync(0xffffffffu, ss, m);
     if ((threadIdx.x & (seg - 1)) == 0) part[idx] = ss;
   }
-  __device__ __forceinline__ void st4(uint32_t off, float v) { *reinterpret_cast<float*>(sm + off) = v; }
+  __device__ __forceinline__ void st4(uint32_t off, float v) {
+    asm volatile("st.shared.f32 [%0], %1;" ::"r"(sm + off), "f"(v));
+  }
   __device__ __forceinline__ void ld4_staged(uint32_t off, uint32_t rot, float* v) {
-    const float4 q = *reinterpret_cast<const float4*>(sm + off);
-    const float w[4] = {q.x, q.y, q.z, q.w};
+    float w[4];
+    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(w[0]), "=f"(w[1]), "=f"(w[2]), "=f"(w[3]) : "r"(sm + off));
     for (int i = 0; i < 4; i++) v[i] = w[i ^ (int)rot];
   }
   // w_N^e for any integer e (reduced mod N), from the two-level table: w^(64 h) * w^l
   __device__ __forceinline__ void tw(int e, float* re, float* im) const {
     e &= (n_tw - 1);
-    const float2 h = tw_hi[e >> 6], l = tw_lo[e & 63];
-    *re = h.x * l.x - h.y * l.y;
-    *im = h.x * l.y + h.y * l.x;
+    float hx, hy, lx, ly;
+    asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(hx), "=f"(hy) : "r"(tw_hi + (uint32_t)((e >> 6) * 8)));
+    asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(lx), "=f"(ly) : "r"(tw_lo + (uint32_t)((e & 63) * 8)));
+    *re = hx * lx - hy * ly;
+    *im = hx * ly + hy * lx;
   }
   // 16 complex values (a + ib) times t0 * w^j (j < 8) and t8 * w^(j-8) (j >= 8), rounded to fp16 pairs:
   // two independent recurrences of four steps, each carrying two elements per f32x2 op.
@@ -511,7 +519,7 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
     // Slot s holds this CTA's groups s, s + NS, ...; each group needs its 2S stages in order.  The issuer
     // scans the slots and issues the next stage of any slot whose operand is ready.
     if (lane == 0 && (!prm.btab || wait_phase(bmat_full, 0u, abort_flag))) {
-      DevOps ops{sm, ACC16, nullptr, nullptr, P::N};
+      DevOps ops{smem_u32(sm), ACC16, 0u, 0u, P::N};
       int done[NS], total[NS], ncommit[NS];
       uint32_t ar_bits = 0;
       int left = 0;
@@ -650,7 +658,7 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
         const int group = (int)blockIdx.x + gi * (int)gridDim.x;
         if (j == 0) gps[l] = group_pairs(group, P::G, prm.B, prm.H);
         const GroupPairs gp = gps[l];
-        DevOps ops{sm + SH::DATA_OFF + s * P::DATA_BYTES, ACC16, tw_lo, tw_hi, P::N};
+        DevOps ops{smem_u32(sm + SH::DATA_OFF + s * P::DATA_BYTES), ACC16, smem_u32(tw_lo), smem_u32(tw_hi), P::N};
         if (lane == 0 && wt == 0) SFFFT_STAMP(2 + team, 3 * ntask);
         if (j == 0) {
           // convert the group's input, measuring each row's energy for the MMA warp, which derives the rows'
