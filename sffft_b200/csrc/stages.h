@@ -335,6 +335,9 @@ struct EpiArgs {
   const uint8_t* kst;   // spectrum rows of channels khf, khf+1, ... staged by the loader warp, or null
   int khf;
   const float* en;      // the group's energy slots (its rows' output scales follow from them, pair_scales)
+  // output stage: pair sg's output scales (pair_out_scales), kept across a thread's units of that pair
+  mutable int sg = -1;
+  mutable float so0 = 0.f, so1 = 0.f;
 };
 
 // 1/sqrt(R): the per-stage scale of a radix-R digit (the reference's 1/sqrt(R) per stage, total 1/N).
@@ -462,10 +465,11 @@ SF_HD void epi_finish(Ops& ops, const EpiArgs& ea, const GroupPairs& gp, const E
 
   if constexpr (OUT) {
     // each row's scale undoes its input scaling (pair_scales): a power of two, or 0 for an all-zero row
-    float s0, s1;
-    pair_out_scales<P, Shape<P, (int)sizeof(TIO)>::TWARPS * 32>(ea.en, g, &s0, &s1);
-    s0 *= SC;
-    s1 *= SC;
+    if (g != ea.sg) {
+      pair_out_scales<P, Shape<P, (int)sizeof(TIO)>::TWARPS * 32>(ea.en, g, &ea.so0, &ea.so1);
+      ea.sg = g;
+    }
+    const float s0 = ea.so0 * SC, s1 = ea.so1 * SC;
     if constexpr (S == 2) {
       const PairInfo pi = gp.get(g, P::L);
       TIO* y = (TIO*)ea.y;
