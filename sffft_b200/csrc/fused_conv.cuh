@@ -533,6 +533,7 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
       int nmma = 0;
       (void)nmma;
       uint64_t t_idle = global_ns();
+      uint32_t idle = 0;
       while (left > 0) {
         bool progressed = false;
 #pragma unroll
@@ -562,7 +563,10 @@ __global__ void __launch_bounds__(Shape<P, sizeof(TIO)>::NT, 1) fused_conv_kerne
         }
         if (progressed) {
           t_idle = global_ns();
-        } else {
+          idle = 0;
+        } else if ((++idle & 15u) == 0) {
+          // the abort flag and the time limit are checked every 16th idle scan, so a scan is only the slots'
+          // barrier tests
           if (*abort_flag) break;
           if (global_ns() - t_idle > s_wait_ns) { *abort_flag = 1; break; }
           // nothing ready: poll again at once (sleeping 32 or 128 ns between polls measured 0.5-1 % slower; the
