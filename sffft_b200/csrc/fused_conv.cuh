@@ -55,9 +55,10 @@ __device__ __forceinline__ u64 mul2(u64 a, u64 b) {
   return d;
 }
 
-// Shared memory is addressed through 32-bit shared-window addresses (st.shared / ld.shared): generic pointers
-// would cost 64-bit address arithmetic and registers in every epilogue unit, and generic loads wait as
-// L1TEX accesses.
+// Shared memory is addressed through 32-bit shared-window addresses (st.shared / ld.shared): the dynamic
+// shared-memory base is aligned through an integer cast, so pointers derived from it are generic, and generic
+// accesses cost 64-bit address arithmetic and registers in every epilogue unit (measured: 6 % fewer warp
+// instructions and 1-7 % faster launches with shared-window addresses).
 struct DevOps {
   uint32_t sm;      // shared-window address of the data buffer the epilogue / conversion writes
   bool acc16;
