@@ -104,6 +104,26 @@ def test_pairs_of_very_different_scale(oracle, name, io, acc):
     assert not y[4].any()
 
 
+@pytest.mark.parametrize("name,io", [("64x32/w8", "fp32"), ("32x16x16/w8", "bf16")])
+def test_pairs_of_very_different_scale_eight_warp_plans(oracle, name, io):
+    # the 8-warp plans' output stage: a thread's units cover several chunks and tiles, so the pair whose output
+    # scales it applies changes from unit to unit (the bench plan, and configs[2]'s plan in its bf16-I/O form)
+    from tests.oracle_py import PAIR_SCALES, per_row_rel_l2, scaled_pair_inputs
+    R = radices(name)
+    L = int(np.prod(R)) // 2
+    u, k = scaled_pair_inputs(oracle, 2, L, io, seed=23)
+    Kc = spectrum_digit_order(k, R)
+    Kf = np.stack([Kc.real, Kc.imag], -1).astype(np.float32)
+    if io == "bf16":
+        y = bf16_from_bits(sf.emu_conv(name, bf16_bits(u), Kf, io="bf16", acc="fp32")).reshape(u.shape)
+    else:
+        y = sf.emu_conv(name, u, Kf, io="fp32", acc="fp32")
+    errs = per_row_rel_l2(y, oracle.direct_conv(u, k))
+    assert errs.shape == (len(PAIR_SCALES), 2)
+    assert np.all(errs <= TOL[(io, "fp32")]), errs
+    assert not y[4].any()
+
+
 SMALL_VARIANTS = [f"{n}@{v}" for n in ["16x16/w8", "32x16/w8", "32x32/w8", "64x32/w8", "64x64/w8", "32x16x16/w8"]
                   for v in (1, 2) if not (n == "16x16/w8" and v == 1)]
 
